@@ -1,0 +1,420 @@
+#!/usr/bin/env python
+"""Benchmark of the NVFP4 data path (prints ONE JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline (metric "NVFP4 GEMM TFLOPS"): the cfg3 block-scaled GEMM M=N=K=8192 on each GPU,
+operands quantized on the device from seeded synthetic bf16 (A ~ N(0,1) with 0.1 % x50
+outliers, B ~ N(0, 0.02)).  One step = one GEMM launch; L2 is flushed (256 MB write) between
+timed steps; steps are timed with CUDA events on the launching stream and the max over ranks
+is taken.  With N > 1 every rank runs its own GEMM (replicas, weak scaling) and the line also
+carries the cfg4 NVFP4 all-reduce (bf16-equivalent bus bandwidth) when the all-reduce module
+is built.  Extra keys: the cfg2 quantizer (GB/s), the roofline of the GEMM kernel, the CPU
+baseline, the end-to-end number through the C ABI with host buffers, and SM clocks sampled
+during the timed region.
+
+--impl reference times the reference's own CPU implementation of the GEMM
+(cpu_gemm_ref_bs from random_cpu_ref/verify_random.h, compiled into oracle/_ref) on a bounded
+sample with all host threads, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M_ = N_ = K_ = 8192
+FLUSH_BYTES = 256 << 20          # > 126 MB L2
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FP4_NOMINAL_TFLOPS = 9000.0       # B200 dense FP4 (NVIDIA spec, without sparsity)
+HBM_FALLBACK_GBS = 6650.0
+BF16_FALLBACK_TFLOPS = 1590.0
+
+
+def load_peaks():
+    try:
+        with open(PEAKS_PATH) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return {"hbm_gbs": HBM_FALLBACK_GBS, "bf16_tflops": BF16_FALLBACK_TFLOPS}, "fallback"
+
+
+# --------------------------------------------------------------- clocks ----
+REASON_BITS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clocks_setting"}
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 3:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+                bits = int(parts[2], 16) if parts[2].startswith("0x") else int(parts[2])
+            except ValueError:
+                continue
+            for b, name in REASON_BITS.items():
+                if bits & b and name != "gpu_idle":
+                    reasons.add(name)
+        sm.sort()
+        med = sm[len(sm) // 2] if sm else None
+        return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------ distributed ----
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------- GEMM ----
+def gemm_setup(nv, rank):
+    import torch
+    from tensorcore_ptx_example_b200 import workloads
+    a = workloads.activations(M_, K_, seed=3 + 17 * rank)
+    b = workloads.gaussian(N_, K_, seed=4 + 17 * rank, std=0.02)
+    pa, sa, gsa = nv.quantize(a, None)
+    pb, sb, gsb = nv.quantize(b, None)
+    torch.cuda.synchronize()
+    del a, b
+    alpha = float(gsa.item()) * float(gsb.item())
+    d = torch.empty((M_, N_), dtype=torch.bfloat16, device="cuda")
+    return pa, sa, pb, sb, alpha, d
+
+
+def timed_steps(fn, steps, flush):
+    """Per-step CUDA-event timing on the current stream with an L2 flush between steps."""
+    import torch
+    s = torch.cuda.current_stream()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        if flush is not None:
+            flush.zero_()
+        evs[i][0].record(s)
+        fn()
+        evs[i][1].record(s)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+def quantize_bench(nv, steps, warmup, flush):
+    """cfg2: 8192 x 7168 bf16 -> NVFP4 with a given global scale (2.5625 B/elt)."""
+    import torch
+    from tensorcore_ptx_example_b200 import workloads
+    rows, cols = workloads.CFG2_SHAPE
+    x = workloads.activations(rows, cols, seed=2)
+    gs = float(nv.amax(x).item()) / 2688.0
+    packed = torch.empty((rows, cols // 2), dtype=torch.uint8, device="cuda")
+    sf = torch.empty(nv.sf_bytes(rows, cols), dtype=torch.uint8, device="cuda")
+    fn = lambda: nv.quantize(x, gs, packed=packed, sf=sf)  # noqa: E731
+    for _ in range(warmup):
+        fn()
+    ts = timed_steps(fn, steps, flush)
+    amax_out = torch.empty(1, dtype=torch.float32, device="cuda")
+    ts_amax = timed_steps(lambda: nv.amax(x, out=amax_out), steps, flush)
+    ws = torch.empty(256, dtype=torch.uint8, device="cuda")
+    gsd = torch.empty(1, dtype=torch.float32, device="cuda")
+    ts_auto = timed_steps(lambda: nv.lib().nvfp4_quantize_bf16_auto(
+        nv._ptr(x), rows, cols, nv._ptr(packed), nv._ptr(sf), nv._ptr(gsd), nv._ptr(ws), nv._stream()), steps, flush)
+    n = rows * cols
+    ms = sum(ts) / len(ts)
+    byts = n * 2.5625
+    return {
+        "workload": "cfg2 quantize 8192x7168 bf16 -> NVFP4 (tcgen05 SF layout), given global scale",
+        "us": round(ms * 1e3, 2),
+        "gbs": round(byts / (ms * 1e-3) / 1e9, 1),
+        "bytes_per_launch": int(byts),
+        "amax_us": round(sum(ts_amax) / len(ts_amax) * 1e3, 2),
+        "auto_scale_total_us": round(sum(ts_auto) / len(ts_auto) * 1e3, 2),
+    }
+
+
+def cpu_baseline_gemm(target_s=8.0):
+    """Reference CPU GEMM (cpu_gemm_ref_bs, random_cpu_ref/verify_random.h:154) on all host
+    threads over a bounded M x N slice of the K=8192 problem; returns TFLOPS."""
+    import ctypes
+
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import py_oracle
+    threads = os.cpu_count() or 1
+    K = K_
+    nseg = K // 16
+    rng = np.random.default_rng(0)
+    vals = np.array([0, .5, 1, 1.5, 2, 3, 4, 6, -.5, -1, -1.5, -2, -3, -4, -6], np.float32)
+
+    def run(M, N):
+        A = rng.choice(vals, size=(M, K)).astype(np.float32)
+        B = rng.choice(vals, size=(N, K)).astype(np.float32)
+        sfa = np.ones(nseg, np.float32)
+        sfb = np.ones(nseg, np.float32)
+        D = np.zeros((M, N), np.float32)
+        p = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+        t0 = time.perf_counter()
+        if py_oracle.ref_verify_available():
+            py_oracle.ref_lib().ref_cpu_gemm_ref_bs_threads(p(A), p(B), p(D), M, N, K, p(sfa), p(sfb), nseg, threads)
+            kind = "reference"
+        else:
+            # oracle port of the same arithmetic (packed operands)
+            pa = np.zeros((M, K // 2), np.uint8)
+            pb = np.zeros((N, K // 2), np.uint8)
+            sa = np.full(py_oracle.sf_bytes(M, K), 0x38, np.uint8)
+            sb = np.full(py_oracle.sf_bytes(N, K), 0x38, np.uint8)
+            py_oracle.gemm_f32(pa, sa, pb, sb, M, N, K, nthreads=threads)
+            kind = "port"
+        return time.perf_counter() - t0, kind
+
+    dt, kind = run(threads, 64)                        # calibration
+    rate = 2.0 * threads * 64 * K / max(dt, 1e-6)
+    M = max(threads, int(target_s * rate / (2.0 * 256 * K)) // threads * threads)
+    M = min(M, 8192)
+    dt, kind = run(M, 256)
+    flops = 2.0 * M * 256 * K
+    return {"value": flops / dt / 1e12, "unit": "TFLOPS", "cores": threads, "kind": kind,
+            "sample": f"{M}x256x{K} slice of the cfg3 GEMM (cpu_gemm_ref_bs, {nseg} K segments)",
+            "seconds": round(dt, 3)}
+
+
+def run_ours(args):
+    import torch
+    import tensorcore_ptx_example_b200 as nv
+    world, rank, local = dist_setup(args)
+    peaks, peak_kind = load_peaks()
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+
+    pa, sa, pb, sb, alpha, d = gemm_setup(nv, rank)
+    fn = lambda: nv.gemm(pa, sa, pb, sb, M_, N_, K_, alpha=alpha, out=d)  # noqa: E731
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    assert nv.device_status() == 0
+    barrier(world)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    ts = timed_steps(fn, args.steps, flush)
+    clocks = sampler.stop()
+    barrier(world)
+    total_ms = max_over_ranks(sum(ts), world)
+    flops = 2.0 * M_ * N_ * K_
+    value = flops * args.steps * world / (total_ms * 1e-3) / 1e12
+    mean_ms = sum(ts) / len(ts)
+    achieved = flops / (mean_ms * 1e-3) / 1e12
+    fp4_peak = 4.0 * float(peaks.get("bf16_tflops", BF16_FALLBACK_TFLOPS))
+    assert nv.device_status() == 0
+
+    # end to end through the public API with host buffers: H2D operands, GEMM, D2H result
+    host = [t.cpu().pin_memory() for t in (pa, sa, pb, sb)]
+    hd = torch.empty((M_, N_), dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    d2h = hd.numel() * 2
+
+    def e2e():
+        for h, dv in zip(host, (pa, sa, pb, sb)):
+            dv.copy_(h, non_blocking=True)
+        fn()
+        hd.copy_(d, non_blocking=True)
+
+    for _ in range(2):
+        e2e()
+    ts_e2e = timed_steps(e2e, max(3, min(args.steps, 10)), None)
+    e2e_ms = max_over_ranks(sum(ts_e2e) / len(ts_e2e), world)
+
+    extra = {}
+    if rank == 0:
+        try:
+            extra["quantize"] = quantize_bench(nv, max(5, args.steps), 3, flush)
+        except Exception as e:  # reported, not fatal
+            extra["quantize"] = {"error": str(e)}
+    if world > 1:
+        try:
+            from tensorcore_ptx_example_b200 import allreduce  # noqa: F401
+            extra["allreduce"] = allreduce_bench(nv, world, rank, args)
+        except ImportError:
+            pass
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_gemm()
+
+    traffic = read_profile_traffic("gemm_cfg3")
+    line = {
+        "metric": "NVFP4 GEMM TFLOPS (1 GPU); NVFP4 all-reduce bf16-equiv GB/s at 2/4/8 B200",
+        "value": round(value, 1),
+        "unit": "TFLOPS",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e2m1 x e2m1 (ue4m3 per-16 scales) -> fp32 accumulate -> bf16",
+        "data": "synthetic (seeded N(0,1)+0.1% x50 outliers / N(0,0.02), quantized on device)",
+        "config": {"workload": "cfg3 NVFP4 GEMM M=N=K=8192, bf16 out", "M": M_, "N": N_, "K": K_,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "flushed between timed steps (256 MB write)",
+                   "tile": "1-CTA 128x256, BK=256, 4 stages, persistent"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(fp4_peak, 1),
+                     "unit": "TFLOP/s", "frac": round(achieved / fp4_peak, 4),
+                     "peak_source": f"4 x {peak_kind} cuBLAS bf16 burst ({peaks.get('bf16_tflops')}) = dense FP4 rate",
+                     "frac_of_nominal_fp4_9000": round(achieved / FP4_NOMINAL_TFLOPS, 4),
+                     "traffic": traffic,
+                     "algorithmic_flops_per_launch": flops},
+        "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12 * world, 2), "unit": "TFLOPS",
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                "path": "pinned host A/B/SF -> device, nvfp4_gemm_bf16, device D -> pinned host"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        **extra,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def allreduce_bench(nv, world, rank, args):   # replaced when the all-reduce module lands
+    return None
+
+
+def read_profile_traffic(name):
+    """DRAM bytes per launch from a committed ncu summary (profiles/<name>*.md line
+    'traffic_bytes_per_launch: N'), or None."""
+    d = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(d):
+        return None
+    for f in sorted(os.listdir(d)):
+        if f.startswith(name) and f.endswith((".md", ".txt")):
+            for ln in open(os.path.join(d, f)):
+                if ln.strip().startswith("traffic_bytes_per_launch:"):
+                    try:
+                        return int(float(ln.split(":", 1)[1].strip().split()[0]))
+                    except ValueError:
+                        return None
+    return None
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    vals = []
+    res = None
+    for i in range(args.warmup + args.steps):
+        res = cpu_baseline_gemm(target_s=2.0)
+        if i >= args.warmup:
+            vals.append(res["value"])
+    v = sum(vals) / len(vals)
+    line = {
+        "impl": "reference",
+        "metric": "NVFP4 GEMM TFLOPS (1 GPU); NVFP4 all-reduce bf16-equiv GB/s at 2/4/8 B200",
+        "value": v, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32 (reference CPU path on decoded E2M1 values)",
+        "data": "synthetic (seeded E2M1 values)",
+        "config": {"workload": "cfg3 NVFP4 GEMM M=N=K=8192 (bounded CPU sample per step)",
+                   "M": M_, "N": N_, "K": K_},
+        "cpu_baseline": {"value": v, "unit": "TFLOPS", "cores": res["cores"], "kind": res["kind"],
+                         "sample": res["sample"]},
+        "e2e": {"value": v, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,360 @@
+/*
+ * verify_random.h -- drop-in randomized CPU-reference test driver for the NVFP4 path.
+ *
+ * Signature-compatible with the reference's random_cpu_ref/verify_random.h (the API its
+ * per-file tests are written against: EncVal value sets, xorshift, pack_set, fill_random,
+ * set_elem, cpu_gemm_ref, cpu_gemm_ref_bs, check_exact, vr_to_core_matrix, VrSpec,
+ * VrRunFn, vr_verify), so a test written for the reference compiles against this header
+ * and runs its "device" through this project's C ABI (include/nvfp4.h) instead.
+ * Behaviour that tests depend on is identical and pinned by tests/test_oracle_pins.py:
+ * the xorshift stream, the draw order of fill_random (row-major, one draw per element),
+ * nibble packing (even element in the low nibble), the fp32 summation order of the CPU
+ * references, and the core-matrix shuffle.
+ *
+ * Additions (not in the reference):
+ *   - vr_fill_codes(): draws uniformly from all 16 E2M1 codes;
+ *   - vr_gemm_ref_blockscaled(): per-(row, 16-block) scales from encoded UE4M3 bytes,
+ *     the scale model of tcgen05 block-scaled MMA, exact per 64-wide K step.
+ *
+ * Host-only C++ (no CUDA).  The mma.sync fragment index helpers of the reference header
+ * are not provided: they belong to the mma.sync instruction tests, not to this path.
+ */
+#pragma once
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+
+struct EncVal {
+    uint32_t enc;
+    float val;
+};
+
+/* Value sets {0, +-0.5, +-1, +-1.5, +-2} in each operand format.  Every pairwise product is
+ * a multiple of 1/4, so for K <= 64 any fp32 summation order gives the same result. */
+static const EncVal FP16_SET[] = {{0x0000, 0.f},  {0x3800, 0.5f},  {0x3C00, 1.f},  {0x3E00, 1.5f}, {0x4000, 2.f},
+                                  {0xB800, -0.5f}, {0xBC00, -1.f}, {0xBE00, -1.5f}, {0xC000, -2.f}};
+static const EncVal BF16_SET[] = {{0x0000, 0.f},  {0x3F00, 0.5f},  {0x3F80, 1.f},  {0x3FC0, 1.5f}, {0x4000, 2.f},
+                                  {0xBF00, -0.5f}, {0xBF80, -1.f}, {0xBFC0, -1.5f}, {0xC000, -2.f}};
+static const EncVal TF32_SET[] = {{0x00000000, 0.f},  {0x3F000000, 0.5f},  {0x3F800000, 1.f},
+                                  {0x3FC00000, 1.5f}, {0x40000000, 2.f},   {0xBF000000, -0.5f},
+                                  {0xBF800000, -1.f}, {0xBFC00000, -1.5f}, {0xC0000000, -2.f}};
+static const EncVal E4M3_SET[] = {{0x00, 0.f},  {0x30, 0.5f},  {0x38, 1.f},  {0x3C, 1.5f}, {0x40, 2.f},
+                                  {0xB0, -0.5f}, {0xB8, -1.f}, {0xBC, -1.5f}, {0xC0, -2.f}};
+static const EncVal E2M1_SET[] = {{0x0, 0.f},  {0x1, 0.5f},  {0x2, 1.f},  {0x3, 1.5f}, {0x4, 2.f},
+                                  {0x9, -0.5f}, {0xA, -1.f}, {0xB, -1.5f}, {0xC, -2.f}};
+static const EncVal S8_SET[] = {{0x00, 0.f}, {0x01, 1.f}, {0x02, 2.f}, {0xFF, -1.f}, {0xFE, -2.f}};
+static const EncVal S4_SET[] = {{0x0, 0.f}, {0x1, 1.f}, {0x2, 2.f}, {0xF, -1.f}, {0xE, -2.f}};
+/* Block-scale sets: UE8M0 powers of two 2^-3..2^3; UE4M3 exponents {0.5, 1, 2} times even
+ * mantissas {1, 1.25, 1.5, 1.75} (12 values). */
+static const EncVal UE8M0_SET[] = {{0x7C, 0.125f}, {0x7D, 0.25f}, {0x7E, 0.5f}, {0x7F, 1.f},
+                                   {0x80, 2.f},    {0x81, 4.f},   {0x82, 8.f}};
+static const EncVal UE4M3_SET[] = {{0x30, 0.5f},  {0x32, 0.625f}, {0x34, 0.75f}, {0x36, 0.875f},
+                                   {0x38, 1.f},   {0x3A, 1.25f},  {0x3C, 1.5f},  {0x3E, 1.75f},
+                                   {0x40, 2.f},   {0x42, 2.5f},   {0x44, 3.f},   {0x46, 3.5f}};
+#define SETN(s) (int)(sizeof(s) / sizeof(EncVal))
+
+/* 32-bit xorshift with shifts 13 / 17 / 5; the seed is the whole state. */
+static inline uint32_t xorshift(uint32_t* s) {
+    uint32_t x = *s;
+    x ^= x << 13;
+    x ^= x >> 17;
+    x ^= x << 5;
+    return *s = x;
+}
+
+/* Store `enc` as element `idx` of buf; ebits in {4, 8, 16, 32}, little endian, 4-bit
+ * element 2j in the low nibble of byte j. */
+static inline void pack_set(uint8_t* buf, int idx, uint32_t enc, int ebits) {
+    switch (ebits) {
+        case 4: {
+            uint8_t& b = buf[idx >> 1];
+            const int sh = (idx & 1) * 4;
+            b = (uint8_t)((b & ~(0xF << sh)) | ((enc & 0xF) << sh));
+            break;
+        }
+        case 8: buf[idx] = (uint8_t)enc; break;
+        case 16: memcpy(buf + 2 * idx, &enc, 2); break;
+        default: memcpy(buf + 4 * idx, &enc, 4); break;
+    }
+}
+
+/* rows x K draws, row-major, one xorshift per element: the encoding goes to enc_buf, the
+ * value to ref[row * K + k]. */
+static inline void fill_random(uint8_t* enc_buf, float* ref, int rows, int K, const EncVal* set, int setn,
+                               int ebits, uint32_t* seed) {
+    const int n = rows * K;
+    for (int i = 0; i < n; i++) {
+        const EncVal& e = set[xorshift(seed) % (uint32_t)setn];
+        pack_set(enc_buf, i, e.enc, ebits);
+        ref[i] = e.val;
+    }
+}
+
+/* Write the exact value v (which must be in the set) at (row, k). */
+static inline void set_elem(uint8_t* enc_buf, float* ref, int K, int row, int k, float v, const EncVal* set,
+                            int setn, int ebits) {
+    for (int i = 0; i < setn; i++) {
+        if (set[i].val != v) continue;
+        pack_set(enc_buf, row * K + k, set[i].enc, ebits);
+        ref[row * K + k] = v;
+        return;
+    }
+    fprintf(stderr, "set_elem: %f not in value set\n", v);
+    exit(1);
+}
+
+/* D[m*N+n] = sum_k A[m*K+k] * B[n*K+k], fp32, k ascending. */
+static inline void cpu_gemm_ref(const float* A, const float* B, float* D, int M, int N, int K) {
+    for (int m = 0; m < M; m++) {
+        const float* a = A + (size_t)m * K;
+        for (int n = 0; n < N; n++) {
+            const float* b = B + (size_t)n * K;
+            float acc = 0.f;
+            for (int k = 0; k < K; k++) acc += a[k] * b[k];
+            D[(size_t)m * N + n] = acc;
+        }
+    }
+}
+
+/* Element-wise == comparison; prints the first four mismatches and a PASS/FAIL line. */
+static inline int check_exact(const float* got, const float* want, int n, const char* tag) {
+    int bad = 0;
+    for (int i = 0; i < n; i++) {
+        if (got[i] == want[i]) continue;
+        if (bad < 4) printf("  [%s] MISMATCH @%d: got %g want %g\n", tag, i, got[i], want[i]);
+        bad++;
+    }
+    printf("  %-10s %s (%d/%d exact)\n", tag, bad ? "FAIL" : "PASS", n - bad, n);
+    return bad;
+}
+
+/* Segment-scaled reference: K split into nseg equal segments, one scale pair per segment
+ * broadcast over all rows; per segment an fp32 partial sum, then acc += sfa*sfb*partial. */
+static inline void cpu_gemm_ref_bs(const float* A, const float* B, float* D, int M, int N, int K, const float* sfa,
+                                   const float* sfb, int nseg) {
+    const int seg_len = K / nseg;
+    for (int m = 0; m < M; m++)
+        for (int n = 0; n < N; n++) {
+            float acc = 0.f;
+            for (int g = 0; g < nseg; g++) {
+                float part = 0.f;
+                for (int k = g * seg_len; k < (g + 1) * seg_len; k++) part += A[m * K + k] * B[n * K + k];
+                acc += sfa[g] * sfb[g] * part;
+            }
+            D[m * N + n] = acc;
+        }
+}
+
+/* No-swizzle core-matrix order for K=64 FP4 rows of 32 bytes: byte (m, kb) moves to
+ * (m/8)*256 + (kb/16)*128 + (m%8)*16 + kb%16 (8-row x 16-byte tiles, LBO 128, SBO 256). */
+static inline void vr_to_core_matrix(uint8_t* buf, int rows) {
+    static uint8_t tmp[256 * 32];
+    memcpy(tmp, buf, (size_t)rows * 32);
+    for (int m = 0; m < rows; m++)
+        for (int kb = 0; kb < 32; kb++) buf[(m / 8) * 256 + (kb / 16) * 128 + (m % 8) * 16 + kb % 16] = tmp[m * 32 + kb];
+}
+
+static inline float vr_u32f(uint32_t u) {
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+/* Encodings of the probe values {0, 1, 2, 3, 4, 6} in each format. */
+static const uint32_t VR_ENC_FP16[6] = {0x0000, 0x3C00, 0x4000, 0x4200, 0x4400, 0x4600};
+static const uint32_t VR_ENC_BF16[6] = {0x0000, 0x3F80, 0x4000, 0x4040, 0x4080, 0x40C0};
+static const uint32_t VR_ENC_TF32[6] = {0, 0x3F800000, 0x40000000, 0x40400000, 0x40800000, 0x40C00000};
+static const uint32_t VR_ENC_E4M3[6] = {0x00, 0x38, 0x40, 0x44, 0x48, 0x4C};
+static const uint32_t VR_ENC_E2M1[6] = {0x0, 0x2, 0x4, 0x5, 0x6, 0x7};
+static const uint32_t VR_ENC_S8[6] = {0, 1, 2, 3, 4, 6};
+static inline uint32_t vr_enc_small(const uint32_t* tab, int v) {
+    static const int probe_vals[6] = {0, 1, 2, 3, 4, 6};
+    for (int i = 0; i < 6; i++)
+        if (probe_vals[i] == v) return tab[i];
+    return 0;
+}
+
+struct VrSpec {
+    int M, N, K;                 /* logical shape */
+    int ebits, is_int;
+    const EncVal* dset;          /* data value set */
+    int dsetn;
+    const EncVal* sset;          /* scale value set (NULL = no block scale) */
+    int ssetn;
+    int nseg;                    /* scale segments along K */
+    uint32_t sf_one;             /* encoding of scale 1.0 (probe rounds) */
+    int core_matrix;             /* shuffle A/B into core-matrix order before run() */
+    int probe;                   /* 1 = D layout unknown: run() returns raw slots, mapped by a probe */
+    int nslot;                   /* raw slots returned in probe mode */
+    const uint32_t* enc_tab;     /* probe-value encodings (probe mode) */
+};
+/* run(): hA / hB already in final layout; sf*_enc one encoding per segment; out receives
+ * nslot raw u32 (probe mode) or M*N floats. */
+typedef void (*VrRunFn)(const uint8_t* hA, const uint8_t* hB, const uint32_t* sfa_enc, const uint32_t* sfb_enc,
+                        void* out);
+
+/* Randomized driver: optional base-4 layout probe, then three rounds of
+ * {draw scales, draw A, draw B, CPU reference, run(), exact compare}.  Returns 0 on PASS.
+ * The draw order (scales a/b interleaved per segment, then A, then B) fixes the whole
+ * random sequence by `seed`. */
+static inline int vr_verify(const VrSpec& sp, VrRunFn run, uint32_t seed) {
+    static uint8_t hA[256 * 32], hB[256 * 32];
+    static float refA[256 * 64], refB[256 * 64], refD[256 * 256];
+    static uint32_t raw[65536];
+    static float dlin[256 * 256];
+    static int slot_row[65536], slot_col[65536];
+    static bool slot_ok[65536];
+    uint32_t sf_unit[8];
+    for (int g = 0; g < 8; g++) sf_unit[g] = sp.sf_one;
+    printf("\n====== random data%s vs CPU reference (seed=%u) ======\n", sp.sset ? " + random scales" : "", seed);
+
+    if (sp.probe) {
+        /* Value-carries-coordinate probe: with A[m][0] = base-4 digit d of m (B[n][0] = 1),
+         * every slot reads digit d of its row; four digits give the row, four more rounds
+         * with the roles swapped give the column, and a doubled round rejects stale slots. */
+        static int dig_r[4][65536], dig_c[4][65536], dbl[65536];
+        auto probe_round = [&](int a_digit, int b_digit, int doubled, int* dst) {
+            memset(hA, 0, sizeof(hA));
+            memset(hB, 0, sizeof(hB));
+            for (int m = 0; m < sp.M; m++) {
+                const int v = a_digit < 0 ? 1 : ((m >> (2 * a_digit)) & 3) * (doubled ? 2 : 1);
+                pack_set(hA, m * sp.K, vr_enc_small(sp.enc_tab, v), sp.ebits);
+            }
+            for (int n = 0; n < sp.N; n++) {
+                const int v = b_digit < 0 ? 1 : ((n >> (2 * b_digit)) & 3);
+                pack_set(hB, n * sp.K, vr_enc_small(sp.enc_tab, v), sp.ebits);
+            }
+            if (sp.core_matrix) {
+                vr_to_core_matrix(hA, sp.M);
+                vr_to_core_matrix(hB, sp.N);
+            }
+            run(hA, hB, sf_unit, sf_unit, raw);
+            for (int s = 0; s < sp.nslot; s++) dst[s] = sp.is_int ? (int)(int32_t)raw[s] : (int)vr_u32f(raw[s]);
+        };
+        for (int d = 0; d < 4; d++) probe_round(d, -1, 0, dig_r[d]);
+        for (int d = 0; d < 4; d++) probe_round(-1, d, 0, dig_c[d]);
+        probe_round(0, -1, 1, dbl);
+        static bool used[256][256];
+        memset(used, 0, sizeof(used));
+        int nvalid = 0;
+        for (int s = 0; s < sp.nslot; s++) {
+            bool ok = true;
+            int row = 0, col = 0;
+            for (int d = 0; d < 4 && ok; d++) {
+                if (dig_r[d][s] < 0 || dig_r[d][s] > 3 || dig_c[d][s] < 0 || dig_c[d][s] > 3) ok = false;
+                row |= dig_r[d][s] << (2 * d);
+                col |= dig_c[d][s] << (2 * d);
+            }
+            ok = ok && row < sp.M && col < sp.N && dbl[s] == 2 * dig_r[0][s] && !used[row][col];
+            slot_ok[s] = ok;
+            slot_row[s] = row;
+            slot_col[s] = col;
+            if (ok) {
+                used[row][col] = true;
+                nvalid++;
+            }
+        }
+        printf("D layout probe: %d/%d slots consistent\n", nvalid, sp.nslot);
+        if (nvalid < sp.nslot / 4) {
+            printf("====== FAIL (probe found too few slots) ======\n");
+            return 1;
+        }
+    }
+
+    int bad = 0;
+    for (int round = 0; round < 3; round++) {
+        uint32_t sfa[8], sfb[8];
+        float sfa_v[8], sfb_v[8];
+        for (int g = 0; g < 8; g++) {
+            sfa[g] = sfb[g] = sp.sf_one;
+            sfa_v[g] = sfb_v[g] = 1.f;
+        }
+        if (sp.sset) {
+            for (int g = 0; g < sp.nseg; g++) {
+                const EncVal& ea = sp.sset[xorshift(&seed) % (uint32_t)sp.ssetn];
+                const EncVal& eb = sp.sset[xorshift(&seed) % (uint32_t)sp.ssetn];
+                sfa[g] = ea.enc;
+                sfa_v[g] = ea.val;
+                sfb[g] = eb.enc;
+                sfb_v[g] = eb.val;
+            }
+        }
+        memset(hA, 0, sizeof(hA));
+        memset(hB, 0, sizeof(hB));
+        fill_random(hA, refA, sp.M, sp.K, sp.dset, sp.dsetn, sp.ebits, &seed);
+        fill_random(hB, refB, sp.N, sp.K, sp.dset, sp.dsetn, sp.ebits, &seed);
+        if (sp.sset) cpu_gemm_ref_bs(refA, refB, refD, sp.M, sp.N, sp.K, sfa_v, sfb_v, sp.nseg);
+        else cpu_gemm_ref(refA, refB, refD, sp.M, sp.N, sp.K);
+        if (sp.core_matrix) {
+            vr_to_core_matrix(hA, sp.M);
+            vr_to_core_matrix(hB, sp.N);
+        }
+        run(hA, hB, sfa, sfb, sp.probe ? (void*)raw : (void*)dlin);
+        static float got[65536], want[65536];
+        int n = 0;
+        if (sp.probe) {
+            for (int s = 0; s < sp.nslot; s++) {
+                if (!slot_ok[s]) continue;
+                got[n] = sp.is_int ? (float)(int32_t)raw[s] : vr_u32f(raw[s]);
+                want[n] = refD[slot_row[s] * sp.N + slot_col[s]];
+                n++;
+            }
+        } else {
+            for (int i = 0; i < sp.M * sp.N; i++) {
+                got[n] = dlin[i];
+                want[n] = refD[i];
+                n++;
+            }
+        }
+        char tag[16];
+        snprintf(tag, sizeof(tag), "random r%d", round);
+        bad += check_exact(got, want, n, tag);
+    }
+    printf("====== %s ======\n", bad ? "FAIL" : "ALL PASS");
+    return bad ? 1 : 0;
+}
+
+/* ------------------------------------------------------------ additions ---- */
+
+/* rows x K E2M1 codes drawn uniformly from all 16 codes (one xorshift per element, row
+ * major); values to ref. */
+static inline void vr_fill_codes(uint8_t* packed, float* ref, int rows, int K, uint32_t* seed) {
+    static const float mag[8] = {0.f, .5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+    for (int i = 0; i < rows * K; i++) {
+        const uint32_t c = xorshift(seed) & 0xF;
+        pack_set(packed, i, c, 4);
+        ref[i] = (c & 8) ? -mag[c & 7] : mag[c & 7];
+    }
+}
+
+/* UE4M3 byte -> value (bias 7, 3 mantissa bits, subnormals below 2^-6). */
+static inline float vr_ue4m3(uint8_t b) {
+    const int e = (b >> 3) & 0xF, m = b & 7;
+    if (e == 0) return std::ldexp((float)m, -9);
+    return std::ldexp(1.f + (float)m / 8.f, e - 7);
+}
+
+/* D[m][n] with per-(row, 16-block) scales sfa[m*(K/16)+kb], sfb[n*(K/16)+kb] (UE4M3 bytes):
+ * every 16-block term is exact; per 64-wide K step the four terms are summed exactly and
+ * added to the fp32 accumulator with one rounding. */
+static inline void vr_gemm_ref_blockscaled(const float* A, const float* B, const uint8_t* sfa, const uint8_t* sfb,
+                                           float* D, int M, int N, int K) {
+    const int nkb = K / 16;
+    for (int m = 0; m < M; m++)
+        for (int n = 0; n < N; n++) {
+            float acc = 0.f;
+            for (int k0 = 0; k0 < nkb; k0 += 4) {
+                long double step = 0.0L;
+                for (int kb = k0; kb < k0 + 4 && kb < nkb; kb++) {
+                    float s = 0.f;
+                    for (int k = kb * 16; k < kb * 16 + 16; k++) s += A[m * K + k] * B[n * K + k];
+                    step += (long double)s * (long double)vr_ue4m3(sfa[m * nkb + kb]) *
+                            (long double)vr_ue4m3(sfb[n * nkb + kb]);
+                }
+                acc = (float)((long double)acc + step);
+            }
+            D[m * N + n] = acc;
+        }
+}

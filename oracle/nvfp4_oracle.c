@@ -1,0 +1,402 @@
+/*
+ * nvfp4_oracle.c -- CPU restatement of the NVFP4 data path (TEST INFRASTRUCTURE ONLY).
+ *
+ * See nvfp4_oracle.h for the contract.  Build flags matter: this file must be compiled
+ * with -ffp-contract=off and without -ffast-math so that every a*b and a+b is one IEEE
+ * operation, exactly like the CUDA kernels (which use __fmul_rn / __fdiv_rn / __fmaf_rn
+ * explicitly).  Fused multiply-adds are written as fmaf() where the kernels use them.
+ */
+#include "nvfp4_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------ RNG ---- */
+/* random_cpu_ref/verify_random.h:63 -- xorshift32 with shifts 13, 17, 5. */
+uint32_t orc_xorshift(uint32_t* state) {
+    uint32_t s = *state;
+    s ^= s << 13;
+    s ^= s >> 17;
+    s ^= s << 5;
+    *state = s;
+    return s;
+}
+
+/* -------------------------------------------------------------- helpers ---- */
+static uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+/* Round a non-negative float holding at most 24 significant bits to the nearest integer,
+ * ties to even.  Exact: every intermediate is representable. */
+static float rne_int(float y) {
+    float r = floorf(y);
+    float d = y - r;
+    if (d > 0.5f) return r + 1.0f;
+    if (d < 0.5f) return r;
+    return (fmodf(r, 2.0f) == 0.0f) ? r : r + 1.0f;
+}
+
+/* ------------------------------------------------------------- codecs ---- */
+/* E2M1 magnitudes by code: 0, .5, 1, 1.5, 2, 3, 4, 6.  Round-to-nearest-even decision
+ * points: ties at 0.25 / 1.25 / 2.5 / 5 go down (to the even code), ties at 0.75 / 1.75
+ * / 3.5 go up (to the even code); above 6 saturates. */
+uint8_t orc_e2m1_encode(float x) {
+    const uint8_t sign = (f2u(x) >> 28) & 0x8;
+    const float a = fabsf(x);
+    uint8_t code = (uint8_t)((a > 0.25f) + (a >= 0.75f) + (a > 1.25f) + (a >= 1.75f) +
+                             (a > 2.5f) + (a >= 3.5f) + (a > 5.0f));
+    return (uint8_t)(sign | code);
+}
+
+float orc_e2m1_decode(uint8_t code) {
+    static const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+    const float m = mag[code & 7];
+    return (code & 8) ? -m : m;
+}
+
+uint8_t orc_e4m3_encode(float x) {
+    const uint8_t sign = (uint8_t)((f2u(x) >> 24) & 0x80);
+    if (isnan(x)) return (uint8_t)(sign | 0x7F);
+    const float a = fabsf(x);
+    if (a >= 448.0f) return (uint8_t)(sign | 0x7E);          /* satfinite */
+    if (a < 0.015625f) {                                     /* below 2^-6: subnormal grid 2^-9 */
+        const float q = rne_int(a * 512.0f);                 /* 0..8; 8 is the first normal */
+        return (uint8_t)(sign | (uint8_t)q);
+    }
+    int e2;
+    frexpf(a, &e2);                                          /* a = f * 2^e2, f in [0.5, 1) */
+    int E = e2 - 1;                                          /* a = 1.m * 2^E, E in [-6, 8] */
+    float q = rne_int(ldexpf(a, 3 - E) - 8.0f);              /* mantissa in eighths */
+    if (q >= 8.0f) { q = 0.0f; E += 1; }
+    return (uint8_t)(sign | (uint8_t)(((E + 7) << 3) | (int)q));
+}
+
+float orc_e4m3_decode(uint8_t code) {
+    const int e = (code >> 3) & 0xF, m = code & 7;
+    float v;
+    if (e == 15 && m == 7) v = NAN;
+    else if (e == 0) v = ldexpf((float)m, -9);
+    else v = ldexpf(1.0f + (float)m / 8.0f, e - 7);
+    return (code & 0x80) ? -v : v;
+}
+
+void orc_e2m1_encode_array(const float* x, uint8_t* out, int64_t n) {
+    for (int64_t i = 0; i < n; i++) out[i] = orc_e2m1_encode(x[i]);
+}
+
+void orc_e4m3_encode_array(const float* x, uint8_t* out, int64_t n) {
+    for (int64_t i = 0; i < n; i++) out[i] = orc_e4m3_encode(x[i]);
+}
+
+uint16_t orc_f32_to_bf16(float x) {
+    uint32_t u = f2u(x);
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((u >> 16) | 0x40);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+float orc_bf16_to_f32(uint16_t h) { return u2f((uint32_t)h << 16); }
+
+/* --------------------------------------------------- scale-factor layout ---- */
+int64_t orc_sf_offset(int64_t row, int64_t kblock, int64_t cols) {
+    const int64_t katoms = (cols + 63) / 64;
+    const int64_t atom = (row / 128) * katoms + kblock / 4;
+    return atom * 512 + (row % 32) * 16 + ((row % 128) / 32) * 4 + (kblock % 4);
+}
+
+int64_t orc_sf_bytes(int64_t rows, int64_t cols) {
+    return ((rows + 127) / 128) * ((cols + 63) / 64) * 512;
+}
+
+/* -------------------------------------------------------------- quantize ---- */
+void orc_global_scale(float amax, float* gs, float* gs_inv) {
+    float g = (amax > 0.0f) ? amax / 2688.0f : 1.0f;   /* 2688 = 6 * 448 */
+    if (g == 0.0f) g = 1.0f;                            /* amax below 2688 * min subnormal */
+    *gs = g;
+    *gs_inv = 1.0f / g;
+}
+
+float orc_amax_bf16(const uint16_t* x, int64_t n) {
+    float m = 0.0f;
+    for (int64_t i = 0; i < n; i++) {
+        const float a = fabsf(orc_bf16_to_f32(x[i]));
+        if (a > m) m = a;
+    }
+    return m;
+}
+
+float orc_amax_f32(const float* x, int64_t n) {
+    float m = 0.0f;
+    for (int64_t i = 0; i < n; i++) {
+        const float a = fabsf(x[i]);
+        if (a > m) m = a;
+    }
+    return m;
+}
+
+void orc_q16(const float* v, float gs_inv, uint8_t* nib, uint8_t* sf) {
+    float amax = 0.0f;
+    for (int i = 0; i < 16; i++) amax = fmaxf(amax, fabsf(v[i]));
+    const float t = amax / 6.0f;
+    const float s = t * gs_inv;
+    const uint8_t code = orc_e4m3_encode(s);
+    const float sq = orc_e4m3_decode(code);
+    *sf = code;
+    if (sq == 0.0f) {
+        for (int i = 0; i < 16; i++) nib[i] = 0;
+        return;
+    }
+    const float inv = gs_inv / sq;
+    for (int i = 0; i < 16; i++) {
+        const float y = v[i] * inv;
+        nib[i] = orc_e2m1_encode(y);
+    }
+}
+
+typedef struct {
+    const uint16_t* xb;
+    const float* xf;
+    int64_t rows, cols, r0, r1;
+    float gs_inv;
+    uint8_t* packed;
+    uint8_t* sf;
+} quant_job;
+
+static void quant_rows(const quant_job* j) {
+    float v[16];
+    uint8_t nib[16], s;
+    for (int64_t r = j->r0; r < j->r1; r++) {
+        for (int64_t kb = 0; kb < j->cols / 16; kb++) {
+            const int64_t base = r * j->cols + kb * 16;
+            for (int i = 0; i < 16; i++)
+                v[i] = j->xb ? orc_bf16_to_f32(j->xb[base + i]) : j->xf[base + i];
+            orc_q16(v, j->gs_inv, nib, &s);
+            uint8_t* dst = j->packed + base / 2;
+            for (int i = 0; i < 8; i++) dst[i] = (uint8_t)(nib[2 * i] | (nib[2 * i + 1] << 4));
+            j->sf[orc_sf_offset(r, kb, j->cols)] = s;
+        }
+    }
+}
+
+static void* quant_thread(void* p) { quant_rows((const quant_job*)p); return NULL; }
+
+static void quantize_any(const uint16_t* xb, const float* xf, int64_t rows, int64_t cols,
+                         float gs, uint8_t* packed, uint8_t* sf, int nthreads) {
+    const float gs_inv = 1.0f / gs;
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    if (nthreads > rows) nthreads = (int)(rows > 0 ? rows : 1);
+    pthread_t th[256];
+    quant_job jobs[256];
+    for (int t = 0; t < nthreads; t++) {
+        jobs[t] = (quant_job){xb, xf, rows, cols, rows * t / nthreads, rows * (t + 1) / nthreads,
+                              gs_inv, packed, sf};
+    }
+    if (nthreads == 1) { quant_rows(&jobs[0]); return; }
+    for (int t = 0; t < nthreads; t++) pthread_create(&th[t], NULL, quant_thread, &jobs[t]);
+    for (int t = 0; t < nthreads; t++) pthread_join(th[t], NULL);
+}
+
+void orc_quantize_bf16(const uint16_t* x, int64_t rows, int64_t cols, float gs,
+                       uint8_t* packed, uint8_t* sf, int nthreads) {
+    quantize_any(x, NULL, rows, cols, gs, packed, sf, nthreads);
+}
+
+void orc_quantize_f32(const float* x, int64_t rows, int64_t cols, float gs,
+                      uint8_t* packed, uint8_t* sf, int nthreads) {
+    quantize_any(NULL, x, rows, cols, gs, packed, sf, nthreads);
+}
+
+static float dq_value(const uint8_t* packed, const uint8_t* sf, int64_t r, int64_t c,
+                      int64_t cols, float gs) {
+    const int64_t idx = r * cols + c;
+    const uint8_t byte = packed[idx / 2];
+    const uint8_t code = (idx & 1) ? (byte >> 4) : (byte & 0xF);
+    const float bs = orc_e4m3_decode(sf[orc_sf_offset(r, c / 16, cols)]) * gs;
+    return orc_e2m1_decode(code) * bs;
+}
+
+void orc_dequantize_f32(const uint8_t* packed, const uint8_t* sf, int64_t rows, int64_t cols,
+                        float gs, float* out) {
+    for (int64_t r = 0; r < rows; r++)
+        for (int64_t c = 0; c < cols; c++) out[r * cols + c] = dq_value(packed, sf, r, c, cols, gs);
+}
+
+void orc_dequantize_bf16(const uint8_t* packed, const uint8_t* sf, int64_t rows, int64_t cols,
+                         float gs, uint16_t* out) {
+    for (int64_t r = 0; r < rows; r++)
+        for (int64_t c = 0; c < cols; c++)
+            out[r * cols + c] = orc_f32_to_bf16(dq_value(packed, sf, r, c, cols, gs));
+}
+
+/* ------------------------------------------------------------------ GEMM ---- */
+/* Exact value of one 16-element block product sum_k a_k b_k * sfa * sfb.  Each E2M1
+ * product is a multiple of 1/4 below 37, so the 16-term sum is exact in float; the two
+ * UE4M3 scales have 4 significant bits each; the result has at most 21 significant bits
+ * and is exact in double. */
+static double block_term(const uint8_t* A, const uint8_t* sfa, const uint8_t* B,
+                         const uint8_t* sfb, int64_t m, int64_t n, int64_t K, int64_t kb) {
+    float s = 0.0f;
+    const uint8_t* a = A + (m * K + kb * 16) / 2;
+    const uint8_t* b = B + (n * K + kb * 16) / 2;
+    for (int i = 0; i < 8; i++) {
+        s += orc_e2m1_decode(a[i] & 0xF) * orc_e2m1_decode(b[i] & 0xF);
+        s += orc_e2m1_decode(a[i] >> 4) * orc_e2m1_decode(b[i] >> 4);
+    }
+    const double sa = orc_e4m3_decode(sfa[orc_sf_offset(m, kb, K)]);
+    const double sb = orc_e4m3_decode(sfb[orc_sf_offset(n, kb, K)]);
+    return (double)s * (sa * sb);
+}
+
+static float gemm_point(const uint8_t* A, const uint8_t* sfa, const uint8_t* B,
+                        const uint8_t* sfb, int64_t m, int64_t n, int64_t K, int model) {
+    const int64_t nkb = K / 16;
+    float acc = 0.0f;
+    if (model == ORC_ACC_EXACT_ALL) {
+        long double t = 0.0L;
+        for (int64_t kb = 0; kb < nkb; kb++) t += (long double)block_term(A, sfa, B, sfb, m, n, K, kb);
+        return (float)t;
+    }
+    if (model == ORC_ACC_PER_BLOCK) {
+        for (int64_t kb = 0; kb < nkb; kb++)
+            acc = (float)((long double)acc + (long double)block_term(A, sfa, B, sfb, m, n, K, kb));
+        return acc;
+    }
+    for (int64_t k0 = 0; k0 < nkb; k0 += 4) {
+        long double step = 0.0L;
+        for (int64_t kb = k0; kb < k0 + 4 && kb < nkb; kb++)
+            step += (long double)block_term(A, sfa, B, sfb, m, n, K, kb);
+        if (model == ORC_ACC_ROUND_PER_MMA) acc = acc + (float)step;
+        else acc = (float)((long double)acc + step);
+    }
+    return acc;
+}
+
+typedef struct {
+    const uint8_t *A, *sfa, *B, *sfb;
+    int64_t M, N, K, r0, r1;
+    int model;
+    float* D;
+} gemm_job;
+
+static void* gemm_thread(void* p) {
+    const gemm_job* j = (const gemm_job*)p;
+    for (int64_t m = j->r0; m < j->r1; m++)
+        for (int64_t n = 0; n < j->N; n++)
+            j->D[m * j->N + n] = gemm_point(j->A, j->sfa, j->B, j->sfb, m, n, j->K, j->model);
+    return NULL;
+}
+
+void orc_gemm_f32(const uint8_t* A, const uint8_t* sfa, const uint8_t* B, const uint8_t* sfb,
+                  int64_t M, int64_t N, int64_t K, int model, float* D, int nthreads) {
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    if (nthreads > M) nthreads = (int)(M > 0 ? M : 1);
+    pthread_t th[256];
+    gemm_job jobs[256];
+    for (int t = 0; t < nthreads; t++)
+        jobs[t] = (gemm_job){A, sfa, B, sfb, M, N, K, M * t / nthreads, M * (t + 1) / nthreads,
+                             model, D};
+    if (nthreads == 1) { gemm_thread(&jobs[0]); return; }
+    for (int t = 0; t < nthreads; t++) pthread_create(&th[t], NULL, gemm_thread, &jobs[t]);
+    for (int t = 0; t < nthreads; t++) pthread_join(th[t], NULL);
+}
+
+void orc_gemm_f32_points(const uint8_t* A, const uint8_t* sfa, const uint8_t* B,
+                         const uint8_t* sfb, int64_t M, int64_t N, int64_t K, int model,
+                         const int64_t* ms, const int64_t* ns, int64_t npts, float* out) {
+    (void)M; (void)N;
+    for (int64_t i = 0; i < npts; i++) out[i] = gemm_point(A, sfa, B, sfb, ms[i], ns[i], K, model);
+}
+
+uint16_t orc_gemm_epilogue_bf16(float acc, float alpha) {
+    const float y = acc * alpha;
+    return orc_f32_to_bf16(y);
+}
+
+/* ------------------------------------------------------------ all-reduce ---- */
+typedef struct {
+    const uint16_t* const* in;
+    int n;
+    int64_t numel, e0, e1; /* element range, multiples of 16 */
+    float gs;
+    int twoshot;
+    uint16_t* out;
+} ar_job;
+
+/* Quantize the 16-element block at element offset e of rank r's input with gs_inv. */
+static void ar_quant_block(const uint16_t* x, int64_t e, float gs_inv, uint8_t* nib, uint8_t* sf) {
+    float v[16];
+    for (int i = 0; i < 16; i++) v[i] = orc_bf16_to_f32(x[e + i]);
+    orc_q16(v, gs_inv, nib, sf);
+}
+
+static void* ar_thread(void* p) {
+    const ar_job* j = (const ar_job*)p;
+    const float gs_inv = 1.0f / j->gs;
+    const float gs_red = j->gs * (float)j->n;
+    const float gs_red_inv = 1.0f / gs_red;
+    uint8_t nib[16], sf;
+    float acc[16];
+    for (int64_t e = j->e0; e < j->e1; e += 16) {
+        for (int i = 0; i < 16; i++) acc[i] = 0.0f;
+        for (int r = 0; r < j->n; r++) {             /* fixed rank order 0 .. n-1 */
+            ar_quant_block(j->in[r], e, gs_inv, nib, &sf);
+            const float bs = orc_e4m3_decode(sf) * j->gs;
+            for (int i = 0; i < 16; i++) acc[i] = fmaf(orc_e2m1_decode(nib[i]), bs, acc[i]);
+        }
+        if (j->twoshot) {                            /* requantize the reduced block */
+            orc_q16(acc, gs_red_inv, nib, &sf);
+            const float bs = orc_e4m3_decode(sf) * gs_red;
+            for (int i = 0; i < 16; i++) acc[i] = fmaf(orc_e2m1_decode(nib[i]), bs, 0.0f);
+        }
+        for (int i = 0; i < 16; i++) j->out[e + i] = orc_f32_to_bf16(acc[i]);
+    }
+    return NULL;
+}
+
+static void ar_run(const uint16_t* const* inputs, int n, int64_t numel, float gs, int twoshot,
+                   uint16_t* out, int nthreads) {
+    const int64_t blocks = numel / 16;
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    if (nthreads > blocks) nthreads = (int)(blocks > 0 ? blocks : 1);
+    pthread_t th[256];
+    ar_job jobs[256];
+    for (int t = 0; t < nthreads; t++)
+        jobs[t] = (ar_job){inputs, n, numel, blocks * t / nthreads * 16,
+                           blocks * (t + 1) / nthreads * 16, gs, twoshot, out};
+    if (nthreads == 1) { ar_thread(&jobs[0]); return; }
+    for (int t = 0; t < nthreads; t++) pthread_create(&th[t], NULL, ar_thread, &jobs[t]);
+    for (int t = 0; t < nthreads; t++) pthread_join(th[t], NULL);
+}
+
+void orc_ar_oneshot(const uint16_t* const* inputs, int n, int64_t numel, float gs,
+                    uint16_t* out, int nthreads) {
+    ar_run(inputs, n, numel, gs, 0, out, nthreads);
+}
+
+void orc_ar_twoshot(const uint16_t* const* inputs, int n, int64_t numel, float gs,
+                    uint16_t* out, int nthreads) {
+    ar_run(inputs, n, numel, gs, 1, out, nthreads);
+}
+
+void orc_ar_bf16(const uint16_t* const* inputs, int n, int64_t numel, uint16_t* out,
+                 int nthreads) {
+    (void)nthreads;
+    for (int64_t i = 0; i < numel; i++) {
+        float acc = 0.0f;
+        for (int r = 0; r < n; r++) acc += orc_bf16_to_f32(inputs[r][i]);
+        out[i] = orc_f32_to_bf16(acc);
+    }
+}
+
+void orc_sum_f64(const uint16_t* const* inputs, int n, int64_t numel, double* out) {
+    for (int64_t i = 0; i < numel; i++) {
+        double acc = 0.0;
+        for (int r = 0; r < n; r++) acc += (double)orc_bf16_to_f32(inputs[r][i]);
+        out[i] = acc;
+    }
+}

@@ -1,0 +1,140 @@
+/*
+ * nvfp4_oracle.h -- CPU restatement of the NVFP4 data path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the checker for the CUDA kernels in
+ * tensorcore_ptx_example_b200/csrc.  Only tests/, __graft_entry__.smoke() and the
+ * cpu_baseline / --impl reference legs of bench.py may load it.  The product path
+ * never calls into it and has no CPU fallback.
+ *
+ * Parity pins (see tests/test_oracle_pins.py):
+ *   - the xorshift stream, fill_random draw order, cpu_gemm_ref_bs and the core-matrix
+ *     shuffle are checked against the reference's own random_cpu_ref/verify_random.h,
+ *     compiled from the reference tree into oracle/_ref (recipe: oracle/Makefile) and
+ *     frozen into tests/golden/ fixtures;
+ *   - the E2M1 / UE4M3 codecs follow the OCP MX / FP8 format definitions (round to
+ *     nearest even, saturate to the largest finite value) and are checked against the
+ *     GPU's cvt.rn.satfinite conversions in the -m gpu tests;
+ *   - the quantizer, dequantizer and all-reduce sums follow the reference's q16 /
+ *     dq32_acc / fused-kernel data flow (blackwell/allreduce_sm100_sm120/
+ *     nvfp4_allreduce.cuh:272-317, :498-619) with the reference's approximate
+ *     reciprocals replaced by IEEE division so that CPU and GPU agree bit for bit.
+ *
+ * Every function below is pure host C with no CUDA dependency.
+ */
+#ifndef NVFP4_ORACLE_H
+#define NVFP4_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- RNG ---- */
+/* 32-bit xorshift (13, 17, 5); random_cpu_ref/verify_random.h:63. */
+uint32_t orc_xorshift(uint32_t* state);
+
+/* ------------------------------------------------------------- codecs ---- */
+/* E2M1: 1 sign, 2 exponent (bias 1), 1 mantissa bit; magnitudes
+ * {0, .5, 1, 1.5, 2, 3, 4, 6}.  Round to nearest even, saturate to 6, keep the sign of
+ * zero (a negative input that rounds to zero gives code 0x8).  NaN and infinite inputs
+ * are outside the contract: the quantizer never produces them from finite data. */
+uint8_t orc_e2m1_encode(float x);
+float   orc_e2m1_decode(uint8_t code);
+
+/* E4M3 (OCP FP8, bias 7, max finite 448, no infinities, 0x7F/0xFF = NaN).
+ * Round to nearest even, saturate finite overflow to +-448. */
+uint8_t orc_e4m3_encode(float x);
+float   orc_e4m3_decode(uint8_t code);
+
+/* Array forms of the two encoders (out[i] = encode(x[i])). */
+void orc_e2m1_encode_array(const float* x, uint8_t* out, int64_t n);
+void orc_e4m3_encode_array(const float* x, uint8_t* out, int64_t n);
+
+/* bfloat16 <-> float, round to nearest even. */
+uint16_t orc_f32_to_bf16(float x);
+float    orc_bf16_to_f32(uint16_t h);
+
+/* --------------------------------------------------- scale-factor layout ---- */
+/* Block-scale byte for (row, kblock) of a rows x cols tensor, kblock = col / 16, in the
+ * tcgen05 scale-factor layout: 512-byte atoms covering 128 rows x 4 kblocks, atoms
+ * ordered kblock-atom fastest, and inside an atom
+ *     offset = (row % 32) * 16 + ((row % 128) / 32) * 4 + (kblock % 4).
+ * One 32-bit word of an atom holds the four scales of one row, which is the word
+ * tcgen05.cp ... 32x128b.warpx4 places in one TMEM column. */
+int64_t orc_sf_offset(int64_t row, int64_t kblock, int64_t cols);
+/* Bytes of the scale buffer: ceil(rows/128)*128 * ceil(cols/64)*4. */
+int64_t orc_sf_bytes(int64_t rows, int64_t cols);
+
+/* -------------------------------------------------------------- quantize ---- */
+/* global scale = amax / (6 * 448) (amax == 0 -> 1.0); gs_inv = 1 / global scale. */
+void  orc_global_scale(float amax, float* gs, float* gs_inv);
+float orc_amax_bf16(const uint16_t* x, int64_t n);
+float orc_amax_f32(const float* x, int64_t n);
+
+/* One 16-element block: nib[i] = E2M1 code of element i, *sf = UE4M3 block scale.
+ *   t   = amax / 6            (IEEE div)
+ *   s   = t * gs_inv          (IEEE mul)
+ *   sf  = e4m3(s)
+ *   inv = gs_inv / decode(sf) (IEEE div); sf == 0 -> every code is 0
+ *   nib = e2m1(v * inv)       (IEEE mul, then RNE)
+ * Follows q16 (nvfp4_allreduce.cuh:272-290) with rcp.approx replaced by division. */
+void orc_q16(const float* v, float gs_inv, uint8_t* nib, uint8_t* sf);
+
+/* Quantize a row-major rows x cols tensor (cols % 16 == 0).
+ * packed: rows x cols/2 bytes, element 2j in the low nibble of byte j.
+ * sf: orc_sf_bytes(rows, cols) bytes in the tcgen05 layout (padding left as zero
+ * when the caller zeroes the buffer). */
+void orc_quantize_bf16(const uint16_t* x, int64_t rows, int64_t cols, float gs,
+                       uint8_t* packed, uint8_t* sf, int nthreads);
+void orc_quantize_f32(const float* x, int64_t rows, int64_t cols, float gs,
+                      uint8_t* packed, uint8_t* sf, int nthreads);
+
+/* Dequantize: value = e2m1(code) * (decode(sf) * gs), the product rounded once. */
+void orc_dequantize_f32(const uint8_t* packed, const uint8_t* sf, int64_t rows, int64_t cols,
+                        float gs, float* out);
+void orc_dequantize_bf16(const uint8_t* packed, const uint8_t* sf, int64_t rows, int64_t cols,
+                         float gs, uint16_t* out);
+
+/* ------------------------------------------------------------------ GEMM ---- */
+/* Accumulation models for D[m][n] = sum_k A[m][k] * B[n][k] * sfa * sfb.
+ * The product of a 16-element block (sum of 16 E2M1 x E2M1 products times the two
+ * UE4M3 scales) is always exact.  The models differ in where fp32 rounding happens. */
+enum {
+    ORC_ACC_EXACT_PER_MMA = 0, /* per 64-wide K step: exact step sum, acc = rn(acc + step) */
+    ORC_ACC_ROUND_PER_MMA = 1, /* per 64-wide K step: acc = rn(acc + rn(step)) */
+    ORC_ACC_PER_BLOCK     = 2, /* per 16-block: acc = rn(acc + block) */
+    ORC_ACC_EXACT_ALL     = 3  /* whole K exact, one rounding */
+};
+/* Block-scaled GEMM, fp32 accumulators.  A: M x K (packed, K-major), B: N x K.
+ * sfa / sfb in the tcgen05 layout.  Output D row-major M x N fp32. */
+void orc_gemm_f32(const uint8_t* A, const uint8_t* sfa, const uint8_t* B, const uint8_t* sfb,
+                  int64_t M, int64_t N, int64_t K, int model, float* D, int nthreads);
+/* Same, but only the listed (m, n) outputs (for spot checks of large GEMMs). */
+void orc_gemm_f32_points(const uint8_t* A, const uint8_t* sfa, const uint8_t* B,
+                         const uint8_t* sfb, int64_t M, int64_t N, int64_t K, int model,
+                         const int64_t* ms, const int64_t* ns, int64_t npts, float* out);
+/* bf16 epilogue: D = bf16(alpha * acc), the product rounded to fp32 first. */
+uint16_t orc_gemm_epilogue_bf16(float acc, float alpha);
+
+/* ------------------------------------------------------------ all-reduce ---- */
+/* One-shot: every rank's input quantized once with gs; output = bf16 of the fp32 sum
+ *   acc = fma(e2m1(code_r), decode(sf_r) * gs, acc) for r = 0 .. n-1, acc starting at 0.
+ * inputs: n pointers to numel bf16 values (numel % 16 == 0). */
+void orc_ar_oneshot(const uint16_t* const* inputs, int n, int64_t numel, float gs,
+                    uint16_t* out, int nthreads);
+/* Two-shot: the same fp32 sum per shard, requantized with global scale gs * n, then
+ * dequantized into bf16 (numel % (16 * n) == 0). */
+void orc_ar_twoshot(const uint16_t* const* inputs, int n, int64_t numel, float gs,
+                    uint16_t* out, int nthreads);
+/* bf16 all-reduce: acc = sum of float(x_r) in rank order, output bf16(acc). */
+void orc_ar_bf16(const uint16_t* const* inputs, int n, int64_t numel, uint16_t* out,
+                 int nthreads);
+/* Exact fp64 sum of the bf16 inputs, for error reports. */
+void orc_sum_f64(const uint16_t* const* inputs, int n, int64_t numel, double* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NVFP4_ORACLE_H */

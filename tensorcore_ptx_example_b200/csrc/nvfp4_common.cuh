@@ -1,0 +1,233 @@
+// nvfp4_common.cuh -- device helpers shared by the NVFP4 kernels (sm_100a only).
+//
+// * NVFP4 codec: E2M1 / UE4M3 conversions through the hardware cvt instructions, and the
+//   per-16-element block quantizer q16 with IEEE division (the reference's q16,
+//   blackwell/allreduce_sm100_sm120/nvfp4_allreduce.cuh:272-290, uses rcp.approx.ftz;
+//   here every reciprocal is a correctly rounded division so that a CPU reproduces the
+//   result bit for bit).
+// * Bounded waits: every spin in this library gives up after a time limit, records an
+//   error code in a device-global status word and returns false.  Nothing traps.
+// * Thin PTX wrappers for mbarrier, TMA and tcgen05.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "this library targets sm_100a only"
+#endif
+
+namespace nvfp4 {
+
+// ------------------------------------------------------------ status word ----
+// Device-global status of the library on this device (0 = OK).  Kernels write the first
+// error they detect; the host reads and clears it with nvfp4_device_status().  The library
+// is one translation unit (nvfp4_lib.cu), so this definition exists once per module.
+__device__ unsigned int g_status = 0;
+
+enum DeviceError : unsigned int {
+    DEV_OK = 0,
+    DEV_TIMEOUT_GEMM_PRODUCER = 0x101,
+    DEV_TIMEOUT_GEMM_MMA = 0x102,
+    DEV_TIMEOUT_GEMM_EPILOGUE = 0x103,
+    DEV_TIMEOUT_GEMM_TEARDOWN = 0x104,
+    DEV_TIMEOUT_AR_BARRIER = 0x201,
+};
+
+__device__ __forceinline__ void record_error(unsigned int code) {
+    atomicCAS(&g_status, 0u, code);
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ------------------------------------------------------------------ codec ----
+// Eight floats -> eight E2M1 nibbles, element i in bits [4i, 4i+4).  Hardware RNE with
+// saturation to +-6; cvt packs its first source operand into the high nibble.
+__device__ __forceinline__ uint32_t e2m1x8(const float* v) {
+    uint32_t out;
+    asm("{\n\t.reg .b8 q0, q1, q2, q3;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 q0, %2, %1;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 q1, %4, %3;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 q2, %6, %5;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 q3, %8, %7;\n\t"
+        "mov.b32 %0, {q0, q1, q2, q3};\n\t}"
+        : "=r"(out)
+        : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]));
+    return out;
+}
+
+// One float -> E4M3 byte (RNE, saturating to +-448).
+__device__ __forceinline__ uint32_t e4m3_encode(float x) {
+    uint16_t pair;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(pair) : "f"(0.0f), "f"(x));
+    return pair & 0xFFu;
+}
+
+// E4M3 byte -> float (exact).
+__device__ __forceinline__ float e4m3_decode(uint32_t code) {
+    uint32_t h2;
+    const uint16_t in = (uint16_t)(code & 0xFFu);
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(in));
+    return __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu)));
+}
+
+// Four E2M1 bytes (8 nibbles) -> 8 floats, nibble i -> out[i] (exact).
+__device__ __forceinline__ void e2m1x8_decode(uint32_t w, float* out) {
+    uint32_t h0, h1, h2, h3;
+    asm("{\n\t.reg .b8 q0, q1, q2, q3;\n\t"
+        "mov.b32 {q0, q1, q2, q3}, %4;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %0, q0;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %1, q1;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %2, q2;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %3, q3;\n\t}"
+        : "=r"(h0), "=r"(h1), "=r"(h2), "=r"(h3)
+        : "r"(w));
+    const uint32_t hs[4] = {h0, h1, h2, h3};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hs[i]));
+        out[2 * i] = f.x;
+        out[2 * i + 1] = f.y;
+    }
+}
+
+// Global scale pair from a tensor amax: gs = amax / (6 * 448), gs_inv = 1 / gs.
+__device__ __forceinline__ void global_scale_from_amax(float amax, float& gs, float& gs_inv) {
+    float g = (amax > 0.0f) ? __fdiv_rn(amax, 2688.0f) : 1.0f;
+    if (g == 0.0f) g = 1.0f;
+    gs = g;
+    gs_inv = __fdiv_rn(1.0f, g);
+}
+
+// Block scale of one 16-element block from its amax:
+//   s = (amax / 6) * gs_inv, stored as E4M3; inv = gs_inv / decode(stored) (0 when the
+//   stored scale is 0).  Returns the scale byte, writes inv.
+__device__ __forceinline__ uint32_t block_scale(float amax, float gs_inv, float& inv) {
+    const float t = __fdiv_rn(amax, 6.0f);
+    const float s = __fmul_rn(t, gs_inv);
+    const uint32_t code = e4m3_encode(s);
+    const float sq = e4m3_decode(code);
+    inv = (sq != 0.0f) ? __fdiv_rn(gs_inv, sq) : 0.0f;
+    return code;
+}
+
+// Quantize 16 floats: writes two 32-bit nibble words, returns the scale byte.
+__device__ __forceinline__ uint32_t q16(const float* v, float gs_inv, uint32_t& w0, uint32_t& w1) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; i++) amax = fmaxf(amax, fabsf(v[i]));
+    float inv;
+    const uint32_t code = block_scale(amax, gs_inv, inv);
+    float y[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) y[i] = __fmul_rn(v[i], inv);
+    w0 = e2m1x8(y);
+    w1 = e2m1x8(y + 8);
+    if (inv == 0.0f) { w0 = 0u; w1 = 0u; }
+    return code;
+}
+
+// ------------------------------------------------------------- PTX basics ----
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ void st_v4(void* p, uint4 v) {
+    asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+
+// --------------------------------------------------------------- mbarrier ----
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for the phase with the given parity to complete; false after `limit_ns`.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_t limit_ns,
+                                          unsigned int err) {
+#pragma unroll 1
+    for (int i = 0; i < 256; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > limit_ns) {
+            record_error(err);
+            return false;
+        }
+    }
+}
+
+// -------------------------------------------------------------------- TMA ----
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int32_t x, int32_t y,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(tmap), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05 ----
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Commit all prior tcgen05 async operations of this thread to an mbarrier (one arrival).
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+}  // namespace nvfp4

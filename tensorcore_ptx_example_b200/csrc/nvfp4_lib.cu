@@ -1,0 +1,5 @@
+// nvfp4_lib.cu -- the whole library as one translation unit (one definition of the device
+// status word and of every kernel; no relocatable device code needed).
+#include "capi.cu"
+#include "quantize.cu"
+#include "gemm.cu"

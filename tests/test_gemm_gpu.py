@@ -1,0 +1,136 @@
+"""Block-scaled GEMM parity on the GPU.
+
+  * the reference's own tile tests (drop-in C++ mains on include/verify_random.h) pass
+    through the C ABI;
+  * cfg1 tile (M128 N256 K256, all 16 E2M1 codes, per-(row, 16-block) scales 2^[-4, 4])
+    is bit-exact (==) against the oracle's accumulation model;
+  * quantized Gaussian GEMMs (cfg3 distributions) are bit-exact in bf16 at small sizes and
+    spot-checked bit-exact at the full 8192^3 size, with the relative error against an
+    fp32 matmul of the dequantized operands also bounded.
+"""
+import os
+import subprocess
+
+import numpy as np
+import pytest
+import torch
+
+from tensorcore_ptx_example_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+# Accumulation model that the tcgen05 block-scaled MMA follows (oracle/nvfp4_oracle.h).
+MODEL = 0   # ORC_ACC_EXACT_PER_MMA
+
+
+def test_reference_tile_tests_dropin():
+    from tensorcore_ptx_example_b200 import build
+    exes = build.build_cpp_tests()
+    for exe in exes:
+        r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
+        assert "ALL TESTS PASSED" in r.stdout
+
+
+def cfg1_tile(oracle, seed, M=128, N=256, K=256):
+    rng = np.random.default_rng(seed)
+    ca = rng.integers(0, 16, size=(M, K)).astype(np.uint8)
+    cb = rng.integers(0, 16, size=(N, K)).astype(np.uint8)
+    ea = oracle.e4m3_encode((2.0 ** rng.integers(-4, 5, size=(M, K // 16))).astype(np.float32)).reshape(M, K // 16)
+    eb = oracle.e4m3_encode((2.0 ** rng.integers(-4, 5, size=(N, K // 16))).astype(np.float32)).reshape(N, K // 16)
+    pa = (ca[:, 0::2] | (ca[:, 1::2] << 4)).astype(np.uint8)
+    pb = (cb[:, 0::2] | (cb[:, 1::2] << 4)).astype(np.uint8)
+    sa = np.zeros(oracle.sf_bytes(M, K), np.uint8)
+    sb = np.zeros(oracle.sf_bytes(N, K), np.uint8)
+    sa[oracle.sf_offsets(M, K)] = ea
+    sb[oracle.sf_offsets(N, K)] = eb
+    return pa, sa, pb, sb
+
+
+def run_f32(nv, pa, sa, pb, sb, M, N, K):
+    t = [torch.from_numpy(a).cuda() for a in (pa, sa, pb, sb)]
+    D = nv.gemm_f32(t[0], t[1], t[2], t[3], M, N, K)
+    torch.cuda.synchronize()
+    assert nv.device_status() == 0
+    return D.cpu().numpy()
+
+
+@pytest.mark.parametrize("seed", [1, 2, 3])
+def test_cfg1_tile_bitexact(nv, oracle, seed):
+    M, N, K = 128, 256, 256
+    pa, sa, pb, sb = cfg1_tile(oracle, seed)
+    got = run_f32(nv, pa, sa, pb, sb, M, N, K)
+    stats = {}
+    for model in range(4):
+        want = oracle.gemm_f32(pa, sa, pb, sb, M, N, K, model=model)
+        stats[model] = int(np.count_nonzero(got != want))
+    assert stats[MODEL] == 0, f"mismatches per accumulation model {stats}"
+
+
+def test_cfg1_multi_tile_grid(nv, oracle):
+    """Several output tiles and a longer K: every tile must match, whichever CTA ran it."""
+    M, N, K = 512, 768, 1024
+    pa, sa, pb, sb = cfg1_tile(oracle, 11, M, N, K)
+    got = run_f32(nv, pa, sa, pb, sb, M, N, K)
+    want = oracle.gemm_f32(pa, sa, pb, sb, M, N, K, model=MODEL)
+    assert np.count_nonzero(got != want) == 0
+
+
+def quantized_operands(nv, oracle, M, N, K, seed):
+    a = workloads.activations(M, K, seed=seed)
+    b = workloads.gaussian(N, K, seed=seed + 1, std=0.02)
+    pa, sa, gsa = nv.quantize(a, None)
+    pb, sb, gsb = nv.quantize(b, None)
+    torch.cuda.synchronize()
+    return pa, sa, pb, sb, float(gsa.item()), float(gsb.item())
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 256), (256, 512, 2048), (384, 256, 4096)])
+def test_gemm_bf16_bitexact(nv, oracle, M, N, K):
+    pa, sa, pb, sb, gsa, gsb = quantized_operands(nv, oracle, M, N, K, seed=M + N + K)
+    alpha = float(np.float32(gsa) * np.float32(gsb))
+    D = nv.gemm(pa, sa, pb, sb, M, N, K, alpha=alpha)
+    torch.cuda.synchronize()
+    assert nv.device_status() == 0
+    acc = oracle.gemm_f32(pa.cpu().numpy(), sa.cpu().numpy(), pb.cpu().numpy(), sb.cpu().numpy(), M, N, K,
+                          model=MODEL)
+    want = oracle.gemm_epilogue_bf16(acc, alpha)
+    got = D.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    assert np.count_nonzero(got != want) == 0
+
+
+def test_gemm_cfg3_full_size(nv, oracle):
+    M, N, K = workloads.CFG3_SHAPE
+    pa, sa, pb, sb, gsa, gsb = quantized_operands(nv, oracle, M, N, K, seed=3)
+    alpha = float(np.float32(gsa) * np.float32(gsb))
+    D = nv.gemm(pa, sa, pb, sb, M, N, K, alpha=alpha)
+    torch.cuda.synchronize()
+    assert nv.device_status() == 0
+    # (1) bit-exact spot check of 4096 seeded output positions (every tile row/col region)
+    rng = np.random.default_rng(0)
+    ms = rng.integers(0, M, 4096)
+    ns = rng.integers(0, N, 4096)
+    acc = oracle.gemm_f32_points(pa.cpu().numpy(), sa.cpu().numpy(), pb.cpu().numpy(), sb.cpu().numpy(),
+                                 M, N, K, ms, ns, model=MODEL)
+    want = oracle.gemm_epilogue_bf16(acc, alpha)
+    got = D[torch.from_numpy(ms).cuda(), torch.from_numpy(ns).cuda()].view(torch.int16).cpu().numpy().view(np.uint16)
+    assert np.count_nonzero(got != want) == 0
+    # (2) whole-matrix tolerance against an fp32 matmul of the exactly dequantized operands
+    #     (bf16 output rounding dominates: relative Frobenius error < 3e-3)
+    da = dequant_f32(oracle, pa, sa, M, K, gsa)
+    db = dequant_f32(oracle, pb, sb, N, K, gsb)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    ref = da @ db.t()
+    err = ((D.float() - ref).norm() / ref.norm()).item()
+    assert err < 3e-3, err
+
+
+def dequant_f32(oracle, packed, sf, rows, cols, gs):
+    """fp32 dequantization on the GPU with torch ops: e2m1(code) * (ue4m3(scale) * gs)."""
+    e2m1 = torch.from_numpy(oracle.E2M1_TABLE).cuda()
+    e4m3 = torch.from_numpy(np.nan_to_num(oracle.e4m3_table())).cuda()
+    codes = torch.stack([packed & 0xF, packed >> 4], dim=-1).reshape(rows, cols).long()
+    offs = torch.from_numpy(oracle.sf_offsets(rows, cols)).cuda()
+    bs = e4m3[sf.long()[offs]] * torch.tensor(gs, dtype=torch.float32, device="cuda")
+    return e2m1[codes] * bs.repeat_interleave(16, dim=1)
