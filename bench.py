@@ -54,58 +54,61 @@ REASON_BITS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_pow
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled through NVML (read
+    only) every 5 ms while the timed region runs."""
 
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
-        self.proc = None
-        self.lines = []
+        self.samples = []
+        self.stop_flag = threading.Event()
         self.thread = None
+        self.err = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.idx), "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            entry = vis.split(",")[self.idx].strip() if vis else str(self.idx)
+            if entry.startswith("GPU-") or entry.startswith("MIG-"):
+                self.h = pynvml.nvmlDeviceGetHandleByUUID(entry)
+            else:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(int(entry))
+            self.nvml = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:
+            self.err = str(e)
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread = threading.Thread(target=self._run, daemon=True)
         self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        n = self.nvml
+        while not self.stop_flag.is_set():
+            try:
+                mhz = n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM)
+                try:
+                    bits = n.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                except AttributeError:
+                    bits = n.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+                self.samples.append((mhz, bits))
+            except Exception as e:
+                self.err = str(e)
+            time.sleep(0.005)
 
     def stop(self):
-        if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.15)
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        if self.thread:
-            self.thread.join(timeout=2)
-        sm, mx, reasons = [], None, set()
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 3:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx = float(parts[1])
-                bits = int(parts[2], 16) if parts[2].startswith("0x") else int(parts[2])
-            except ValueError:
-                continue
+        if self.thread is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [f"nvml unavailable: {self.err}"]}
+        self.stop_flag.set()
+        self.thread.join(timeout=2)
+        sm = sorted(s[0] for s in self.samples)
+        reasons = set()
+        for _, bits in self.samples:
             for b, name in REASON_BITS.items():
                 if bits & b and name != "gpu_idle":
                     reasons.add(name)
-        sm.sort()
         med = sm[len(sm) // 2] if sm else None
-        return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons), "samples": len(sm)}
 
 
 # ------------------------------------------------------------ distributed ----
@@ -403,7 +406,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -24,6 +24,7 @@ ACC_EXACT_PER_MMA = 0
 ACC_ROUND_PER_MMA = 1
 ACC_PER_BLOCK = 2
 ACC_EXACT_ALL = 3
+ACC_TCGEN05 = 4   # measured tcgen05 block-scaled MMA arithmetic (the hardware model)
 
 _lib = None
 
