@@ -403,6 +403,28 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_only(args):
+    """One workload alone (used under ncu): warmup + steps launches, timings printed."""
+    import torch
+    import tensorcore_ptx_example_b200 as nv
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    if args.only == "quantize":
+        out = quantize_bench(nv, args.steps, args.warmup, flush)
+    else:
+        pa, sa, pb, sb, alpha, d = gemm_setup(nv, 0)
+        fn = lambda: nv.gemm(pa, sa, pb, sb, M_, N_, K_, alpha=alpha, out=d)  # noqa: E731
+        for _ in range(args.warmup):
+            fn()
+        ts = timed_steps(fn, args.steps, flush)
+        ms = sum(ts) / len(ts)
+        out = {"workload": "cfg3 GEMM 8192^3", "ms": round(ms, 4),
+               "tflops": round(2.0 * M_ * N_ * K_ / (ms * 1e-3) / 1e12, 1)}
+    torch.cuda.synchronize()
+    out["device_status"] = nv.device_status()
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -410,10 +432,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["gemm", "quantize"], default=None,
+                    help="profiling mode: run one workload (warmup + steps launches) and print its "
+                         "timings; not the benchmark line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.only:
+        run_only(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -41,6 +41,7 @@ SIGNATURES = {
     "nvfp4_gemm_f32": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "nvfp4_diag_e2m1_encode": (_I, [_P, _P, _I64, _P]),
     "nvfp4_diag_e4m3_encode": (_I, [_P, _P, _I64, _P]),
+    "nvfp4_diag_mma_peak": (_I, [_I, _I, _P]),
 }
 
 
@@ -190,3 +191,23 @@ def diag_e4m3_encode(x, stream=None):
     out = torch.empty(x.numel(), dtype=torch.uint8, device=x.device)
     check(lib().nvfp4_diag_e4m3_encode(_ptr(x), _ptr(out), x.numel(), _stream(stream)))
     return out
+
+
+def diag_mma_peak(cta_group: int = 2, iters: int = 4096, repeats: int = 3, stream=None) -> float:
+    """Measured FP4 block-scaled MMA rate in TFLOP/s (best of `repeats` launches)."""
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    if cta_group == 2:
+        sms = 2 * (sms // 2)
+    flops = 2.0 * 128 * 256 * 64 * iters * sms
+    check(lib().nvfp4_diag_mma_peak(cta_group, iters, _stream(s)))     # warm-up
+    best = 0.0
+    for _ in range(repeats):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        check(lib().nvfp4_diag_mma_peak(cta_group, iters, _stream(s)))
+        b.record(s)
+        b.synchronize()
+        best = max(best, flops / (a.elapsed_time(b) * 1e-3) / 1e12)
+    return best

@@ -4,7 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/nvfp4.h"
+#include "nvfp4.h"
 
 namespace nvfp4 {
 

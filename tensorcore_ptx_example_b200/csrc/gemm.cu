@@ -149,6 +149,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_ptr;
+    // Self-check: a 512-column allocation owns all of TMEM and starts at lane 0, column 0.
+    const int ntiles = (tmem == 0u) ? tiles : 0;
+    if (tmem != 0u && threadIdx.x == 0) record_error(DEV_TMEM_BASE);
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer ----
@@ -157,7 +160,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
             uint32_t phase = 0;
             bool ok = true;
             uint32_t pending = 0;   // stages with loads issued but not yet released by the MMA
-            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+            for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
                 const int m_blk = tile % num_m, n_blk = tile / num_m;
                 for (int kb = 0; kb < nkb; kb++) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_PRODUCER)) {
@@ -179,12 +182,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
             }
-            if (!ok) {
-                // Do not leave bulk copies in flight into shared memory that is about to be
-                // released: wait (bounded) for every stage that still has loads outstanding.
-                for (int s = 0; s < STAGES; s++) {
-                    if (!(pending & (1u << s))) continue;
-                    const uint32_t par = (s < stage) ? phase : (phase ^ 1u);
+            for (int s = 0; s < STAGES; s++) {
+                if (!(pending & (1u << s))) continue;
+                const uint32_t par = (s < stage) ? phase : (phase ^ 1u);
+                if (ok) {
+                    // Tail: wait until the MMA released every filled stage, so no completion
+                    // signal of the tensor pipe lands in shared memory after the CTA exits.
+                    if (!mbar_wait(empty_bar(s), par, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_TEARDOWN)) break;
+                } else {
+                    // Do not leave bulk copies in flight into shared memory that is about to be
+                    // released: wait (bounded) for every stage that still has loads outstanding.
                     mbar_wait(full_bar(s), par, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_TEARDOWN);
                 }
             }
@@ -194,7 +201,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         int stage = 0;
         uint32_t phase = 0, acc_phase = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
             if (!mbar_wait(tmem_empty, acc_phase ^ 1u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA)) { ok = false; break; }
             tc_fence_after();
             for (int kb = 0; kb < nkb; kb++) {
@@ -235,7 +242,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         // ------------------------------------------------------------ epilogue ----
         const int quad = warp & 3;
         uint32_t acc_phase = 0;
-        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
             const int m_blk = tile % num_m, n_blk = tile / num_m;
             if (!mbar_wait(tmem_full, acc_phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_EPILOGUE)) break;
             tc_fence_after();
@@ -343,20 +350,3 @@ static nvfp4_status_t launch(const void* A, const void* sfa, const void* B, cons
 }  // namespace gemm
 }  // namespace nvfp4
 
-using namespace nvfp4;
-
-extern "C" {
-
-nvfp4_status_t nvfp4_gemm_bf16(const void* A, const void* sfa, const void* B, const void* sfb, float alpha, void* D,
-                               int64_t M, int64_t N, int64_t K, void* stream) {
-    clear_error();
-    return gemm::launch<false>(A, sfa, B, sfb, alpha, D, M, N, K, (cudaStream_t)stream);
-}
-
-nvfp4_status_t nvfp4_gemm_f32(const void* A, const void* sfa, const void* B, const void* sfb, float* D, int64_t M,
-                              int64_t N, int64_t K, void* stream) {
-    clear_error();
-    return gemm::launch<true>(A, sfa, B, sfb, 1.0f, D, M, N, K, (cudaStream_t)stream);
-}
-
-}  // extern "C"

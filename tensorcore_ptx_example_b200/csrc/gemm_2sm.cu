@@ -1,0 +1,410 @@
+// gemm_2sm.cu -- NVFP4 block-scaled GEMM on CTA pairs (tcgen05 cta_group::2), sm_100a.
+//
+// Pair tile 256 x 256 (each CTA owns 128 rows of A / D), K step 64, 256 K per stage.
+//   Operand feed per CTA and stage (38 KB): its own 128 rows of A (16 KB), its own half of B
+//   (128 rows, 16 KB), the scale atoms of its A rows (2 KB) and of all 256 B rows (4 KB).  The
+//   pair MMA reads both B halves, so each SM moves 38 KB per 128x256x256 block instead of the
+//   54 KB of a single-CTA 128x256 tile.  Every TMA load carries .cta_group::2 and completes on
+//   the leader CTA's "full" barrier; no load uses multicast.
+//   The leader's MMA warp copies the scale atoms smem -> TMEM (tcgen05.cp.cta_group::2, each
+//   CTA from its own shared memory into its own TMEM), issues four
+//   tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X (M256 N256 K64) per stage
+//   and signals the "empty" barrier of both CTAs with one tcgen05.commit carrying a CTA mask.
+//   Before exiting, every CTA waits until all of its stages have been released and the leader
+//   waits for the epilogues' last arrival, so no completion signal targets an exited CTA.
+//
+// TMEM (512 columns per CTA): accumulator buffer 0 = columns [0, 256), buffer 1 = [192, 448)
+// (the two overlap in [192, 256)); scale factors in [448, 512).  Tiles alternate buffers.  The
+// epilogue drains the overlapping 64 columns of a tile first and then signals the leader, so
+// the next tile's MMAs start after one quarter of the drain instead of all of it.
+//
+// Epilogue (warps 2..5 of both CTAs): tcgen05.ld 32x32b -> alpha * acc -> bf16 -> swizzled
+// shared-memory staging (2 x 16 KB) -> 2D TMA store, double buffered.
+#include "capi_internal.h"
+#include "nvfp4_common.cuh"
+#include "tma_host.h"
+
+namespace nvfp4 {
+namespace gemm2 {
+
+using gemm::desc_sf;
+using gemm::desc_sw128;
+using gemm::tc_ld32;
+using gemm::tc_wait_ld;
+
+constexpr int BM = 128;                               // rows of A per CTA (pair: 256)
+constexpr int BN = 256;                               // columns of D per pair tile
+constexpr int BK = 256;                               // K per stage
+constexpr int STAGES = 5;
+constexpr int A_BYTES = BM * BK / 2;                  // 16 KB
+constexpr int B_BYTES = (BN / 2) * BK / 2;            // 16 KB
+constexpr int SFA_BYTES = 4 * 512;                    // 2 KB
+constexpr int SFB_BYTES = 2 * 4 * 512;                // 4 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+constexpr int EPI_BYTES = 128 * 128;                  // one staging buffer: 128 rows x 128 bytes
+constexpr int NUM_THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int ACC1_COL = 192;
+constexpr int TMEM_SFA = 448;
+constexpr int TMEM_SFB = 464;
+
+constexpr int OFF_A = 0;
+constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
+constexpr int OFF_SFA = OFF_B + STAGES * B_BYTES;
+constexpr int OFF_SFB = OFF_SFA + STAGES * SFA_BYTES;
+constexpr int OFF_EPI = OFF_SFB + STAGES * SFB_BYTES;
+constexpr int OFF_BAR = OFF_EPI + 2 * EPI_BYTES;
+constexpr int NUM_BARS = 2 * STAGES + 3;              // full, empty, tmem_full, tmem_empty, drain
+constexpr int OFF_TMEM_PTR = OFF_BAR + NUM_BARS * 8;
+constexpr int SMEM_BYTES = 1024 + OFF_TMEM_PTR + 16;
+static_assert(OFF_EPI % 1024 == 0, "staging buffers must be 1024-byte aligned");
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
+constexpr uint32_t IDESC = (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Address of the same shared-memory variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 2D TMA load into this CTA's shared memory, completing on a barrier of either CTA of the pair.
+__device__ __forceinline__ void tma_load_pair(uint32_t dst, const void* tmap, int32_t x, int32_t y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(tmap), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap), "r"(src),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void tc_cp_sf2(uint32_t taddr, uint64_t desc) {
+    asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
+}
+__device__ __forceinline__ void tc_mma2(uint32_t d, uint64_t a, uint64_t b, uint32_t sfa, uint32_t sfb,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(IDESC), "r"(accumulate), "r"(sfa), "r"(sfb)
+        : "memory");
+}
+// One arrival on this CTA's mbarrier when this thread's prior tcgen05 operations finish.
+__device__ __forceinline__ void tc_commit2(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// The same arrival on the mbarrier at this shared-memory offset in both CTAs of the pair
+// (CTA mask 0b11).  This is the completion signal of tcgen05, not a data load.
+__device__ __forceinline__ void tc_commit2_pair(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+        "h"((uint16_t)3)
+        : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void spin_ns(uint64_t ns) {
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < ns) {
+    }
+}
+
+template <bool kOutF32>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+             const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
+             const __grid_constant__ CUtensorMap tmap_d, int M, int N, int K, float alpha) {
+    constexpr int CHUNK = kOutF32 ? 32 : 64;          // output columns per 128-byte staging row
+    constexpr int NCHUNK = BN / CHUNK;
+    constexpr int OVL = 64 / CHUNK;                   // chunks inside the overlapping 64 columns
+
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    const uint32_t base = (raw_addr + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (base - raw_addr);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const uint32_t bar0 = base + OFF_BAR;
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+    const uint32_t tmem_full = bar0 + 8u * (2 * STAGES);
+    const uint32_t tmem_empty = tmem_full + 8u;
+    const uint32_t drain_bar = tmem_full + 16u;
+    uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + OFF_TMEM_PTR);
+
+    const int num_m = M / 256, num_n = N / BN, tiles = num_m * num_n;
+    const int nkb = K / BK;
+    const int katoms = K / 64;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmap_a);
+        prefetch_tmap(&tmap_b);
+        prefetch_tmap(&tmap_sfa);
+        prefetch_tmap(&tmap_sfb);
+        prefetch_tmap(&tmap_d);
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        mbar_init(tmem_full, 1);
+        mbar_init(tmem_empty, 8);                      // one elected lane of 4 epilogue warps x 2 CTAs
+        mbar_init(drain_bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_ptr)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+        tc_fence_before();
+    }
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_ptr;
+    // Self-check: a 512-column allocation owns all of TMEM and starts at lane 0, column 0.
+    const int ntiles = (tmem == 0u) ? tiles : 0;
+    if (tmem != 0u && threadIdx.x == 0) record_error(DEV_TMEM_BASE);
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer ----
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            long fills = 0;
+            for (int tile = pair; tile < ntiles && ok; tile += npairs) {
+                const int tm = tile % num_m, tn = tile / num_m;
+                const int a_row = tm * 256 + (int)rank * BM;
+                const int b_row = tn * BN + (int)rank * (BN / 2);
+                const int sfa_atom = (a_row / 128) * katoms;
+                const int sfb_atom0 = (tn * 2) * katoms, sfb_atom1 = (tn * 2 + 1) * katoms;
+                for (int kb = 0; kb < nkb; kb++) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = mapa(full_bar(stage), 0);
+                    if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * STAGE_BYTES);
+                    tma_load_pair(base + OFF_A + stage * A_BYTES, &tmap_a, kb * (BK / 2), a_row, fb);
+                    tma_load_pair(base + OFF_B + stage * B_BYTES, &tmap_b, kb * (BK / 2), b_row, fb);
+                    tma_load_pair(base + OFF_SFA + stage * SFA_BYTES, &tmap_sfa, 0, sfa_atom + kb * 4, fb);
+                    tma_load_pair(base + OFF_SFB + stage * SFB_BYTES, &tmap_sfb, 0, sfb_atom0 + kb * 4, fb);
+                    tma_load_pair(base + OFF_SFB + stage * SFB_BYTES + SFB_BYTES / 2, &tmap_sfb, 0, sfb_atom1 + kb * 4,
+                                  fb);
+                    fills++;
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (ok) {
+                // Tail: wait until the MMA has released every stage this CTA filled, so that no
+                // completion signal of the leader's tensor pipe lands in this CTA's shared
+                // memory after it has exited.
+                for (int s = 0; s < STAGES; s++) {
+                    if (s >= fills) break;
+                    const uint32_t par = (s < stage) ? phase : (phase ^ 1u);
+                    if (!mbar_wait(empty_bar(s), par, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_TEARDOWN)) break;
+                }
+            } else {
+                // After a failed wait, loads may still be landing in this CTA's shared memory and
+                // only the leader can observe their barrier: give them time before teardown.
+                spin_ns(2000000);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------- MMA issuer (leader) ----
+        if (leader) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int iter = 0;
+            for (int tile = pair; tile < ntiles && ok; tile += npairs, iter++) {
+                if (iter > 0 &&
+                    !mbar_wait(tmem_empty, (uint32_t)((iter - 1) & 1), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t dcol = (iter & 1) ? ACC1_COL : 0;
+                for (int kb = 0; kb < nkb; kb++) {
+                    if (!mbar_wait(full_bar(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA)) { ok = false; break; }
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t sa = base + OFF_SFA + stage * SFA_BYTES;
+                        const uint32_t sb = base + OFF_SFB + stage * SFB_BYTES;
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            tc_cp_sf2(tmem + TMEM_SFA + 4 * j, desc_sf(sa + 512 * j));
+                            tc_cp_sf2(tmem + TMEM_SFB + 8 * j, desc_sf(sb + 512 * j));
+                            tc_cp_sf2(tmem + TMEM_SFB + 8 * j + 4, desc_sf(sb + SFB_BYTES / 2 + 512 * j));
+                        }
+                        const uint32_t a0 = base + OFF_A + stage * A_BYTES;
+                        const uint32_t b0 = base + OFF_B + stage * B_BYTES;
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+                            tc_mma2(tmem + dcol, desc_sw128(a0 + 32 * j), desc_sw128(b0 + 32 * j), tmem + TMEM_SFA + 4 * j,
+                                    tmem + TMEM_SFB + 8 * j, (kb | j) != 0);
+                        tc_commit2_pair(empty_bar(stage));
+                    }
+                    __syncwarp();
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                if (lane == 0) tc_commit2_pair(tmem_full);
+                __syncwarp();
+            }
+            if (lane == 0) {
+                tc_commit2(drain_bar);
+                mbar_wait(drain_bar, 0, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_TEARDOWN);
+                // Tail: the epilogues of both CTAs arrive remotely on tmem_empty after draining
+                // the last tile's shared columns; wait for those arrivals so none lands after
+                // this CTA has exited.
+                if (ok && iter > 0)
+                    mbar_wait(tmem_empty, (uint32_t)((iter - 1) & 1), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_TEARDOWN);
+            }
+            __syncwarp();
+        }
+    } else {
+        // -------------------------------------------------------- epilogue ----
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;                     // row within this CTA's 128
+        const uint32_t leader_empty = mapa(tmem_empty, 0);
+        const bool issuer = (warp == 2 && lane == 0);
+        int sbuf = 0;
+        int iter = 0;
+        for (int tile = pair; tile < ntiles; tile += npairs, iter++) {
+            const int tm = tile % num_m, tn = tile / num_m;
+            if (!mbar_wait(tmem_full, (uint32_t)(iter & 1), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_EPILOGUE)) break;
+            tc_fence_after();
+            const uint32_t dcol = (iter & 1) ? ACC1_COL : 0;
+            const int m0 = tm * 256 + (int)rank * BM;
+#pragma unroll 1
+            for (int idx = 0; idx < NCHUNK; idx++) {
+                // buffer 0 drains its last OVL chunks (the shared columns) first
+                const int c = (iter & 1) ? idx : (idx + NCHUNK - OVL) % NCHUNK;
+                uint32_t r[64];
+                const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + dcol + c * CHUNK;
+                tc_ld32(taddr, r);
+                if constexpr (!kOutF32) tc_ld32(taddr + 32, r + 32);
+                tc_wait_ld();
+                if (idx == OVL - 1) {                          // shared columns drained
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_remote(leader_empty);
+                }
+                if (issuer) bulk_wait_read1();
+                epi_bar();
+                uint8_t* srow = smem + OFF_EPI + sbuf * EPI_BYTES + row * 128;
+                if constexpr (kOutF32) {
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        *reinterpret_cast<uint4*>(srow + ((j ^ (row & 7)) << 4)) =
+                            make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        uint32_t o[4];
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const int e = 8 * j + 2 * i;
+                            const __nv_bfloat162 p = __floats2bfloat162_rn(__fmul_rn(__uint_as_float(r[e]), alpha),
+                                                                           __fmul_rn(__uint_as_float(r[e + 1]), alpha));
+                            o[i] = *reinterpret_cast<const uint32_t*>(&p);
+                        }
+                        *reinterpret_cast<uint4*>(srow + ((j ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                    }
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                epi_bar();
+                if (issuer) {
+                    tma_store_2d(&tmap_d, base + OFF_EPI + sbuf * EPI_BYTES, tn * BN + c * CHUNK, m0);
+                    bulk_commit();
+                }
+                sbuf ^= 1;
+            }
+        }
+        if (issuer) bulk_wait_all();
+    }
+
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+}
+
+// ------------------------------------------------------------------ host ----
+template <bool kOutF32>
+nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void* sfb, float alpha, void* D, int64_t M,
+                      int64_t N, int64_t K, cudaStream_t s) {
+    CUtensorMap ta, tb, tsa, tsb, td;
+    nvfp4_status_t st;
+    if ((st = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, M, K / 2, 128, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+    if ((st = make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2, 128, BN / 2,
+                           CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+    // scale buffers as [atoms][128 x u32]; a box of 4 atoms = one stage (256 K) of one 128-row group
+    if ((st = make_tmap_2d(&tsa, sfa, CU_TENSOR_MAP_DATA_TYPE_UINT32, 128, (M / 128) * (K / 64), 512, 128, 4,
+                           CU_TENSOR_MAP_SWIZZLE_NONE)))
+        return st;
+    if ((st = make_tmap_2d(&tsb, sfb, CU_TENSOR_MAP_DATA_TYPE_UINT32, 128, (N / 128) * (K / 64), 512, 128, 4,
+                           CU_TENSOR_MAP_SWIZZLE_NONE)))
+        return st;
+    if (kOutF32) st = make_tmap_2d(&td, D, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M, N * 4, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    else st = make_tmap_2d(&td, D, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, N, M, N * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+
+    static bool attr_set[64] = {};
+    static int max_pairs[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const bool cacheable = dev >= 0 && dev < 64;
+    if (!cacheable || !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemm2_kernel<kOutF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "gemm2: smem attribute: %s", cudaGetErrorString(e));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
+        cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+        cfg.dynamicSmemBytes = SMEM_BYTES;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, gemm2_kernel<kOutF32>, &cfg) != cudaSuccess || clusters <= 0) {
+            cudaGetLastError();
+            clusters = sm_count() / 2;
+        }
+        if (cacheable) {
+            attr_set[dev] = true;
+            max_pairs[dev] = clusters;
+        }
+    }
+    const int pairs_cap = cacheable ? max_pairs[dev] : sm_count() / 2;
+    const int tiles = (int)((M / 256) * (N / BN));
+    const int pairs = tiles < pairs_cap ? tiles : pairs_cap;
+    gemm2_kernel<kOutF32><<<2 * pairs, NUM_THREADS, SMEM_BYTES, s>>>(ta, tb, tsa, tsb, td, (int)M, (int)N, (int)K, alpha);
+    return check_launch("gemm2_kernel");
+}
+
+}  // namespace gemm2
+}  // namespace nvfp4

@@ -3,3 +3,6 @@
 #include "capi.cu"
 #include "quantize.cu"
 #include "gemm.cu"
+#include "gemm_2sm.cu"
+#include "gemm_api.cu"
+#include "diag_mma.cu"

@@ -2,13 +2,14 @@
 //
 // Data movement (HBM-bound; algorithmic bytes per element: read 2, write 0.5 packed +
 // 0.0625 scale = 2.5625 B):
-//   One CTA of 128 threads owns one scale-factor atom: 128 rows x 64 columns.  Thread t
-//   handles row (t % 4) * 32 + t / 4 of the atom, so the 32-bit word of four block scales
-//   it produces sits at word t of the 512-byte atom and the CTA writes the atom with one
-//   fully coalesced 512-byte store.  Each thread reads its 128 contiguous input bytes with
-//   eight 16-byte non-allocating loads and writes its 32 packed bytes with two 16-byte
-//   stores.  CTAs walk atoms in memory order (k-atom fastest) with a grid-stride loop
-//   sized to the SM count.
+//   The unit of work is one scale-factor atom: 128 rows x 64 columns.  A persistent CTA
+//   (two per SM) streams its atoms' bf16 tiles (128 rows x 128 bytes) into a 6-stage shared
+//   memory ring with one 2D TMA load each (SWIZZLE_128B, so the per-row reads below are bank
+//   conflict free); a producer warp issues the loads, four consumer warps quantize.
+//   Consumer thread t handles row (t % 4) * 32 + t / 4 of the atom, so the 32-bit word of
+//   four block scales it produces sits at word t of the 512-byte atom and the warps write
+//   the atom with fully coalesced stores; each thread writes its 32 packed bytes with two
+//   16-byte stores.  CTAs walk atoms in memory order (k-atom fastest).
 //
 // Arithmetic (per 16-element block; bit-exact against oracle/nvfp4_oracle.c orc_q16):
 //   amax -> s = (amax / 6) * gs_inv -> e4m3(s) -> inv = gs_inv / e4m3(s) -> e2m1(v * inv).
@@ -16,17 +17,69 @@
 //   writes a linear scale layout instead of the tcgen05 one).
 #include "capi_internal.h"
 #include "nvfp4_common.cuh"
+#include "tma_host.h"
 
 namespace nvfp4 {
 
-constexpr int QTHREADS = 128;
+constexpr int QTHREADS = 128;                 // dequantizer CTA
+constexpr int QT_STAGES = 6;                  // quantizer ring depth
+constexpr int QT_TILE = 128 * 128;            // 128 rows x 64 bf16
+constexpr int QT_THREADS = 160;               // warps 0-3 consume, warp 4 loads
+constexpr int QT_SMEM = 1024 + QT_STAGES * QT_TILE + 2 * QT_STAGES * 8;
+constexpr uint64_t QT_WAIT_NS = 2000000000ull;
 
 // Scale word for one (row, 64-column group): four block scales, kblock j in byte j.
 template <bool kDevScale>
-__global__ void __launch_bounds__(QTHREADS)
-quantize_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t cols, float gs_host,
+__global__ void __launch_bounds__(QT_THREADS)
+quantize_kernel(const __grid_constant__ CUtensorMap tmap_x, int64_t rows, int64_t cols, float gs_host,
                 const uint32_t* __restrict__ amax_word, float* __restrict__ gs_out,
                 uint8_t* __restrict__ packed, uint32_t* __restrict__ sf_words, int64_t units) {
+    extern __shared__ uint8_t qsmem_raw[];
+    const uint32_t raw_addr = smem_u32(qsmem_raw);
+    const uint32_t base = (raw_addr + 1023u) & ~1023u;
+    const uint8_t* tiles = qsmem_raw + (base - raw_addr);
+    const uint32_t bar0 = base + QT_STAGES * QT_TILE;
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (QT_STAGES + s); };
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t katoms = cols / 64;
+
+    if (warp == 4 && lane == 0) {
+        prefetch_tmap(&tmap_x);
+        for (int s = 0; s < QT_STAGES; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 128);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == 4) {
+        // ---------------------------------------------------------------- loads ----
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0, pending = 0;
+            bool ok = true;
+            for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
+                if (!mbar_wait(empty_bar(stage), phase ^ 1u, QT_WAIT_NS, DEV_TIMEOUT_QUANT)) { ok = false; break; }
+                pending &= ~(1u << stage);
+                const int64_t rg = u / katoms, kg = u - rg * katoms;
+                mbar_arrive_expect_tx(full_bar(stage), QT_TILE);
+                tma_load_2d(base + stage * QT_TILE, &tmap_x, (int32_t)(kg * 64), (int32_t)(rg * 128), full_bar(stage));
+                pending |= 1u << stage;
+                if (++stage == QT_STAGES) { stage = 0; phase ^= 1u; }
+            }
+            if (!ok)   // never release shared memory with loads still landing in it
+                for (int s = 0; s < QT_STAGES; s++)
+                    if (pending & (1u << s))
+                        mbar_wait(full_bar(s), s < stage ? phase : (phase ^ 1u), QT_WAIT_NS, DEV_TIMEOUT_QUANT);
+        }
+        __syncwarp();
+        return;
+    }
+
+    // ------------------------------------------------------------------ consumers ----
     float gs = gs_host, gs_inv;
     if constexpr (kDevScale) {
         global_scale_from_amax(__uint_as_float(*amax_word), gs, gs_inv);
@@ -34,19 +87,29 @@ quantize_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t cols,
     } else {
         gs_inv = __fdiv_rn(1.0f, gs);
     }
-    const int64_t katoms = cols / 64;
     const int t = threadIdx.x;
     const int r_in_atom = (t & 3) * 32 + (t >> 2);
+    int stage = 0;
+    uint32_t phase = 0;
 #pragma unroll 1
     for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
+        if (!mbar_wait(full_bar(stage), phase, QT_WAIT_NS, DEV_TIMEOUT_QUANT)) break;
+        // Row r_in_atom of the tile: 16-byte chunk c sits at chunk c ^ (row % 8) (SWIZZLE_128B).
+        const uint8_t* srow = tiles + stage * QT_TILE + r_in_atom * 128;
+        uint4 raw[8];
+#pragma unroll
+        for (int c = 0; c < 8; c++)
+            raw[c] = *reinterpret_cast<const uint4*>(srow + ((c ^ (r_in_atom & 7)) << 4));
+        // The stage is released only after the values read from it have been consumed (a
+        // register dependency): an arrive issued right after the shared-memory loads let the
+        // next TMA write overtake them (measured on B200 as rare corrupted rows).
+        const uint32_t my_stage = stage;
+        if (++stage == QT_STAGES) { stage = 0; phase ^= 1u; }
+
         const int64_t rg = u / katoms, kg = u - rg * katoms;
         const int64_t row = rg * 128 + r_in_atom;
         uint32_t word = 0;
         if (row < rows) {
-            const uint8_t* src = reinterpret_cast<const uint8_t*>(x + row * cols + kg * 64);
-            uint4 raw[8];
-#pragma unroll
-            for (int i = 0; i < 8; i++) raw[i] = ld_nc_v4(src + 16 * i);
             uint32_t nib[8];
 #pragma unroll
             for (int b = 0; b < 4; b++) {
@@ -64,10 +127,12 @@ quantize_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t cols,
                 const uint32_t code = q16(v, gs_inv, nib[2 * b], nib[2 * b + 1]);
                 word |= code << (8 * b);
             }
+            mbar_arrive(empty_bar(my_stage));
             uint8_t* dst = packed + row * (cols / 2) + kg * 32;
             st_v4(dst, make_uint4(nib[0], nib[1], nib[2], nib[3]));
             st_v4(dst + 16, make_uint4(nib[4], nib[5], nib[6], nib[7]));
         }
+        else mbar_arrive(empty_bar(my_stage));
         sf_words[u * 128 + t] = word;
     }
 }
@@ -143,6 +208,32 @@ static int quant_grid(int64_t units) {
     return (int)(units < cap ? units : cap);
 }
 
+// Launch the TMA quantizer (kDevScale: the global scale comes from *amax_word).
+template <bool kDevScale>
+static nvfp4_status_t launch_quantize(const void* x, int64_t rows, int64_t cols, float gs, const uint32_t* amax_word,
+                                      float* gs_out, void* packed, void* sf, cudaStream_t s) {
+    const int64_t units = ((rows + 127) / 128) * (cols / 64);
+    if (units == 0) return NVFP4_OK;
+    CUtensorMap tm;
+    nvfp4_status_t st = make_tmap_2d(&tm, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, cols, rows, cols * 2, 64, 128,
+                                     CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != NVFP4_OK) return st;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(quantize_kernel<kDevScale>, cudaFuncAttributeMaxDynamicSharedMemorySize, QT_SMEM);
+        if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "quantize: smem attribute: %s", cudaGetErrorString(e));
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    const int64_t cap = (int64_t)sm_count() * 2;
+    const int grid = (int)(units < cap ? units : cap);
+    quantize_kernel<kDevScale><<<grid, QT_THREADS, QT_SMEM, s>>>(tm, rows, cols, gs, amax_word, gs_out,
+                                                                reinterpret_cast<uint8_t*>(packed),
+                                                                reinterpret_cast<uint32_t*>(sf), units);
+    return check_launch("quantize_kernel");
+}
+
 static nvfp4_status_t launch_amax(const void* x, int64_t numel, uint32_t* word, cudaStream_t s) {
     cudaError_t e = cudaMemsetAsync(word, 0, sizeof(uint32_t), s);
     if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "amax memset: %s", cudaGetErrorString(e));
@@ -187,12 +278,7 @@ nvfp4_status_t nvfp4_quantize_bf16(const void* x, int64_t rows, int64_t cols, fl
     if (st != NVFP4_OK) return st;
     if (!(global_scale > 0.0f) || !isfinite(global_scale))
         return fail(NVFP4_ERR_INVALID_ARG, "quantize: global_scale must be finite and > 0");
-    const int64_t units = ((rows + 127) / 128) * (cols / 64);
-    if (units == 0) return NVFP4_OK;
-    quantize_kernel<false><<<quant_grid(units), QTHREADS, 0, (cudaStream_t)stream>>>(
-        reinterpret_cast<const __nv_bfloat16*>(x), rows, cols, global_scale, nullptr, nullptr,
-        reinterpret_cast<uint8_t*>(packed), reinterpret_cast<uint32_t*>(sf), units);
-    return check_launch("quantize_kernel");
+    return launch_quantize<false>(x, rows, cols, global_scale, nullptr, nullptr, packed, sf, (cudaStream_t)stream);
 }
 
 size_t nvfp4_quantize_workspace_bytes(void) { return 256; }
@@ -209,12 +295,7 @@ nvfp4_status_t nvfp4_quantize_bf16_auto(const void* x, int64_t rows, int64_t col
     uint32_t* word = reinterpret_cast<uint32_t*>(workspace);
     st = launch_amax(x, rows * cols, word, s);
     if (st != NVFP4_OK) return st;
-    const int64_t units = ((rows + 127) / 128) * (cols / 64);
-    if (units == 0) return NVFP4_OK;
-    quantize_kernel<true><<<quant_grid(units), QTHREADS, 0, s>>>(
-        reinterpret_cast<const __nv_bfloat16*>(x), rows, cols, 1.0f, word, global_scale_dev,
-        reinterpret_cast<uint8_t*>(packed), reinterpret_cast<uint32_t*>(sf), units);
-    return check_launch("quantize_kernel<auto>");
+    return launch_quantize<true>(x, rows, cols, 1.0f, word, global_scale_dev, packed, sf, s);
 }
 
 nvfp4_status_t nvfp4_dequantize_bf16(const void* packed, const void* sf, int64_t rows, int64_t cols,
