@@ -129,10 +129,11 @@ NVFP4_API nvfp4_status_t nvfp4_gemm_f32(const void* A, const void* sfa, const vo
 NVFP4_API nvfp4_status_t nvfp4_diag_e2m1_encode(const float* x, uint8_t* out, int64_t n, void* stream);
 NVFP4_API nvfp4_status_t nvfp4_diag_e4m3_encode(const float* x, uint8_t* out, int64_t n, void* stream);
 /* FP4 tensor-core issue-rate microbenchmark: every SM (cta_group 1, M128 N256) or SM pair
- * (cta_group 2, M256 N256) issues `iters` K64 block-scaled MMAs from resident shared memory.
+ * (cta_group 2, M256 N256) issues `iters` K64 block-scaled MMAs from resident shared memory,
+ * on sparse constant operands or (random_operands != 0) pseudo-random E2M1 codes.
  * FLOPs = 2 * 128 * 256 * 64 * iters * (number of SMs); time it with events around the call.
  * The measured rate is the roofline denominator of nvfp4_gemm_bf16. */
-NVFP4_API nvfp4_status_t nvfp4_diag_mma_peak(int cta_group, int iters, void* stream);
+NVFP4_API nvfp4_status_t nvfp4_diag_mma_peak(int cta_group, int iters, int random_operands, void* stream);
 
 #ifdef __cplusplus
 }

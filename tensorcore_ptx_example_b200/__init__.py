@@ -41,7 +41,7 @@ SIGNATURES = {
     "nvfp4_gemm_f32": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "nvfp4_diag_e2m1_encode": (_I, [_P, _P, _I64, _P]),
     "nvfp4_diag_e4m3_encode": (_I, [_P, _P, _I64, _P]),
-    "nvfp4_diag_mma_peak": (_I, [_I, _I, _P]),
+    "nvfp4_diag_mma_peak": (_I, [_I, _I, _I, _P]),
 }
 
 
@@ -193,7 +193,8 @@ def diag_e4m3_encode(x, stream=None):
     return out
 
 
-def diag_mma_peak(cta_group: int = 2, iters: int = 4096, repeats: int = 3, stream=None) -> float:
+def diag_mma_peak(cta_group: int = 2, iters: int = 4096, repeats: int = 3, random_operands: bool = True,
+                  stream=None) -> float:
     """Measured FP4 block-scaled MMA rate in TFLOP/s (best of `repeats` launches)."""
     import torch
     s = stream if stream is not None else torch.cuda.current_stream()
@@ -201,12 +202,13 @@ def diag_mma_peak(cta_group: int = 2, iters: int = 4096, repeats: int = 3, strea
     if cta_group == 2:
         sms = 2 * (sms // 2)
     flops = 2.0 * 128 * 256 * 64 * iters * sms
-    check(lib().nvfp4_diag_mma_peak(cta_group, iters, _stream(s)))     # warm-up
+    ro = 1 if random_operands else 0
+    check(lib().nvfp4_diag_mma_peak(cta_group, iters, ro, _stream(s)))     # warm-up
     best = 0.0
     for _ in range(repeats):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(s)
-        check(lib().nvfp4_diag_mma_peak(cta_group, iters, _stream(s)))
+        check(lib().nvfp4_diag_mma_peak(cta_group, iters, ro, _stream(s)))
         b.record(s)
         b.synchronize()
         best = max(best, flops / (a.elapsed_time(b) * 1e-3) / 1e12)

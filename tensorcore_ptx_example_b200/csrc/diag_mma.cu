@@ -23,15 +23,22 @@ constexpr int PEAK_SMEM = 128 * 1024;
 static_assert(PEAK_SMEM >= PEAK_SMEM_USED, "peak kernel buffer");
 
 template <int kCtaGroup>
-__global__ void __launch_bounds__(128, 1) mma_peak_kernel(int iters) {
+__global__ void __launch_bounds__(128, 1) mma_peak_kernel(int iters, int random_operands) {
     extern __shared__ uint8_t peak_raw[];
     __shared__ __align__(8) uint64_t bars[2];
     __shared__ uint32_t tmem_slot;
     const uint32_t raw_addr = smem_u32(peak_raw);
     uint8_t* ops = peak_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int i = threadIdx.x; i < (PEAK_A + PEAK_B) / 4; i += blockDim.x)
-        reinterpret_cast<uint32_t*>(ops)[i] = (i % 5 == 0) ? 0x22222222u : 0u;
+    // Operands: sparse constant codes, or (random_operands) every nibble pseudo-random so the
+    // multipliers toggle like they do on real data (power, and with it the clock, depends on it).
+    for (int i = threadIdx.x; i < (PEAK_A + PEAK_B) / 4; i += blockDim.x) {
+        uint32_t h = (uint32_t)i * 0x9E3779B1u + blockIdx.x * 0x85EBCA77u;
+        h ^= h >> 15;
+        h *= 0x2C1B3C6Du;
+        h ^= h >> 13;
+        reinterpret_cast<uint32_t*>(ops)[i] = random_operands ? h : ((i % 5 == 0) ? 0x22222222u : 0u);
+    }
     for (int i = threadIdx.x; i < PEAK_SF / 4; i += blockDim.x)
         reinterpret_cast<uint32_t*>(ops + PEAK_A + PEAK_B)[i] = 0x38383838u;   // scale 1.0
     uint32_t rank = 0;
@@ -125,7 +132,7 @@ using namespace nvfp4;
 
 extern "C" {
 
-nvfp4_status_t nvfp4_diag_mma_peak(int cta_group, int iters, void* stream) {
+nvfp4_status_t nvfp4_diag_mma_peak(int cta_group, int iters, int random_operands, void* stream) {
     clear_error();
     if ((cta_group != 1 && cta_group != 2) || iters < 64)
         return fail(NVFP4_ERR_INVALID_ARG, "diag_mma_peak: cta_group in {1,2}, iters >= 64");
@@ -134,7 +141,7 @@ nvfp4_status_t nvfp4_diag_mma_peak(int cta_group, int iters, void* stream) {
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, diag::PEAK_SMEM);
     if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "diag_mma_peak: %s", cudaGetErrorString(e));
     if (cta_group == 1) {
-        diag::mma_peak_kernel<1><<<sms, 128, diag::PEAK_SMEM, (cudaStream_t)stream>>>(iters);
+        diag::mma_peak_kernel<1><<<sms, 128, diag::PEAK_SMEM, (cudaStream_t)stream>>>(iters, random_operands);
     } else {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
@@ -148,7 +155,7 @@ nvfp4_status_t nvfp4_diag_mma_peak(int cta_group, int iters, void* stream) {
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, diag::mma_peak_kernel<2>, iters);
+        e = cudaLaunchKernelEx(&cfg, diag::mma_peak_kernel<2>, iters, random_operands);
         if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "diag_mma_peak: %s", cudaGetErrorString(e));
     }
     return check_launch("mma_peak_kernel");
