@@ -108,6 +108,16 @@ NVFP4_API nvfp4_status_t nvfp4_quantize_bf16_auto(const void* x, int64_t rows, i
                                         void* sf, float* global_scale_dev, void* workspace,
                                         void* stream);
 
+/* nvfp4_quantize_bf16_auto for callers that cannot allocate device memory (no counterpart
+ * in the reference).  Same arguments and results minus `workspace`: the amax hand-off uses a
+ * fixed 256-byte file-scope device array of this library instead (one per device, held until
+ * the process exits; the scratch it needs does not grow with rows x cols).  It calls no
+ * cudaMalloc / cudaFree.  The first call on a device looks the array's address up with
+ * cudaGetSymbolAddress: make that call before any stream capture.  All calls on a device share
+ * the array and clear it on `stream` before use, so calls that overlap on the GPU race. */
+NVFP4_API nvfp4_status_t nvfp4_quantize_bf16_auto_noalloc(const void* x, int64_t rows, int64_t cols, void* packed,
+                                                void* sf, float* global_scale_dev, void* stream);
+
 /* Dequantize to bf16: out = bf16(e2m1(code) * (ue4m3(scale) * gs)). */
 NVFP4_API nvfp4_status_t nvfp4_dequantize_bf16(const void* packed, const void* sf, int64_t rows, int64_t cols,
                                      float global_scale, void* out, void* stream);

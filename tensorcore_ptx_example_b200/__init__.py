@@ -36,6 +36,7 @@ SIGNATURES = {
     "nvfp4_quantize_bf16": (_I, [_P, _I64, _I64, _F, _P, _P, _P]),
     "nvfp4_quantize_workspace_bytes": (ctypes.c_size_t, []),
     "nvfp4_quantize_bf16_auto": (_I, [_P, _I64, _I64, _P, _P, _P, _P, _P]),
+    "nvfp4_quantize_bf16_auto_noalloc": (_I, [_P, _I64, _I64, _P, _P, _P, _P]),
     "nvfp4_dequantize_bf16": (_I, [_P, _P, _I64, _I64, _F, _P, _P]),
     "nvfp4_gemm_bf16": (_I, [_P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _P]),
     "nvfp4_gemm_f32": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),

@@ -2,6 +2,7 @@
 // status word and of every kernel; no relocatable device code needed).
 #include "capi.cu"
 #include "quantize.cu"
+#include "quantize_noalloc.cu"
 #include "gemm.cu"
 #include "gemm_2sm.cu"
 #include "gemm_api.cu"
