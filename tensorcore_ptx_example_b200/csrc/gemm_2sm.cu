@@ -6,17 +6,24 @@
 //   pair MMA reads both B halves, so each SM moves 38 KB per 128x256x256 block instead of the
 //   54 KB of a single-CTA 128x256 tile.  Every TMA load carries .cta_group::2 and completes on
 //   the leader CTA's "full" barrier; no load uses multicast.
-//   The leader's MMA warp copies the scale atoms smem -> TMEM (tcgen05.cp.cta_group::2, each
-//   CTA from its own shared memory into its own TMEM), issues four
+//   Four scale warps per CTA (one per TMEM lane quadrant) move the scale atoms shared memory ->
+//   registers -> TMEM with tcgen05.st into a ring of TMEM slots, each CTA into its own TMEM.
+//   The leader's MMA warp issues four
 //   tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X (M256 N256 K64) per stage
 //   and signals the "empty" barrier of both CTAs with one tcgen05.commit carrying a CTA mask.
+//   Scales do not go through tcgen05.cp: tcgen05 operations execute in issue order in the
+//   tensor pipe, so a copy waits for every MMA queued before it and drains the pipe (measured
+//   on B200 with copies every 4 MMAs: 3.3 PFLOP/s, against 8.2 with tcgen05.st from other warps).
+//   The A/B loads complete on the leader's "full" barrier; each CTA's scale loads complete on a
+//   barrier of its own CTA, which its scale warps wait on.
 //   Before exiting, every CTA waits until all of its stages have been released and the leader
 //   waits for the epilogues' last arrival, so no completion signal targets an exited CTA.
 //
-// TMEM (512 columns per CTA): accumulator buffer 0 = columns [0, 256), buffer 1 = [192, 448)
-// (the two overlap in [192, 256)); scale factors in [448, 512).  Tiles alternate buffers.  The
-// epilogue drains the overlapping 64 columns of a tile first and then signals the leader, so
-// the next tile's MMAs start after one quarter of the drain instead of all of it.
+// TMEM (512 columns per CTA): accumulator buffer 0 = columns [0, 256), buffer 1 = [128, 384)
+// (the two overlap in [128, 256)); scale-factor ring in [384, 504): five slots of two K steps,
+// 24 columns each (per K step: SFA 4 columns, SFB 8 columns).  Tiles alternate accumulator
+// buffers.  The epilogue drains the overlapping 128 columns of a tile first and then signals the
+// leader, so the next tile's MMAs start after half of the drain instead of all of it.
 //
 // Epilogue (warps 2..5 of both CTAs): tcgen05.ld 32x32b -> alpha * acc -> bf16 -> swizzled
 // shared-memory staging (2 x 16 KB) -> 2D TMA store, double buffered.
@@ -27,7 +34,6 @@
 namespace nvfp4 {
 namespace gemm2 {
 
-using gemm::desc_sf;
 using gemm::desc_sw128;
 using gemm::tc_ld32;
 using gemm::tc_wait_ld;
@@ -42,11 +48,23 @@ constexpr int SFA_BYTES = 4 * 512;                    // 2 KB
 constexpr int SFB_BYTES = 2 * 4 * 512;                // 4 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
 constexpr int EPI_BYTES = 128 * 128;                  // one staging buffer: 128 rows x 128 bytes
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 320;                      // 10 warps: TMA, MMA, 4 epilogue, 4 scale
 constexpr int TMEM_COLS = 512;
-constexpr int ACC1_COL = 192;
-constexpr int TMEM_SFA = 448;
-constexpr int TMEM_SFB = 464;
+#ifndef GEMM2_ACC1_COL
+#define GEMM2_ACC1_COL 128
+#endif
+constexpr int ACC1_COL = GEMM2_ACC1_COL;
+constexpr int OVL_COLS = 256 - ACC1_COL;              // columns shared by the two accumulator buffers
+constexpr int SF_RING_COL = ACC1_COL + 256;
+#ifndef GEMM2_SF_KSTEPS
+#define GEMM2_SF_KSTEPS 4
+#endif
+constexpr int SF_KSTEPS = GEMM2_SF_KSTEPS;            // K steps per scale slot
+constexpr int SF_SLOT_COLS = 12 * SF_KSTEPS;          // per K step: SFA 4 + SFB 8 columns
+constexpr int SF_SLOTS = (TMEM_COLS - SF_RING_COL) / SF_SLOT_COLS;
+constexpr int SF_PER_STAGE = (BK / 64) / SF_KSTEPS;   // slots consumed per stage
+static_assert(SF_RING_COL >= ACC1_COL + 256, "scale ring clear of the accumulators");
+static_assert(SF_RING_COL + SF_SLOT_COLS * SF_SLOTS <= TMEM_COLS, "scale ring fits in TMEM");
 
 constexpr int OFF_A = 0;
 constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
@@ -54,7 +72,8 @@ constexpr int OFF_SFA = OFF_B + STAGES * B_BYTES;
 constexpr int OFF_SFB = OFF_SFA + STAGES * SFA_BYTES;
 constexpr int OFF_EPI = OFF_SFB + STAGES * SFB_BYTES;
 constexpr int OFF_BAR = OFF_EPI + 2 * EPI_BYTES;
-constexpr int NUM_BARS = 2 * STAGES + 3;              // full, empty, tmem_full, tmem_empty, drain
+// full, empty, tmem_full, tmem_empty, drain, sf_full, sf_empty, sf_landed
+constexpr int NUM_BARS = 2 * STAGES + 3 + 2 * SF_SLOTS + STAGES;
 constexpr int OFF_TMEM_PTR = OFF_BAR + NUM_BARS * 8;
 constexpr int SMEM_BYTES = 1024 + OFF_TMEM_PTR + 16;
 static_assert(OFF_EPI % 1024 == 0, "staging buffers must be 1024-byte aligned");
@@ -94,9 +113,6 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-__device__ __forceinline__ void tc_cp_sf2(uint32_t taddr, uint64_t desc) {
-    asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
-}
 __device__ __forceinline__ void tc_mma2(uint32_t d, uint64_t a, uint64_t b, uint32_t sfa, uint32_t sfb,
                                         uint32_t accumulate) {
     asm volatile(
@@ -118,6 +134,21 @@ __device__ __forceinline__ void tc_commit2_pair(uint32_t bar) {
         "h"((uint16_t)3)
         : "memory");
 }
+// Per-warp TMEM stores of this thread's lane: 4 / 8 consecutive 32-bit columns.
+__device__ __forceinline__ void tc_st_x4(uint32_t taddr, uint4 v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_st_x8(uint32_t taddr, uint4 v, uint4 w) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t bar) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t bar) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -127,6 +158,19 @@ __device__ __forceinline__ void spin_ns(uint64_t ns) {
     }
 }
 
+#ifdef GEMM2_PROF
+__device__ unsigned long long g_gemm2_prof[296][16];
+#define PROF_WAIT(slot, expr)                                               \
+    ([&]() {                                                                \
+        const unsigned long long _t0 = clock64();                          \
+        const bool _r = (expr);                                             \
+        if ((slot) != 7) atomicAdd(&g_gemm2_prof[blockIdx.x][slot], clock64() - _t0); \
+        return _r;                                                          \
+    }())
+#else
+#define PROF_WAIT(slot, expr) (expr)
+#endif
+
 template <bool kOutF32>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -134,7 +178,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
              const __grid_constant__ CUtensorMap tmap_d, int M, int N, int K, float alpha) {
     constexpr int CHUNK = kOutF32 ? 32 : 64;          // output columns per 128-byte staging row
     constexpr int NCHUNK = BN / CHUNK;
-    constexpr int OVL = 64 / CHUNK;                   // chunks inside the overlapping 64 columns
+    constexpr int OVL = OVL_COLS / CHUNK;             // chunks inside the overlapping columns
 
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -150,6 +194,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
     const uint32_t tmem_full = bar0 + 8u * (2 * STAGES);
     const uint32_t tmem_empty = tmem_full + 8u;
     const uint32_t drain_bar = tmem_full + 16u;
+    auto sf_full = [&](int k) { return drain_bar + 8u + 8u * k; };
+    auto sf_empty = [&](int k) { return drain_bar + 8u + 8u * (SF_SLOTS + k); };
+    auto sf_landed = [&](int st) { return drain_bar + 8u + 8u * (2 * SF_SLOTS + st); };
     uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + OFF_TMEM_PTR);
 
     const int num_m = M / 256, num_n = N / BN, tiles = num_m * num_n;
@@ -170,6 +217,11 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
         mbar_init(tmem_full, 1);
         mbar_init(tmem_empty, 8);                      // one elected lane of 4 epilogue warps x 2 CTAs
         mbar_init(drain_bar, 1);
+        for (int k = 0; k < SF_SLOTS; k++) {
+            mbar_init(sf_full(k), 8);                 // 4 scale warps x 2 CTAs
+            mbar_init(sf_empty(k), 1);
+        }
+        for (int st = 0; st < STAGES; st++) mbar_init(sf_landed(st), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -201,18 +253,19 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                 const int sfa_atom = (a_row / 128) * katoms;
                 const int sfb_atom0 = (tn * 2) * katoms, sfb_atom1 = (tn * 2 + 1) * katoms;
                 for (int kb = 0; kb < nkb; kb++) {
-                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_PRODUCER)) {
+                    if (!PROF_WAIT(5, mbar_wait(empty_bar(stage), phase ^ 1u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_PRODUCER))) {
                         ok = false;
                         break;
                     }
                     const uint32_t fb = mapa(full_bar(stage), 0);
-                    if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * STAGE_BYTES);
+                    if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * (A_BYTES + B_BYTES));
                     tma_load_pair(base + OFF_A + stage * A_BYTES, &tmap_a, kb * (BK / 2), a_row, fb);
                     tma_load_pair(base + OFF_B + stage * B_BYTES, &tmap_b, kb * (BK / 2), b_row, fb);
-                    tma_load_pair(base + OFF_SFA + stage * SFA_BYTES, &tmap_sfa, 0, sfa_atom + kb * 4, fb);
-                    tma_load_pair(base + OFF_SFB + stage * SFB_BYTES, &tmap_sfb, 0, sfb_atom0 + kb * 4, fb);
-                    tma_load_pair(base + OFF_SFB + stage * SFB_BYTES + SFB_BYTES / 2, &tmap_sfb, 0, sfb_atom1 + kb * 4,
-                                  fb);
+                    const uint32_t lb = sf_landed(stage);
+                    mbar_arrive_expect_tx(lb, SFA_BYTES + SFB_BYTES);
+                    tma_load_2d(base + OFF_SFA + stage * SFA_BYTES, &tmap_sfa, 0, sfa_atom + kb * 4, lb);
+                    tma_load_2d(base + OFF_SFB + stage * SFB_BYTES, &tmap_sfb, 0, sfb_atom0 + kb * 4, lb);
+                    tma_load_2d(base + OFF_SFB + stage * SFB_BYTES + SFB_BYTES / 2, &tmap_sfb, 0, sfb_atom1 + kb * 4, lb);
                     fills++;
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
@@ -239,35 +292,49 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
             uint32_t phase = 0;
             bool ok = true;
             int iter = 0;
+            int sf_slot = 0;
+            uint32_t sf_phase = 0;
             for (int tile = pair; tile < ntiles && ok; tile += npairs, iter++) {
                 if (iter > 0 &&
-                    !mbar_wait(tmem_empty, (uint32_t)((iter - 1) & 1), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA)) {
+                    !PROF_WAIT(lane == 0 ? 2 : 7, mbar_wait(tmem_empty, (uint32_t)((iter - 1) & 1), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t dcol = (iter & 1) ? ACC1_COL : 0;
                 for (int kb = 0; kb < nkb; kb++) {
-                    if (!mbar_wait(full_bar(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA)) { ok = false; break; }
+                    if (!PROF_WAIT(lane == 0 ? 0 : 7, mbar_wait(full_bar(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA))) { ok = false; break; }
                     tc_fence_after();
                     if (lane == 0) {
-                        const uint32_t sa = base + OFF_SFA + stage * SFA_BYTES;
-                        const uint32_t sb = base + OFF_SFB + stage * SFB_BYTES;
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            tc_cp_sf2(tmem + TMEM_SFA + 4 * j, desc_sf(sa + 512 * j));
-                            tc_cp_sf2(tmem + TMEM_SFB + 8 * j, desc_sf(sb + 512 * j));
-                            tc_cp_sf2(tmem + TMEM_SFB + 8 * j + 4, desc_sf(sb + SFB_BYTES / 2 + 512 * j));
-                        }
                         const uint32_t a0 = base + OFF_A + stage * A_BYTES;
                         const uint32_t b0 = base + OFF_B + stage * B_BYTES;
 #pragma unroll
-                        for (int j = 0; j < 4; j++)
-                            tc_mma2(tmem + dcol, desc_sw128(a0 + 32 * j), desc_sw128(b0 + 32 * j), tmem + TMEM_SFA + 4 * j,
-                                    tmem + TMEM_SFB + 8 * j, (kb | j) != 0);
-                        tc_commit2_pair(empty_bar(stage));
+                        for (int h = 0; h < SF_PER_STAGE && ok; h++) {
+                            if (!PROF_WAIT(1, mbar_wait(sf_full(sf_slot), sf_phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA))) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+#ifdef GEMM2_PROF
+                            const unsigned long long t_issue = clock64();
+#endif
+                            const uint32_t scol = tmem + SF_RING_COL + SF_SLOT_COLS * sf_slot;
+#pragma unroll
+                            for (int i = 0; i < SF_KSTEPS; i++) {
+                                const int j = h * SF_KSTEPS + i;
+                                tc_mma2(tmem + dcol, desc_sw128(a0 + 32 * j), desc_sw128(b0 + 32 * j), scol + 12 * i,
+                                        scol + 12 * i + 4, (kb | j) != 0);
+                            }
+                            tc_commit2_pair(sf_empty(sf_slot));
+#ifdef GEMM2_PROF
+                            atomicAdd(&g_gemm2_prof[blockIdx.x][7], clock64() - t_issue);
+#endif
+                            if (++sf_slot == SF_SLOTS) { sf_slot = 0; sf_phase ^= 1u; }
+                        }
+                        if (ok) tc_commit2_pair(empty_bar(stage));
                     }
-                    __syncwarp();
+                    ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+                    if (!ok) break;
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
                 if (!ok) break;
@@ -285,6 +352,100 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
             }
             __syncwarp();
         }
+    } else if (warp >= 6) {
+        // ------------------------------------------------------ scale warps (both CTAs) ----
+        // Warp w writes TMEM lane quadrant w % 4.  Per K step, lane r of the quadrant receives
+        // 16 bytes of each scale atom (row r % 32 of the atom: the four scale words of rows r,
+        // r+32, r+64, r+96), the same data tcgen05.cp 32x128b.warpx4 would place there:
+        // SFA in slot columns +0..3, SFB rows 0-127 in +4..7, rows 128-255 in +8..11.
+        const uint32_t q = (uint32_t)(warp & 3);
+        const uint32_t lane_base = (q * 32u) << 16;
+        int stage = 0;
+        uint32_t phase = 0;
+        int sf_slot = 0;
+        uint32_t sf_phase = 0;
+        int writes = 0;
+        bool ok = true;
+        for (int tile = pair; tile < ntiles && ok; tile += npairs) {
+            for (int kb = 0; kb < nkb && ok; kb++) {
+                // every lane waits (each must observe the phase before reading the atoms); the
+                // outcome is made warp-uniform before the .sync.aligned TMEM stores
+                if (!__all_sync(0xFFFFFFFFu, PROF_WAIT((warp == 6 && lane == 0) ? 3 : 7, mbar_wait(sf_landed(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_SF)))) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* sa = smem + OFF_SFA + stage * SFA_BYTES + lane * 16;
+                const uint8_t* sb = smem + OFF_SFB + stage * SFB_BYTES + lane * 16;
+                for (int h = 0; h < SF_PER_STAGE; h++) {
+                    // the slot is free once the MMAs that read it last have completed
+                    if (!__all_sync(0xFFFFFFFFu,
+                                    PROF_WAIT((warp == 6 && lane == 0) ? 4 : 7, mbar_wait(sf_empty(sf_slot), sf_phase ^ 1u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_SF)))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#ifdef GEMM2_PROF
+                    const unsigned long long p0 = clock64();
+#endif
+                    const uint32_t scol = tmem + lane_base + SF_RING_COL + SF_SLOT_COLS * sf_slot;
+#pragma unroll
+                    for (int i = 0; i < SF_KSTEPS; i++) {
+                        const int j = h * SF_KSTEPS + i;
+                        const uint4 a = *reinterpret_cast<const uint4*>(sa + 512 * j);
+                        const uint4 b0 = *reinterpret_cast<const uint4*>(sb + 512 * j);
+                        const uint4 b1 = *reinterpret_cast<const uint4*>(sb + SFB_BYTES / 2 + 512 * j);
+                        tc_st_x4(scol + 12 * i, a);
+                        tc_st_x8(scol + 12 * i + 4, b0, b1);
+                    }
+#ifdef GEMM2_PROF
+                    const unsigned long long p1 = clock64();
+#endif
+                    tc_wait_st();
+#ifdef GEMM2_PROF
+                    const unsigned long long p2 = clock64();
+#endif
+                    tc_fence_before();
+#ifdef GEMM2_PROF
+                    const unsigned long long p2b = clock64();
+#endif
+                    __syncwarp();
+#ifdef GEMM2_PROF
+                    const unsigned long long p2c = clock64();
+                    if (lane == 0 && warp == 6) {
+                        atomicAdd(&g_gemm2_prof[blockIdx.x][12], p2b - p2);
+                        atomicAdd(&g_gemm2_prof[blockIdx.x][13], p2c - p2b);
+                    }
+#endif
+// The stores are complete (tcgen05.wait::st) and ordered by the tcgen05 fence before this
+                    // arrival; a relaxed arrival is enough to hand the slot over.  A release at
+                    // cluster scope costs ~1300 cycles per arrival here (measured), which the
+                    // scale warps cannot afford once per stage.
+                    if (lane == 0) mbar_arrive_remote_relaxed(mapa(sf_full(sf_slot), 0));
+#ifdef GEMM2_PROF
+                    if (lane == 0 && warp == 6) {
+                        const unsigned long long p3 = clock64();
+                        atomicAdd(&g_gemm2_prof[blockIdx.x][8], p1 - p0);
+                        atomicAdd(&g_gemm2_prof[blockIdx.x][9], p2 - p1);
+                        atomicAdd(&g_gemm2_prof[blockIdx.x][10], p3 - p2c);
+                        atomicAdd(&g_gemm2_prof[blockIdx.x][11], 1ull);
+                    }
+#endif
+                    writes++;
+                    if (++sf_slot == SF_SLOTS) { sf_slot = 0; sf_phase ^= 1u; }
+                }
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+        }
+        // Tail: the leader's MMA warp releases each slot with a commit that arrives on sf_empty in
+        // both CTAs; wait for the release of every slot's last use so that no arrival lands in
+        // this CTA's shared memory after it has exited.
+        if (ok && warp == 6 && lane == 0) {
+            for (int k = 0; k < SF_SLOTS && k < writes; k++)
+                if (!mbar_wait(sf_empty(k), k < sf_slot ? sf_phase : (sf_phase ^ 1u), WAIT_LIMIT_NS,
+                               DEV_TIMEOUT_GEMM_TEARDOWN))
+                    break;
+        }
+        __syncwarp();
     } else {
         // -------------------------------------------------------- epilogue ----
         const int quad = warp & 3;
@@ -295,7 +456,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
         int iter = 0;
         for (int tile = pair; tile < ntiles; tile += npairs, iter++) {
             const int tm = tile % num_m, tn = tile / num_m;
-            if (!mbar_wait(tmem_full, (uint32_t)(iter & 1), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_EPILOGUE)) break;
+            if (!PROF_WAIT((warp == 2 && lane == 0) ? 6 : 7, mbar_wait(tmem_full, (uint32_t)(iter & 1), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_EPILOGUE))) break;
             tc_fence_after();
             const uint32_t dcol = (iter & 1) ? ACC1_COL : 0;
             const int m0 = tm * 256 + (int)rank * BM;
@@ -408,3 +569,14 @@ nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void*
 
 }  // namespace gemm2
 }  // namespace nvfp4
+
+#ifdef GEMM2_PROF
+extern "C" NVFP4_API int nvfp4_diag_gemm2_prof(unsigned long long* out, int clear) {
+    cudaMemcpyFromSymbol(out, nvfp4::gemm2::g_gemm2_prof, sizeof(unsigned long long) * 296 * 16);
+    if (clear) {
+        static unsigned long long zero[296 * 16] = {};
+        cudaMemcpyToSymbol(nvfp4::gemm2::g_gemm2_prof, zero, sizeof(zero));
+    }
+    return (int)cudaGetLastError();
+}
+#endif

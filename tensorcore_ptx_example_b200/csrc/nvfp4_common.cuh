@@ -33,6 +33,7 @@ enum DeviceError : unsigned int {
     DEV_TIMEOUT_GEMM_MMA = 0x102,
     DEV_TIMEOUT_GEMM_EPILOGUE = 0x103,
     DEV_TIMEOUT_GEMM_TEARDOWN = 0x104,
+    DEV_TIMEOUT_GEMM_SF = 0x106,
     DEV_TMEM_BASE = 0x105,
     DEV_TIMEOUT_QUANT = 0x301,
     DEV_TIMEOUT_AR_BARRIER = 0x201,
