@@ -1,27 +1,30 @@
 // gemm_2sm.cu -- NVFP4 block-scaled GEMM on CTA pairs (tcgen05 cta_group::2), sm_100a.
 //
-// Pair tile 256 x 256 (each CTA owns 128 rows of A / D), K step 64, 256 K per stage.
-//   Operand feed per CTA and stage (38 KB): its own 128 rows of A (16 KB), its own half of B
-//   (128 rows, 16 KB), the scale atoms of its A rows (2 KB) and of all 256 B rows (4 KB).  The
-//   pair MMA reads both B halves, so each SM moves 38 KB per 128x256x256 block instead of the
-//   54 KB of a single-CTA 128x256 tile.  Every TMA load carries .cta_group::2 and completes on
-//   the leader CTA's "full" barrier; no load uses multicast.
-//   Four scale warps per CTA (one per TMEM lane quadrant) move the scale atoms shared memory ->
-//   registers -> TMEM with tcgen05.st into a ring of TMEM slots, each CTA into its own TMEM.
-//   The leader's MMA warp issues four
-//   tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X (M256 N256 K64) per stage
-//   and signals the "empty" barrier of both CTAs with one tcgen05.commit carrying a CTA mask.
+// Pair tile 256 x 256 (each CTA owns 128 rows of A / D), K step 64, 256 K per stage, 5 stages.
+//   Operand feed per CTA and stage (38 KB): its own 128 rows of A (16 KB) and its own half of B
+//   (128 rows, 16 KB) by TMA with .cta_group::2, completing on the leader's "full" barrier; the
+//   scale atoms of its A rows (2 KB) and of all 256 B rows (4 KB) by TMA into its own shared
+//   memory, completing on a barrier of its own CTA.  The pair MMA reads both B halves, so each SM
+//   moves 38 KB per 128x256x256 block instead of the 54 KB of a single-CTA 128x256 tile.  No
+//   load uses multicast.
+//   Warp roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer (leader CTA), warps 2-5
+//   epilogue, warps 6-9 scale warps.  The scale warps (one per TMEM lane quadrant, in both
+//   CTAs) move the scale atoms shared memory -> registers -> TMEM with tcgen05.st into a ring of
+//   TMEM slots and hand each slot to the MMA warp through the leader's "sf_full" barrier.  The
+//   MMA warp issues four tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X
+//   (M256 N256 K64) per stage and releases the stage (shared memory and scale slot) in both
+//   CTAs with one tcgen05.commit carrying a CTA mask.
 //   Scales do not go through tcgen05.cp: tcgen05 operations execute in issue order in the
-//   tensor pipe, so a copy waits for every MMA queued before it and drains the pipe (measured
-//   on B200 with copies every 4 MMAs: 3.3 PFLOP/s, against 8.2 with tcgen05.st from other warps).
-//   The A/B loads complete on the leader's "full" barrier; each CTA's scale loads complete on a
-//   barrier of its own CTA, which its scale warps wait on.
+//   tensor pipe, so a copy issued by the MMA thread waits for every MMA queued before it and
+//   drains the pipe, and copies from another thread still occupy the pipe (measured on B200:
+//   3.3 PFLOP/s with 12 copies per stage in the MMA thread, 1.9 from a separate thread, 8.2 with
+//   tcgen05.st from other warps).
 //   Before exiting, every CTA waits until all of its stages have been released and the leader
 //   waits for the epilogues' last arrival, so no completion signal targets an exited CTA.
 //
 // TMEM (512 columns per CTA): accumulator buffer 0 = columns [0, 256), buffer 1 = [128, 384)
-// (the two overlap in [128, 256)); scale-factor ring in [384, 504): five slots of two K steps,
-// 24 columns each (per K step: SFA 4 columns, SFB 8 columns).  Tiles alternate accumulator
+// (the two overlap in [128, 256)); scale-factor ring from column 384: slots of one stage,
+// 48 columns each (per K step: SFA 4 columns, SFB 8 columns).  Tiles alternate accumulator
 // buffers.  The epilogue drains the overlapping 128 columns of a tile first and then signals the
 // leader, so the next tile's MMAs start after half of the drain instead of all of it.
 //
@@ -44,9 +47,9 @@ constexpr int BK = 256;                               // K per stage
 constexpr int STAGES = 5;
 constexpr int A_BYTES = BM * BK / 2;                  // 16 KB
 constexpr int B_BYTES = (BN / 2) * BK / 2;            // 16 KB
-constexpr int SFA_BYTES = 4 * 512;                    // 2 KB
-constexpr int SFB_BYTES = 2 * 4 * 512;                // 4 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+constexpr int SFA_BYTES = 4 * 512;                    // 2 KB: scale atoms of this CTA's 128 A rows
+constexpr int SFB_BYTES = 2 * 4 * 512;                // 4 KB: scale atoms of all 256 B rows
+constexpr int AB_BYTES = A_BYTES + B_BYTES;
 constexpr int EPI_BYTES = 128 * 128;                  // one staging buffer: 128 rows x 128 bytes
 constexpr int NUM_THREADS = 320;                      // 10 warps: TMA, MMA, 4 epilogue, 4 scale
 constexpr int TMEM_COLS = 512;
@@ -56,13 +59,9 @@ constexpr int TMEM_COLS = 512;
 constexpr int ACC1_COL = GEMM2_ACC1_COL;
 constexpr int OVL_COLS = 256 - ACC1_COL;              // columns shared by the two accumulator buffers
 constexpr int SF_RING_COL = ACC1_COL + 256;
-#ifndef GEMM2_SF_KSTEPS
-#define GEMM2_SF_KSTEPS 4
-#endif
-constexpr int SF_KSTEPS = GEMM2_SF_KSTEPS;            // K steps per scale slot
-constexpr int SF_SLOT_COLS = 12 * SF_KSTEPS;          // per K step: SFA 4 + SFB 8 columns
+constexpr int SF_SLOT_COLS = 48;                      // one stage: 4 K steps x (SFA 4 + SFB 8 columns)
 constexpr int SF_SLOTS = (TMEM_COLS - SF_RING_COL) / SF_SLOT_COLS;
-constexpr int SF_PER_STAGE = (BK / 64) / SF_KSTEPS;   // slots consumed per stage
+static_assert(SF_SLOTS >= 2 && SF_SLOTS <= STAGES, "scale ring: at least two slots, no more than the stages");
 static_assert(SF_RING_COL >= ACC1_COL + 256, "scale ring clear of the accumulators");
 static_assert(SF_RING_COL + SF_SLOT_COLS * SF_SLOTS <= TMEM_COLS, "scale ring fits in TMEM");
 
@@ -72,8 +71,8 @@ constexpr int OFF_SFA = OFF_B + STAGES * B_BYTES;
 constexpr int OFF_SFB = OFF_SFA + STAGES * SFA_BYTES;
 constexpr int OFF_EPI = OFF_SFB + STAGES * SFB_BYTES;
 constexpr int OFF_BAR = OFF_EPI + 2 * EPI_BYTES;
-// full, empty, tmem_full, tmem_empty, drain, sf_full, sf_empty, sf_landed
-constexpr int NUM_BARS = 2 * STAGES + 3 + 2 * SF_SLOTS + STAGES;
+// full, empty, tmem_full, tmem_empty, drain, sf_full, sf_landed
+constexpr int NUM_BARS = 2 * STAGES + 3 + SF_SLOTS + STAGES;
 constexpr int OFF_TMEM_PTR = OFF_BAR + NUM_BARS * 8;
 constexpr int SMEM_BYTES = 1024 + OFF_TMEM_PTR + 16;
 static_assert(OFF_EPI % 1024 == 0, "staging buffers must be 1024-byte aligned");
@@ -146,6 +145,9 @@ __device__ __forceinline__ void tc_st_x8(uint32_t taddr, uint4 v, uint4 w) {
                  : "memory");
 }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive_relaxed(uint32_t bar) {
+    asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t bar) {
     asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -195,8 +197,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
     const uint32_t tmem_empty = tmem_full + 8u;
     const uint32_t drain_bar = tmem_full + 16u;
     auto sf_full = [&](int k) { return drain_bar + 8u + 8u * k; };
-    auto sf_empty = [&](int k) { return drain_bar + 8u + 8u * (SF_SLOTS + k); };
-    auto sf_landed = [&](int st) { return drain_bar + 8u + 8u * (2 * SF_SLOTS + st); };
+    auto sf_landed = [&](int st) { return drain_bar + 8u + 8u * (SF_SLOTS + st); };
     uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + OFF_TMEM_PTR);
 
     const int num_m = M / 256, num_n = N / BN, tiles = num_m * num_n;
@@ -217,10 +218,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
         mbar_init(tmem_full, 1);
         mbar_init(tmem_empty, 8);                      // one elected lane of 4 epilogue warps x 2 CTAs
         mbar_init(drain_bar, 1);
-        for (int k = 0; k < SF_SLOTS; k++) {
-            mbar_init(sf_full(k), 8);                 // 4 scale warps x 2 CTAs
-            mbar_init(sf_empty(k), 1);
-        }
+        for (int k = 0; k < SF_SLOTS; k++) mbar_init(sf_full(k), 8);   // 4 scale warps x 2 CTAs
         for (int st = 0; st < STAGES; st++) mbar_init(sf_landed(st), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -258,9 +256,11 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                         break;
                     }
                     const uint32_t fb = mapa(full_bar(stage), 0);
-                    if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * (A_BYTES + B_BYTES));
+                    if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * AB_BYTES);
                     tma_load_pair(base + OFF_A + stage * A_BYTES, &tmap_a, kb * (BK / 2), a_row, fb);
                     tma_load_pair(base + OFF_B + stage * B_BYTES, &tmap_b, kb * (BK / 2), b_row, fb);
+                    // scale atoms: this CTA's 128 A rows and both 128-row halves of B, into its
+                    // own shared memory, completing on its own barrier
                     const uint32_t lb = sf_landed(stage);
                     mbar_arrive_expect_tx(lb, SFA_BYTES + SFB_BYTES);
                     tma_load_2d(base + OFF_SFA + stage * SFA_BYTES, &tmap_sfa, 0, sfa_atom + kb * 4, lb);
@@ -287,7 +287,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
         }
     } else if (warp == 1) {
         // ---------------------------------------------------- MMA issuer (leader) ----
-        if (leader) {
+        if (leader && lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
@@ -296,154 +296,105 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
             uint32_t sf_phase = 0;
             for (int tile = pair; tile < ntiles && ok; tile += npairs, iter++) {
                 if (iter > 0 &&
-                    !PROF_WAIT(lane == 0 ? 2 : 7, mbar_wait(tmem_empty, (uint32_t)((iter - 1) & 1), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA))) {
+                    !PROF_WAIT(2, mbar_wait(tmem_empty, (uint32_t)((iter - 1) & 1), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t dcol = (iter & 1) ? ACC1_COL : 0;
                 for (int kb = 0; kb < nkb; kb++) {
-                    if (!PROF_WAIT(lane == 0 ? 0 : 7, mbar_wait(full_bar(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA))) { ok = false; break; }
-                    tc_fence_after();
-                    if (lane == 0) {
-                        const uint32_t a0 = base + OFF_A + stage * A_BYTES;
-                        const uint32_t b0 = base + OFF_B + stage * B_BYTES;
-#pragma unroll
-                        for (int h = 0; h < SF_PER_STAGE && ok; h++) {
-                            if (!PROF_WAIT(1, mbar_wait(sf_full(sf_slot), sf_phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA))) {
-                                ok = false;
-                                break;
-                            }
-                            tc_fence_after();
-#ifdef GEMM2_PROF
-                            const unsigned long long t_issue = clock64();
-#endif
-                            const uint32_t scol = tmem + SF_RING_COL + SF_SLOT_COLS * sf_slot;
-#pragma unroll
-                            for (int i = 0; i < SF_KSTEPS; i++) {
-                                const int j = h * SF_KSTEPS + i;
-                                tc_mma2(tmem + dcol, desc_sw128(a0 + 32 * j), desc_sw128(b0 + 32 * j), scol + 12 * i,
-                                        scol + 12 * i + 4, (kb | j) != 0);
-                            }
-                            tc_commit2_pair(sf_empty(sf_slot));
-#ifdef GEMM2_PROF
-                            atomicAdd(&g_gemm2_prof[blockIdx.x][7], clock64() - t_issue);
-#endif
-                            if (++sf_slot == SF_SLOTS) { sf_slot = 0; sf_phase ^= 1u; }
-                        }
-                        if (ok) tc_commit2_pair(empty_bar(stage));
+                    if (!PROF_WAIT(0, mbar_wait(full_bar(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA)) ||
+                        !PROF_WAIT(1, mbar_wait(sf_full(sf_slot), sf_phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA))) {
+                        ok = false;
+                        break;
                     }
-                    ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t a0 = base + OFF_A + stage * A_BYTES;
+                    const uint32_t b0 = base + OFF_B + stage * B_BYTES;
+                    const uint32_t scol = tmem + SF_RING_COL + SF_SLOT_COLS * sf_slot;
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        tc_mma2(tmem + dcol, desc_sw128(a0 + 32 * j), desc_sw128(b0 + 32 * j), scol + 12 * j,
+                                scol + 12 * j + 4, (kb | j) != 0);
+                    // releases the stage's shared memory (producer) and its scale slot (scale warps)
+                    tc_commit2_pair(empty_bar(stage));
+                    if (++sf_slot == SF_SLOTS) { sf_slot = 0; sf_phase ^= 1u; }
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
                 if (!ok) break;
-                if (lane == 0) tc_commit2_pair(tmem_full);
-                __syncwarp();
+                tc_commit2_pair(tmem_full);
             }
-            if (lane == 0) {
-                tc_commit2(drain_bar);
-                mbar_wait(drain_bar, 0, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_TEARDOWN);
-                // Tail: the epilogues of both CTAs arrive remotely on tmem_empty after draining
-                // the last tile's shared columns; wait for those arrivals so none lands after
-                // this CTA has exited.
-                if (ok && iter > 0)
-                    mbar_wait(tmem_empty, (uint32_t)((iter - 1) & 1), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_TEARDOWN);
-            }
-            __syncwarp();
+            tc_commit2(drain_bar);
+            mbar_wait(drain_bar, 0, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_TEARDOWN);
+            // Tail: the epilogues of both CTAs arrive remotely on tmem_empty after draining the
+            // last tile's shared columns; wait for those arrivals so none lands after this CTA
+            // has exited.
+            if (ok && iter > 0)
+                mbar_wait(tmem_empty, (uint32_t)((iter - 1) & 1), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_TEARDOWN);
         }
+        __syncwarp();
     } else if (warp >= 6) {
         // ------------------------------------------------------ scale warps (both CTAs) ----
         // Warp w writes TMEM lane quadrant w % 4.  Per K step, lane r of the quadrant receives
         // 16 bytes of each scale atom (row r % 32 of the atom: the four scale words of rows r,
         // r+32, r+64, r+96), the same data tcgen05.cp 32x128b.warpx4 would place there:
         // SFA in slot columns +0..3, SFB rows 0-127 in +4..7, rows 128-255 in +8..11.
+        // One slot holds one stage (4 K steps).  Slot reuse: global stage g writes the slot
+        // that stage g - SF_SLOTS used; the MMA commit that releases that stage's shared memory
+        // (empty_bar) also marks its scale slot free.
         const uint32_t q = (uint32_t)(warp & 3);
         const uint32_t lane_base = (q * 32u) << 16;
         int stage = 0;
         uint32_t phase = 0;
         int sf_slot = 0;
-        uint32_t sf_phase = 0;
-        int writes = 0;
         bool ok = true;
+        long g = 0;
         for (int tile = pair; tile < ntiles && ok; tile += npairs) {
-            for (int kb = 0; kb < nkb && ok; kb++) {
-                // every lane waits (each must observe the phase before reading the atoms); the
-                // outcome is made warp-uniform before the .sync.aligned TMEM stores
-                if (!__all_sync(0xFFFFFFFFu, PROF_WAIT((warp == 6 && lane == 0) ? 3 : 7, mbar_wait(sf_landed(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_SF)))) {
+            for (int kb = 0; kb < nkb; kb++, g++) {
+                // Every lane waits (each must observe the phase before reading the atoms); the
+                // outcome is made warp-uniform before the .sync.aligned TMEM stores.
+                bool w = true;
+                if (g >= SF_SLOTS) {
+                    const long p = g - SF_SLOTS;
+                    w = PROF_WAIT((warp == 6 && lane == 0) ? 4 : 7,
+                                  mbar_wait(empty_bar((int)(p % STAGES)), (uint32_t)((p / STAGES) & 1),
+                                            WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_SF));
+                }
+                w = w && PROF_WAIT((warp == 6 && lane == 0) ? 3 : 7,
+                                   mbar_wait(sf_landed(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_SF));
+                if (!__all_sync(0xFFFFFFFFu, w)) {
                     ok = false;
                     break;
                 }
+                tc_fence_after();
                 const uint8_t* sa = smem + OFF_SFA + stage * SFA_BYTES + lane * 16;
                 const uint8_t* sb = smem + OFF_SFB + stage * SFB_BYTES + lane * 16;
-                for (int h = 0; h < SF_PER_STAGE; h++) {
-                    // the slot is free once the MMAs that read it last have completed
-                    if (!__all_sync(0xFFFFFFFFu,
-                                    PROF_WAIT((warp == 6 && lane == 0) ? 4 : 7, mbar_wait(sf_empty(sf_slot), sf_phase ^ 1u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_SF)))) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-#ifdef GEMM2_PROF
-                    const unsigned long long p0 = clock64();
-#endif
-                    const uint32_t scol = tmem + lane_base + SF_RING_COL + SF_SLOT_COLS * sf_slot;
+                uint4 va[4], vb0[4], vb1[4];
 #pragma unroll
-                    for (int i = 0; i < SF_KSTEPS; i++) {
-                        const int j = h * SF_KSTEPS + i;
-                        const uint4 a = *reinterpret_cast<const uint4*>(sa + 512 * j);
-                        const uint4 b0 = *reinterpret_cast<const uint4*>(sb + 512 * j);
-                        const uint4 b1 = *reinterpret_cast<const uint4*>(sb + SFB_BYTES / 2 + 512 * j);
-                        tc_st_x4(scol + 12 * i, a);
-                        tc_st_x8(scol + 12 * i + 4, b0, b1);
-                    }
-#ifdef GEMM2_PROF
-                    const unsigned long long p1 = clock64();
-#endif
-                    tc_wait_st();
-#ifdef GEMM2_PROF
-                    const unsigned long long p2 = clock64();
-#endif
-                    tc_fence_before();
-#ifdef GEMM2_PROF
-                    const unsigned long long p2b = clock64();
-#endif
-                    __syncwarp();
-#ifdef GEMM2_PROF
-                    const unsigned long long p2c = clock64();
-                    if (lane == 0 && warp == 6) {
-                        atomicAdd(&g_gemm2_prof[blockIdx.x][12], p2b - p2);
-                        atomicAdd(&g_gemm2_prof[blockIdx.x][13], p2c - p2b);
-                    }
-#endif
-// The stores are complete (tcgen05.wait::st) and ordered by the tcgen05 fence before this
-                    // arrival; a relaxed arrival is enough to hand the slot over.  A release at
-                    // cluster scope costs ~1300 cycles per arrival here (measured), which the
-                    // scale warps cannot afford once per stage.
-                    if (lane == 0) mbar_arrive_remote_relaxed(mapa(sf_full(sf_slot), 0));
-#ifdef GEMM2_PROF
-                    if (lane == 0 && warp == 6) {
-                        const unsigned long long p3 = clock64();
-                        atomicAdd(&g_gemm2_prof[blockIdx.x][8], p1 - p0);
-                        atomicAdd(&g_gemm2_prof[blockIdx.x][9], p2 - p1);
-                        atomicAdd(&g_gemm2_prof[blockIdx.x][10], p3 - p2c);
-                        atomicAdd(&g_gemm2_prof[blockIdx.x][11], 1ull);
-                    }
-#endif
-                    writes++;
-                    if (++sf_slot == SF_SLOTS) { sf_slot = 0; sf_phase ^= 1u; }
+                for (int j = 0; j < 4; j++) {
+                    va[j] = *reinterpret_cast<const uint4*>(sa + 512 * j);
+                    vb0[j] = *reinterpret_cast<const uint4*>(sb + 512 * j);
+                    vb1[j] = *reinterpret_cast<const uint4*>(sb + SFB_BYTES / 2 + 512 * j);
                 }
+                const uint32_t scol = tmem + lane_base + SF_RING_COL + SF_SLOT_COLS * sf_slot;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    tc_st_x4(scol + 12 * j, va[j]);
+                    tc_st_x8(scol + 12 * j + 4, vb0[j], vb1[j]);
+                }
+                tc_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                // The stores are complete (tcgen05.wait::st) and ordered by the tcgen05 fence
+                // before this arrival, so a relaxed arrival hands the slot over.  A release at
+                // cluster scope costs ~1300 cycles per arrival here (measured), more than a stage.
+                if (lane == 0) {
+                    if (leader) mbar_arrive_relaxed(sf_full(sf_slot));
+                    else mbar_arrive_remote_relaxed(mapa(sf_full(sf_slot), 0));
+                }
+                if (++sf_slot == SF_SLOTS) sf_slot = 0;
                 if (++stage == STAGES) { stage = 0; phase ^= 1u; }
             }
-        }
-        // Tail: the leader's MMA warp releases each slot with a commit that arrives on sf_empty in
-        // both CTAs; wait for the release of every slot's last use so that no arrival lands in
-        // this CTA's shared memory after it has exited.
-        if (ok && warp == 6 && lane == 0) {
-            for (int k = 0; k < SF_SLOTS && k < writes; k++)
-                if (!mbar_wait(sf_empty(k), k < sf_slot ? sf_phase : (sf_phase ^ 1u), WAIT_LIMIT_NS,
-                               DEV_TIMEOUT_GEMM_TEARDOWN))
-                    break;
         }
         __syncwarp();
     } else {
