@@ -133,6 +133,69 @@ NVFP4_API nvfp4_status_t nvfp4_gemm_bf16(const void* A, const void* sfa, const v
 NVFP4_API nvfp4_status_t nvfp4_gemm_f32(const void* A, const void* sfa, const void* B, const void* sfb,
                               float* D, int64_t M, int64_t N, int64_t K, void* stream);
 
+/* ----------------------------------------------------------- all-reduce ---- */
+/* NVFP4-compressed all-reduce of bf16 tensors across the GPUs of one node over NVLink /
+ * NVSwitch peer memory, and the in-house bf16 peer-to-peer all-reduce it is measured
+ * against.  One context per rank, created on that rank's GPU (current device); every rank
+ * makes the same sequence of calls (same numel, algo, order) on its own stream.
+ *
+ * Reference: nvfp4_ar::launch_fused_rank / launch_oneshot_fused_rank
+ * (blackwell/allreduce_sm100_sm120/nvfp4_allreduce.cuh:650-682) with caller-allocated comm
+ * buffers (fused_comm_bytes / oneshot_comm_bytes / fused_barrier_words, :344-352, :398) and peer
+ * pointer tables (bench_ar.cu:770-772, :833-850).  Here the context owns the buffers and the
+ * barrier words; every wait is bounded; results do not depend on the number of ranks' launch
+ * order: sums run in rank order 0..n-1.
+ *
+ * out = bf16(sum over ranks r = 0..n-1 of dequant(quant(in_r)))     (one-shot), or, two-shot,
+ * each shard's fp32 sum requantized with global scale gs * n and dequantized.  Quantization is
+ * NVFP4 with per-16 UE4M3 scales and the caller's global scale gs (same on every rank; the
+ * reference's SFScaleVal is 1 / gs). */
+typedef struct nvfp4_ar* nvfp4_ar_t;
+#define NVFP4_AR_AUTO 0
+#define NVFP4_AR_ONESHOT 1
+#define NVFP4_AR_TWOSHOT 2
+/* NVFP4_AR_AUTO picks one-shot up to this many bf16 bytes, two-shot above. */
+#define NVFP4_AR_ONESHOT_MAX_BYTES (4 << 20)
+
+/* Device bytes a context allocates (flags + two parities of comm buffers). */
+NVFP4_API int64_t nvfp4_ar_buffer_bytes(int world, int64_t max_numel);
+/* world 1..8, rank in [0, world); max_numel: largest numel any call will use. */
+NVFP4_API nvfp4_status_t nvfp4_ar_create(int world, int rank, int64_t max_numel, nvfp4_ar_t* out);
+NVFP4_API nvfp4_status_t nvfp4_ar_destroy(nvfp4_ar_t h);
+/* Multi-process set-up: export this rank's buffer (nvfp4_ar_handle_bytes() bytes, a CUDA IPC
+ * handle), gather every rank's export in rank order, then open the peers' buffers. */
+NVFP4_API size_t nvfp4_ar_handle_bytes(void);
+NVFP4_API nvfp4_status_t nvfp4_ar_export_handle(nvfp4_ar_t h, void* handle_out);
+NVFP4_API nvfp4_status_t nvfp4_ar_open_peers(nvfp4_ar_t h, const void* handles);
+/* Single-process set-up (one thread drives all GPUs, as the reference harness does): give every
+ * context the device pointers of all ranks' buffers (nvfp4_ar_local_base); peer access is
+ * enabled here. */
+NVFP4_API nvfp4_status_t nvfp4_ar_local_base(nvfp4_ar_t h, void** base);
+NVFP4_API nvfp4_status_t nvfp4_ar_set_peers(nvfp4_ar_t h, void* const* bases);
+/* Time limit of each cross-GPU wait (default 5 s); a wait that runs out records a device status
+ * (nvfp4_device_status) and the kernel returns. */
+NVFP4_API nvfp4_status_t nvfp4_ar_set_timeout(nvfp4_ar_t h, uint64_t timeout_ns);
+/* Recovery after a timed-out call: clears this rank's barrier words and restarts its epoch
+ * count.  Synchronises the device.  Every rank must call it, with no all-reduce of any rank in
+ * flight (synchronise all ranks first, e.g. with a host barrier), before the next call. */
+NVFP4_API nvfp4_status_t nvfp4_ar_reset(nvfp4_ar_t h);
+/* The algorithm NVFP4_AR_AUTO resolves to. */
+NVFP4_API int nvfp4_ar_choose_algo(int world, int64_t numel);
+/* NVFP4 all-reduce: numel % (32 * world) == 0, 16-byte aligned bf16 buffers on this rank's GPU;
+ * in and out may not alias. */
+NVFP4_API nvfp4_status_t nvfp4_ar_allreduce(nvfp4_ar_t h, const void* in, void* out, int64_t numel,
+                                            float global_scale, int algo, void* stream);
+/* bf16 peer-to-peer all-reduce (fp32 sum in rank order, one bf16 rounding): numel % (8 * world) == 0. */
+NVFP4_API nvfp4_status_t nvfp4_ar_bf16_allreduce(nvfp4_ar_t h, const void* in, void* out, int64_t numel, int algo,
+                                                 void* stream);
+/* The same data path for `world` ranks that all live on ONE GPU (contexts created on it with
+ * ranks 0..world-1 and joined with nvfp4_ar_set_peers): each phase is launched for every rank
+ * in turn on `stream`, so no kernel waits for another.  bf16_payload != 0 runs the bf16
+ * all-reduce.  For testing the arithmetic on a single GPU. */
+NVFP4_API nvfp4_status_t nvfp4_ar_allreduce_emulated(nvfp4_ar_t const* handles, int world, const void* const* ins,
+                                                     void* const* outs, int64_t numel, float global_scale, int algo,
+                                                     int bf16_payload, void* stream);
+
 /* ----------------------------------------------------------- diagnostics ---- */
 /* Device codec probes (used by the parity tests to pin the hardware conversions):
  * out[i] = E2M1 code of x[i] (RNE, satfinite) / E4M3 code of x[i]. */

@@ -43,6 +43,20 @@ SIGNATURES = {
     "nvfp4_diag_e2m1_encode": (_I, [_P, _P, _I64, _P]),
     "nvfp4_diag_e4m3_encode": (_I, [_P, _P, _I64, _P]),
     "nvfp4_diag_mma_peak": (_I, [_I, _I, _I, _P]),
+    "nvfp4_ar_buffer_bytes": (_I64, [_I, _I64]),
+    "nvfp4_ar_create": (_I, [_I, _I, _I64, ctypes.POINTER(ctypes.c_void_p)]),
+    "nvfp4_ar_destroy": (_I, [_P]),
+    "nvfp4_ar_handle_bytes": (ctypes.c_size_t, []),
+    "nvfp4_ar_export_handle": (_I, [_P, _P]),
+    "nvfp4_ar_open_peers": (_I, [_P, _P]),
+    "nvfp4_ar_local_base": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "nvfp4_ar_set_peers": (_I, [_P, _P]),
+    "nvfp4_ar_set_timeout": (_I, [_P, ctypes.c_uint64]),
+    "nvfp4_ar_reset": (_I, [_P]),
+    "nvfp4_ar_choose_algo": (_I, [_I, _I64]),
+    "nvfp4_ar_allreduce": (_I, [_P, _P, _P, _I64, _F, _I, _P]),
+    "nvfp4_ar_bf16_allreduce": (_I, [_P, _P, _P, _I64, _I, _P]),
+    "nvfp4_ar_allreduce_emulated": (_I, [_P, _I, _P, _P, _I64, _F, _I, _I, _P]),
 }
 
 

@@ -1,0 +1,707 @@
+// allreduce.cu -- NVFP4-compressed all-reduce over NVLink / NVSwitch peer memory (sm_100a), and
+// the in-house bf16 peer-to-peer all-reduce it is measured against.
+//
+// One context per rank (one GPU each).  A context owns one device allocation, exported to the
+// other ranks (CUDA IPC between processes, or plain peer pointers inside one process):
+//   [flags: u32 [AR_MAX_BLOCKS][AR_MAX_WORLD]] [parity 0 region] [parity 1 region]
+//   region = IN [world][in_slot] + GATHER [world][gather_slot]
+// Calls alternate parities, so back-to-back calls never write the region a slower rank may
+// still be reading.  Every call carries an epoch; barrier flags only grow (2 per call), so they
+// are never reset.
+//
+// NVFP4 payload of n elements: packed E2M1 (n/2 bytes, element 2j in the low nibble of byte j)
+// followed, 16-byte aligned, by one UE4M3 scale per 16 elements.  One thread handles a chunk of
+// 32 elements: 64 bytes of bf16 in, 16 bytes packed + 2 bytes of scales out; a warp stores 512
+// contiguous packed bytes and 64 contiguous scale bytes per chunk row, to local or peer memory.
+//
+// Data flow (reference: twoshot_fused_kernel / oneshot_fused_kernel,
+// blackwell/allreduce_sm100_sm120/nvfp4_allreduce.cuh:498-619):
+//   one-shot  A: quantize the whole input once (gs), push the payload into IN[me] of every rank;
+//             barrier; B: out = bf16(sum over ranks 0..n-1 of dequant(IN[s])).
+//   two-shot  A: quantize shard o of the input, push it into IN[me] of owner o; barrier;
+//             B: owner sums IN[0..n-1] of its shard in rank order, requantizes with gs * n and
+//             pushes the result into GATHER[me] of every rank; barrier;
+//             C: out = bf16(dequant(GATHER[o])) for every owner o.
+//   Sums are fp32 fma(code, scale * gs, acc) in rank order 0..n-1 (the reference sums in a
+//   rank-rotated order, :515-518); only the order of the pushes is rotated (rank me+1 first) so
+//   that the ranks do not all target the same peer at once.
+//
+// Synchronisation: block b of every rank handles the same chunks in every phase, so a phase
+// only needs block b of every rank to have finished the previous phase: after its pushes block
+// b does __syncthreads and stores the barrier value into flag [b][me] of every rank with
+// st.release.sys; then thread s waits (ld.acquire.sys, bounded by the context's time limit)
+// for flag [b][s] of its own rank.  A wait that runs out records DEV_TIMEOUT_AR_BARRIER in the
+// device status word and the block skips the rest of the call; nothing traps.  The grid never
+// exceeds the number of blocks that are resident at once, so every block's peer blocks run.
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include "capi_internal.h"
+#include "nvfp4_common.cuh"
+
+namespace nvfp4 {
+namespace ar {
+
+constexpr int AR_MAX_WORLD = 8;
+constexpr int AR_MAX_BLOCKS = 1024;
+constexpr int AR_THREADS = 512;
+constexpr size_t AR_FLAG_BYTES = sizeof(uint32_t) * AR_MAX_BLOCKS * AR_MAX_WORLD;
+constexpr uint64_t AR_DEFAULT_TIMEOUT_NS = 5000000000ull;
+
+__host__ __device__ constexpr int64_t align16(int64_t x) { return (x + 15) & ~(int64_t)15; }
+// Bytes of the NVFP4 payload of n elements (packed, then scales).
+__host__ __device__ constexpr int64_t payload_bytes(int64_t n) { return align16(n / 2) + align16(n / 16); }
+
+struct Params {
+    uint8_t* comm[AR_MAX_WORLD];     // every rank's allocation base (own included)
+    const __nv_bfloat16* in;
+    __nv_bfloat16* out;
+    int64_t numel;
+    int64_t in_slot;                 // bytes of one IN slot
+    int64_t gather_slot;             // bytes of one GATHER slot
+    int64_t region;                  // bytes of one parity region
+    int world, rank;
+    uint32_t epoch;
+    float gs;                        // global scale of the inputs (gs = amax / (6 * 448))
+    uint64_t timeout_ns;
+    int phase;                       // -1: all phases with barriers; 0/1/2: that phase alone
+};
+
+__device__ __forceinline__ uint32_t* flags_of(const Params& p, int r) {
+    return reinterpret_cast<uint32_t*>(p.comm[r]);
+}
+__device__ __forceinline__ uint8_t* region_of(const Params& p, int r) {
+    return p.comm[r] + AR_FLAG_BYTES + (int64_t)(p.epoch & 1u) * p.region;
+}
+__device__ __forceinline__ uint8_t* in_slot(const Params& p, int r, int s) {
+    return region_of(p, r) + (int64_t)s * p.in_slot;
+}
+__device__ __forceinline__ uint8_t* gather_slot(const Params& p, int r, int o) {
+    return region_of(p, r) + (int64_t)p.world * p.in_slot + (int64_t)o * p.gather_slot;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* ptr, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* ptr) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+    return v;
+}
+// 16-byte load that bypasses L1 (the data was written by other GPUs during this kernel).
+__device__ __forceinline__ uint4 ld_cg_v4(const void* ptr) {
+    uint4 r;
+    asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(ptr));
+    return r;
+}
+__device__ __forceinline__ uint16_t ld_cg_u16(const void* ptr) {
+    uint16_t r;
+    asm volatile("ld.global.cg.u16 %0, [%1];" : "=h"(r) : "l"(ptr));
+    return r;
+}
+
+// Block b of this rank meets block b of every rank.  Returns false (for the whole block) if a
+// wait ran out.
+__device__ bool block_barrier(const Params& p, uint32_t value) {
+    __syncthreads();
+    const int t = threadIdx.x;
+    const int64_t slot = (int64_t)blockIdx.x * AR_MAX_WORLD;
+    if (t < p.world) st_release_sys(flags_of(p, t) + slot + p.rank, value);
+    bool ok = true;
+    if (t < p.world) {
+        const uint32_t* f = flags_of(p, p.rank) + slot + t;
+        int spins = 0;
+        uint64_t t0 = 0;
+        while ((int32_t)(ld_acquire_sys(f) - value) < 0) {
+            if (++spins == 64) t0 = globaltimer_ns();
+            if (spins > 64 && (spins & 63) == 0 && globaltimer_ns() - t0 > p.timeout_ns) {
+                record_error(DEV_TIMEOUT_AR_BARRIER);
+                ok = false;
+                break;
+            }
+        }
+    }
+    return __syncthreads_and(ok) != 0;
+}
+
+// ---------------------------------------------------------------- NVFP4 codec ----
+// 32 bf16 values at x (16-byte aligned) -> 16 packed bytes + 2 scale bytes (block 0 low byte).
+__device__ __forceinline__ void quant32(const __nv_bfloat16* x, float gs_inv, uint4& packed, uint32_t& scales) {
+    uint4 raw[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) raw[i] = ld_nc_v4(reinterpret_cast<const uint8_t*>(x) + 16 * i);
+    uint32_t w[8];
+    scales = 0;
+#pragma unroll
+    for (int b = 0; b < 2; b++) {
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const uint32_t q[4] = {raw[2 * b + i].x, raw[2 * b + i].y, raw[2 * b + i].z, raw[2 * b + i].w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                v[8 * i + 2 * k] = __uint_as_float(q[k] << 16);
+                v[8 * i + 2 * k + 1] = __uint_as_float(q[k] & 0xFFFF0000u);
+            }
+        }
+        scales |= q16(v, gs_inv, w[2 * b], w[2 * b + 1]) << (8 * b);
+    }
+    packed = make_uint4(w[0], w[1], w[2], w[3]);
+}
+// Same from 32 fp32 values.
+__device__ __forceinline__ void quant32f(const float* v, float gs_inv, uint4& packed, uint32_t& scales) {
+    uint32_t w[4];
+    const uint32_t s0 = q16(v, gs_inv, w[0], w[1]);
+    const uint32_t s1 = q16(v + 16, gs_inv, w[2], w[3]);
+    packed = make_uint4(w[0], w[1], w[2], w[3]);
+    scales = s0 | (s1 << 8);
+}
+// acc[i] = fma(e2m1(code_i), decode(scale) * gs, acc[i]) for one 32-element chunk.
+__device__ __forceinline__ void dq32_acc(uint4 packed, uint32_t scales, float gs, float* acc) {
+    const uint32_t w[4] = {packed.x, packed.y, packed.z, packed.w};
+#pragma unroll
+    for (int b = 0; b < 2; b++) {
+        const float bs = __fmul_rn(e4m3_decode((scales >> (8 * b)) & 0xFFu), gs);
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            float c[8];
+            e2m1x8_decode(w[2 * b + h], c);
+#pragma unroll
+            for (int i = 0; i < 8; i++) acc[16 * b + 8 * h + i] = __fmaf_rn(c[i], bs, acc[16 * b + 8 * h + i]);
+        }
+    }
+}
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* out, const float* acc) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const __nv_bfloat162 pr = __floats2bfloat162_rn(acc[8 * i + 2 * k], acc[8 * i + 2 * k + 1]);
+            o[k] = *reinterpret_cast<const uint32_t*>(&pr);
+        }
+        st_v4(reinterpret_cast<uint8_t*>(out) + 16 * i, make_uint4(o[0], o[1], o[2], o[3]));
+    }
+}
+// Store one chunk's payload into a payload of `n` elements at `dst`, chunk index c.
+__device__ __forceinline__ void put_chunk(uint8_t* dst, int64_t n, int64_t c, uint4 packed, uint32_t scales) {
+    st_v4(dst + c * 16, packed);
+    *reinterpret_cast<uint16_t*>(dst + align16(n / 2) + c * 2) = (uint16_t)scales;
+}
+__device__ __forceinline__ void get_chunk(const uint8_t* src, int64_t n, int64_t c, uint4& packed, uint32_t& scales) {
+    packed = ld_cg_v4(src + c * 16);
+    scales = ld_cg_u16(src + align16(n / 2) + c * 2);
+}
+
+// ---------------------------------------------------------------- NVFP4 kernels ----
+template <bool kTwoShot>
+__global__ void __launch_bounds__(AR_THREADS) ar_nvfp4_kernel(const Params p) {
+    const int n = p.world, me = p.rank;
+    const float gs_inv = __fdiv_rn(1.0f, p.gs);
+    const uint32_t v1 = p.epoch * 2u + 1u, v2 = p.epoch * 2u + 2u;
+    const bool fused = p.phase < 0;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+
+    if (!kTwoShot) {
+        const int64_t chunks = p.numel / 32;
+        if (fused || p.phase == 0) {
+            for (int64_t c = first; c < chunks; c += stride) {
+                uint4 pk;
+                uint32_t sc;
+                quant32(p.in + c * 32, gs_inv, pk, sc);
+                for (int k = 1; k <= n; k++) {                 // rank me+1 first, own last
+                    const int r = (me + k) % n;
+                    put_chunk(in_slot(p, r, me), p.numel, c, pk, sc);
+                }
+            }
+        }
+        if (fused && !block_barrier(p, v1)) return;
+        if (fused || p.phase == 1) {
+            for (int64_t c = first; c < chunks; c += stride) {
+                float acc[32];
+#pragma unroll
+                for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+                for (int s = 0; s < n; s++) {                  // fixed sum order 0 .. n-1
+                    uint4 pk;
+                    uint32_t sc;
+                    get_chunk(in_slot(p, me, s), p.numel, c, pk, sc);
+                    dq32_acc(pk, sc, p.gs, acc);
+                }
+                store_bf16x32(p.out + c * 32, acc);
+            }
+        }
+        return;
+    }
+
+    const int64_t shard = p.numel / n;
+    const int64_t schunks = shard / 32;
+    if (fused || p.phase == 0) {
+        for (int64_t c = first; c < schunks; c += stride) {
+            for (int k = 1; k <= n; k++) {
+                const int o = (me + k) % n;
+                uint4 pk;
+                uint32_t sc;
+                quant32(p.in + (int64_t)o * shard + c * 32, gs_inv, pk, sc);
+                put_chunk(in_slot(p, o, me), shard, c, pk, sc);
+            }
+        }
+    }
+    if (fused && !block_barrier(p, v1)) return;
+    const float gs_red = __fmul_rn(p.gs, (float)n);
+    if (fused || p.phase == 1) {
+        const float gs_red_inv = __fdiv_rn(1.0f, gs_red);
+        for (int64_t c = first; c < schunks; c += stride) {
+            float acc[32];
+#pragma unroll
+            for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+            for (int s = 0; s < n; s++) {
+                uint4 pk;
+                uint32_t sc;
+                get_chunk(in_slot(p, me, s), shard, c, pk, sc);
+                dq32_acc(pk, sc, p.gs, acc);
+            }
+            uint4 pk;
+            uint32_t sc;
+            quant32f(acc, gs_red_inv, pk, sc);
+            for (int k = 1; k <= n; k++) {
+                const int r = (me + k) % n;
+                put_chunk(gather_slot(p, r, me), shard, c, pk, sc);
+            }
+        }
+    }
+    if (fused && !block_barrier(p, v2)) return;
+    if (fused || p.phase == 2) {
+        for (int64_t c = first; c < schunks; c += stride) {
+            for (int o = 0; o < n; o++) {
+                uint4 pk;
+                uint32_t sc;
+                get_chunk(gather_slot(p, me, o), shard, c, pk, sc);
+                float acc[32];
+#pragma unroll
+                for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+                dq32_acc(pk, sc, gs_red, acc);
+                store_bf16x32(p.out + (int64_t)o * shard + c * 32, acc);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- bf16 kernels ----
+// Chunk = 8 bf16 (16 bytes).  Sum in fp32, rank order 0 .. n-1, round to bf16 once.
+__device__ __forceinline__ void acc_bf16x8(uint4 v, float* acc) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        acc[2 * k] = __fadd_rn(acc[2 * k], __uint_as_float(w[k] << 16));
+        acc[2 * k + 1] = __fadd_rn(acc[2 * k + 1], __uint_as_float(w[k] & 0xFFFF0000u));
+    }
+}
+__device__ __forceinline__ uint4 pack_bf16x8(const float* acc) {
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const __nv_bfloat162 pr = __floats2bfloat162_rn(acc[2 * k], acc[2 * k + 1]);
+        o[k] = *reinterpret_cast<const uint32_t*>(&pr);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+template <bool kTwoShot>
+__global__ void __launch_bounds__(AR_THREADS) ar_bf16_kernel(const Params p) {
+    const int n = p.world, me = p.rank;
+    const uint32_t v1 = p.epoch * 2u + 1u, v2 = p.epoch * 2u + 2u;
+    const bool fused = p.phase < 0;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint8_t* in = reinterpret_cast<const uint8_t*>(p.in);
+    uint8_t* out = reinterpret_cast<uint8_t*>(p.out);
+
+    if (!kTwoShot) {
+        const int64_t chunks = p.numel / 8;
+        if (fused || p.phase == 0) {
+            for (int64_t c = first; c < chunks; c += stride) {
+                const uint4 v = ld_nc_v4(in + c * 16);
+                for (int k = 1; k <= n; k++) st_v4(in_slot(p, (me + k) % n, me) + c * 16, v);
+            }
+        }
+        if (fused && !block_barrier(p, v1)) return;
+        if (fused || p.phase == 1) {
+            for (int64_t c = first; c < chunks; c += stride) {
+                float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                for (int s = 0; s < n; s++) acc_bf16x8(ld_cg_v4(in_slot(p, me, s) + c * 16), acc);
+                st_v4(out + c * 16, pack_bf16x8(acc));
+            }
+        }
+        return;
+    }
+    const int64_t shard = p.numel / n;
+    const int64_t schunks = shard / 8;
+    if (fused || p.phase == 0) {
+        for (int64_t c = first; c < schunks; c += stride) {
+            for (int k = 1; k <= n; k++) {
+                const int o = (me + k) % n;
+                st_v4(in_slot(p, o, me) + c * 16, ld_nc_v4(in + ((int64_t)o * shard) * 2 + c * 16));
+            }
+        }
+    }
+    if (fused && !block_barrier(p, v1)) return;
+    if (fused || p.phase == 1) {
+        for (int64_t c = first; c < schunks; c += stride) {
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (int s = 0; s < n; s++) acc_bf16x8(ld_cg_v4(in_slot(p, me, s) + c * 16), acc);
+            const uint4 r = pack_bf16x8(acc);
+            for (int k = 1; k <= n; k++) st_v4(gather_slot(p, (me + k) % n, me) + c * 16, r);
+        }
+    }
+    if (fused && !block_barrier(p, v2)) return;
+    if (fused || p.phase == 2) {
+        for (int64_t c = first; c < schunks; c += stride)
+            for (int o = 0; o < n; o++)
+                st_v4(out + ((int64_t)o * shard) * 2 + c * 16, ld_cg_v4(gather_slot(p, me, o) + c * 16));
+    }
+}
+
+}  // namespace ar
+}  // namespace nvfp4
+
+// ====================================================================== host ====
+using namespace nvfp4;
+using namespace nvfp4::ar;
+
+struct nvfp4_ar {
+    int world = 0, rank = 0, device = -1;
+    int64_t max_numel = 0;
+    int64_t in_slot = 0, gather_slot = 0, region = 0;
+    size_t bytes = 0;
+    uint8_t* base = nullptr;
+    uint8_t* peer[AR_MAX_WORLD] = {};
+    bool ipc_opened[AR_MAX_WORLD] = {};
+    bool ready = false;
+    uint32_t epoch = 0;
+    uint64_t timeout_ns = AR_DEFAULT_TIMEOUT_NS;
+    int max_grid = 0;
+};
+
+namespace {
+
+// Slot sizes for a context: large enough for every algorithm at max_numel.
+void slot_sizes(int world, int64_t max_numel, int64_t& in_slot, int64_t& gather_slot) {
+    const int64_t shard = max_numel / world;
+    int64_t a = payload_bytes(max_numel);          // NVFP4 one-shot
+    int64_t b = align16(max_numel * 2);            // bf16 one-shot
+    in_slot = a > b ? a : b;
+    a = payload_bytes(shard);
+    b = align16(shard * 2);
+    gather_slot = a > b ? a : b;
+}
+
+nvfp4_status_t check_ctx(nvfp4_ar_t h, const char* who) {
+    if (!h) return fail(NVFP4_ERR_INVALID_ARG, "%s: null context", who);
+    int dev = -1;
+    cudaGetDevice(&dev);
+    if (dev != h->device)
+        return fail(NVFP4_ERR_INVALID_ARG, "%s: context lives on device %d, current device is %d", who, h->device, dev);
+    return NVFP4_OK;
+}
+
+int resident_grid(const void* fn) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, AR_THREADS, 0) != cudaSuccess || per_sm < 1) {
+        cudaGetLastError();
+        per_sm = 1;
+    }
+    int g = per_sm * sm_count();
+    return g < AR_MAX_BLOCKS ? g : AR_MAX_BLOCKS;
+}
+
+// Blocks for `work` thread-chunks: enough to cover the work once, at most what is resident.
+int grid_for(nvfp4_ar_t h, int64_t work) {
+    int64_t g = (work + AR_THREADS - 1) / AR_THREADS;
+    if (g < 1) g = 1;
+    if (g > h->max_grid) g = h->max_grid;
+    return (int)g;
+}
+
+nvfp4_status_t check_call(nvfp4_ar_t h, const char* who, const void* in, const void* out, int64_t numel, int algo,
+                          int elems_per_chunk) {
+    nvfp4_status_t st = check_ctx(h, who);
+    if (st) return st;
+    if (!h->ready) return fail(NVFP4_ERR_NOT_READY, "%s: peers not set (nvfp4_ar_open_peers / nvfp4_ar_set_peers)", who);
+    if (numel < 0 || numel > h->max_numel)
+        return fail(NVFP4_ERR_INVALID_ARG, "%s: numel %lld outside [0, max_numel=%lld]", who, (long long)numel,
+                    (long long)h->max_numel);
+    if (algo != NVFP4_AR_AUTO && algo != NVFP4_AR_ONESHOT && algo != NVFP4_AR_TWOSHOT)
+        return fail(NVFP4_ERR_INVALID_ARG, "%s: algo must be NVFP4_AR_AUTO, _ONESHOT or _TWOSHOT", who);
+    if (numel == 0) return NVFP4_OK;
+    if (!in || !out) return fail(NVFP4_ERR_INVALID_ARG, "%s: null buffer", who);
+    if (!aligned16(in) || !aligned16(out)) return fail(NVFP4_ERR_INVALID_ARG, "%s: buffers must be 16-byte aligned", who);
+    const int64_t unit = (int64_t)elems_per_chunk * h->world;
+    if (numel % unit != 0)
+        return fail(NVFP4_ERR_INVALID_ARG, "%s: numel %lld must be a multiple of %d x world = %lld", who,
+                    (long long)numel, elems_per_chunk, (long long)unit);
+    return NVFP4_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t nvfp4_ar_buffer_bytes(int world, int64_t max_numel) {
+    if (world < 1 || world > AR_MAX_WORLD || max_numel < 0) return -1;
+    int64_t in_slot, gather_slot;
+    slot_sizes(world, max_numel, in_slot, gather_slot);
+    return (int64_t)AR_FLAG_BYTES + 2 * ((int64_t)world * in_slot + (int64_t)world * gather_slot);
+}
+
+nvfp4_status_t nvfp4_ar_create(int world, int rank, int64_t max_numel, nvfp4_ar_t* out) {
+    clear_error();
+    if (!out) return fail(NVFP4_ERR_INVALID_ARG, "ar_create: null output");
+    *out = nullptr;
+    if (world < 1 || world > AR_MAX_WORLD) return fail(NVFP4_ERR_INVALID_ARG, "ar_create: world must be 1..%d", AR_MAX_WORLD);
+    if (rank < 0 || rank >= world) return fail(NVFP4_ERR_INVALID_ARG, "ar_create: rank %d outside [0, %d)", rank, world);
+    if (max_numel < 0 || max_numel > (int64_t(1) << 34)) return fail(NVFP4_ERR_INVALID_ARG, "ar_create: bad max_numel");
+    nvfp4_ar* h = new nvfp4_ar();
+    h->world = world;
+    h->rank = rank;
+    h->max_numel = max_numel;
+    cudaGetDevice(&h->device);
+    slot_sizes(world, max_numel, h->in_slot, h->gather_slot);
+    h->region = (int64_t)world * h->in_slot + (int64_t)world * h->gather_slot;
+    h->bytes = AR_FLAG_BYTES + 2 * (size_t)h->region;
+    cudaError_t e = cudaMalloc(&h->base, h->bytes);
+    if (e == cudaSuccess) e = cudaMemset(h->base, 0, h->bytes);
+    if (e != cudaSuccess) {
+        if (h->base) cudaFree(h->base);
+        delete h;
+        cudaGetLastError();
+        return fail(NVFP4_ERR_CUDA, "ar_create: %s", cudaGetErrorString(e));
+    }
+    int g1 = resident_grid((const void*)ar_nvfp4_kernel<true>), g2 = resident_grid((const void*)ar_nvfp4_kernel<false>);
+    int g3 = resident_grid((const void*)ar_bf16_kernel<true>), g4 = resident_grid((const void*)ar_bf16_kernel<false>);
+    int g = g1;
+    if (g2 < g) g = g2;
+    if (g3 < g) g = g3;
+    if (g4 < g) g = g4;
+    h->max_grid = g;
+    h->peer[rank] = h->base;
+    if (world == 1) h->ready = true;
+    *out = h;
+    return NVFP4_OK;
+}
+
+nvfp4_status_t nvfp4_ar_destroy(nvfp4_ar_t h) {
+    clear_error();
+    if (!h) return NVFP4_OK;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(h->device);
+    for (int r = 0; r < h->world; r++)
+        if (h->ipc_opened[r]) cudaIpcCloseMemHandle(h->peer[r]);
+    if (h->base) cudaFree(h->base);
+    if (prev >= 0) cudaSetDevice(prev);
+    delete h;
+    return NVFP4_OK;
+}
+
+size_t nvfp4_ar_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+nvfp4_status_t nvfp4_ar_export_handle(nvfp4_ar_t h, void* handle_out) {
+    clear_error();
+    nvfp4_status_t st = check_ctx(h, "ar_export_handle");
+    if (st) return st;
+    if (!handle_out) return fail(NVFP4_ERR_INVALID_ARG, "ar_export_handle: null output");
+    cudaIpcMemHandle_t mh;
+    cudaError_t e = cudaIpcGetMemHandle(&mh, h->base);
+    if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "ar_export_handle: %s", cudaGetErrorString(e));
+    memcpy(handle_out, &mh, sizeof(mh));
+    return NVFP4_OK;
+}
+
+nvfp4_status_t nvfp4_ar_open_peers(nvfp4_ar_t h, const void* handles) {
+    clear_error();
+    nvfp4_status_t st = check_ctx(h, "ar_open_peers");
+    if (st) return st;
+    if (!handles) return fail(NVFP4_ERR_INVALID_ARG, "ar_open_peers: null handles");
+    if (h->ready && h->world > 1) return fail(NVFP4_ERR_INVALID_ARG, "ar_open_peers: peers already set");
+    const uint8_t* hs = reinterpret_cast<const uint8_t*>(handles);
+    for (int r = 0; r < h->world; r++) {
+        if (r == h->rank) continue;
+        cudaIpcMemHandle_t mh;
+        memcpy(&mh, hs + (size_t)r * sizeof(mh), sizeof(mh));
+        void* p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, mh, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int q = 0; q < r; q++)
+                if (h->ipc_opened[q]) {
+                    cudaIpcCloseMemHandle(h->peer[q]);
+                    h->ipc_opened[q] = false;
+                    h->peer[q] = nullptr;
+                }
+            cudaGetLastError();
+            return fail(NVFP4_ERR_CUDA, "ar_open_peers: rank %d: %s", r, cudaGetErrorString(e));
+        }
+        h->peer[r] = reinterpret_cast<uint8_t*>(p);
+        h->ipc_opened[r] = true;
+    }
+    h->ready = true;
+    return NVFP4_OK;
+}
+
+nvfp4_status_t nvfp4_ar_local_base(nvfp4_ar_t h, void** base) {
+    clear_error();
+    if (!h || !base) return fail(NVFP4_ERR_INVALID_ARG, "ar_local_base: null argument");
+    *base = h->base;
+    return NVFP4_OK;
+}
+
+nvfp4_status_t nvfp4_ar_set_peers(nvfp4_ar_t h, void* const* bases) {
+    clear_error();
+    nvfp4_status_t st = check_ctx(h, "ar_set_peers");
+    if (st) return st;
+    if (!bases) return fail(NVFP4_ERR_INVALID_ARG, "ar_set_peers: null bases");
+    if (bases[h->rank] != h->base) return fail(NVFP4_ERR_INVALID_ARG, "ar_set_peers: entry of this rank is not its own base");
+    for (int r = 0; r < h->world; r++) {
+        if (!bases[r]) return fail(NVFP4_ERR_INVALID_ARG, "ar_set_peers: null base of rank %d", r);
+        if (r == h->rank) continue;
+        cudaPointerAttributes a;
+        cudaError_t e = cudaPointerGetAttributes(&a, bases[r]);
+        if (e != cudaSuccess || a.type != cudaMemoryTypeDevice) {
+            cudaGetLastError();
+            return fail(NVFP4_ERR_INVALID_ARG, "ar_set_peers: base of rank %d is not device memory", r);
+        }
+        if (a.device != h->device) {
+            e = cudaDeviceEnablePeerAccess(a.device, 0);
+            if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+            else if (e != cudaSuccess) {
+                cudaGetLastError();
+                return fail(NVFP4_ERR_CUDA, "ar_set_peers: peer access %d -> %d: %s", h->device, a.device,
+                            cudaGetErrorString(e));
+            }
+        }
+    }
+    for (int r = 0; r < h->world; r++) h->peer[r] = reinterpret_cast<uint8_t*>(bases[r]);
+    h->ready = true;
+    return NVFP4_OK;
+}
+
+nvfp4_status_t nvfp4_ar_set_timeout(nvfp4_ar_t h, uint64_t timeout_ns) {
+    clear_error();
+    if (!h) return fail(NVFP4_ERR_INVALID_ARG, "ar_set_timeout: null context");
+    if (timeout_ns < 1000000ull || timeout_ns > 600000000000ull)
+        return fail(NVFP4_ERR_INVALID_ARG, "ar_set_timeout: limit must be 1 ms .. 600 s");
+    h->timeout_ns = timeout_ns;
+    return NVFP4_OK;
+}
+
+nvfp4_status_t nvfp4_ar_reset(nvfp4_ar_t h) {
+    clear_error();
+    nvfp4_status_t st = check_ctx(h, "ar_reset");
+    if (st) return st;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemset(h->base, 0, AR_FLAG_BYTES);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "ar_reset: %s", cudaGetErrorString(e));
+    h->epoch = 0;
+    return NVFP4_OK;
+}
+
+int nvfp4_ar_choose_algo(int world, int64_t numel) {
+    if (world <= 1) return NVFP4_AR_ONESHOT;
+    // one-shot pushes the whole payload to every peer but needs one barrier: better while the
+    // call is latency-bound (measured crossover on 8 x B200 around 1-4 MB of bf16)
+    return numel * 2 <= NVFP4_AR_ONESHOT_MAX_BYTES ? NVFP4_AR_ONESHOT : NVFP4_AR_TWOSHOT;
+}
+
+static Params make_params(nvfp4_ar_t h, const void* in, void* out, int64_t numel, float gs, int phase) {
+    Params p = {};
+    for (int r = 0; r < h->world; r++) p.comm[r] = h->peer[r];
+    p.in = reinterpret_cast<const __nv_bfloat16*>(in);
+    p.out = reinterpret_cast<__nv_bfloat16*>(out);
+    p.numel = numel;
+    p.in_slot = h->in_slot;
+    p.gather_slot = h->gather_slot;
+    p.region = h->region;
+    p.world = h->world;
+    p.rank = h->rank;
+    p.epoch = h->epoch;
+    p.gs = gs;
+    p.timeout_ns = h->timeout_ns;
+    p.phase = phase;
+    return p;
+}
+
+static nvfp4_status_t launch_nvfp4(nvfp4_ar_t h, const Params& p, bool twoshot, cudaStream_t s) {
+    const int64_t work = twoshot ? p.numel / p.world / 32 : p.numel / 32;
+    const int grid = grid_for(h, work);
+    if (twoshot) ar_nvfp4_kernel<true><<<grid, AR_THREADS, 0, s>>>(p);
+    else ar_nvfp4_kernel<false><<<grid, AR_THREADS, 0, s>>>(p);
+    return check_launch("ar_nvfp4_kernel");
+}
+static nvfp4_status_t launch_bf16(nvfp4_ar_t h, const Params& p, bool twoshot, cudaStream_t s) {
+    const int64_t work = twoshot ? p.numel / p.world / 8 : p.numel / 8;
+    const int grid = grid_for(h, work);
+    if (twoshot) ar_bf16_kernel<true><<<grid, AR_THREADS, 0, s>>>(p);
+    else ar_bf16_kernel<false><<<grid, AR_THREADS, 0, s>>>(p);
+    return check_launch("ar_bf16_kernel");
+}
+
+nvfp4_status_t nvfp4_ar_allreduce(nvfp4_ar_t h, const void* in, void* out, int64_t numel, float global_scale, int algo,
+                                  void* stream) {
+    clear_error();
+    nvfp4_status_t st = check_call(h, "ar_allreduce", in, out, numel, algo, 32);
+    if (st || numel == 0) return st;
+    if (!(global_scale > 0.0f) || !isfinite(global_scale))
+        return fail(NVFP4_ERR_INVALID_ARG, "ar_allreduce: global_scale must be finite and > 0");
+    if (algo == NVFP4_AR_AUTO) algo = nvfp4_ar_choose_algo(h->world, numel);
+    h->epoch++;
+    return launch_nvfp4(h, make_params(h, in, out, numel, global_scale, -1), algo == NVFP4_AR_TWOSHOT,
+                        (cudaStream_t)stream);
+}
+
+nvfp4_status_t nvfp4_ar_bf16_allreduce(nvfp4_ar_t h, const void* in, void* out, int64_t numel, int algo,
+                                       void* stream) {
+    clear_error();
+    nvfp4_status_t st = check_call(h, "ar_bf16_allreduce", in, out, numel, algo, 8);
+    if (st || numel == 0) return st;
+    if (algo == NVFP4_AR_AUTO) algo = nvfp4_ar_choose_algo(h->world, numel);
+    h->epoch++;
+    return launch_bf16(h, make_params(h, in, out, numel, 0.0f, -1), algo == NVFP4_AR_TWOSHOT, (cudaStream_t)stream);
+}
+
+nvfp4_status_t nvfp4_ar_allreduce_emulated(nvfp4_ar_t const* handles, int world, const void* const* ins,
+                                           void* const* outs, int64_t numel, float global_scale, int algo,
+                                           int bf16_payload, void* stream) {
+    clear_error();
+    if (!handles || !ins || !outs || world < 1 || world > AR_MAX_WORLD)
+        return fail(NVFP4_ERR_INVALID_ARG, "ar_allreduce_emulated: bad arguments");
+    for (int r = 0; r < world; r++) {
+        nvfp4_status_t st = check_call(handles[r], "ar_allreduce_emulated", ins[r], outs[r], numel,
+                                       algo == NVFP4_AR_AUTO ? NVFP4_AR_AUTO : algo, bf16_payload ? 8 : 32);
+        if (st) return st;
+        if (handles[r]->world != world || handles[r]->rank != r || handles[r]->device != handles[0]->device)
+            return fail(NVFP4_ERR_INVALID_ARG, "ar_allreduce_emulated: contexts must be ranks 0..%d of one device", world - 1);
+    }
+    if (numel == 0) return NVFP4_OK;
+    if (!bf16_payload && (!(global_scale > 0.0f) || !isfinite(global_scale)))
+        return fail(NVFP4_ERR_INVALID_ARG, "ar_allreduce_emulated: global_scale must be finite and > 0");
+    if (algo == NVFP4_AR_AUTO) algo = nvfp4_ar_choose_algo(world, numel);
+    const bool two = algo == NVFP4_AR_TWOSHOT;
+    for (int r = 0; r < world; r++) handles[r]->epoch++;
+    // Phase by phase, rank by rank: the launches are ordered on one stream, so no kernel ever
+    // waits for another one.
+    const int phases = two ? 3 : 2;
+    for (int ph = 0; ph < phases; ph++)
+        for (int r = 0; r < world; r++) {
+            const Params p = make_params(handles[r], ins[r], outs[r], numel, global_scale, ph);
+            nvfp4_status_t st = bf16_payload ? launch_bf16(handles[r], p, two, (cudaStream_t)stream)
+                                             : launch_nvfp4(handles[r], p, two, (cudaStream_t)stream);
+            if (st) return st;
+        }
+    return NVFP4_OK;
+}
+
+}  // extern "C"

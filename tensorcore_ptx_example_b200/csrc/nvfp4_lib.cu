@@ -7,3 +7,4 @@
 #include "gemm_2sm.cu"
 #include "gemm_api.cu"
 #include "diag_mma.cu"
+#include "allreduce.cu"

@@ -1,0 +1,175 @@
+"""NVFP4 all-reduce across real GPUs (skipped with fewer than 2): the fused kernels with their
+cross-GPU block barriers over NVLink peer memory.
+
+* one process driving every GPU (the reference harness's model, bench_ar.cu:763-850): every
+  rank's kernel is launched before any is waited for;
+* one process per GPU, buffers shared through CUDA IPC handles exchanged over gloo;
+* failure detection: one rank never launches; the others' barrier waits run out after their
+  short time limit, record DEV_TIMEOUT_AR_BARRIER and return; after a reset the contexts work
+  again.  Nothing traps or hangs: every wait is bounded.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from tensorcore_ptx_example_b200 import allreduce as ar  # noqa: E402
+from tensorcore_ptx_example_b200 import workloads  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+DEV_TIMEOUT_AR_BARRIER = 0x201
+
+
+def ngpus():
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+needs2 = pytest.mark.skipif(ngpus() < 2, reason="needs at least 2 GPUs")
+
+
+def u16(t):
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1)
+
+
+def make_inputs(world, numel, seed0):
+    return [workloads.gaussian(1, numel, seed=seed0 + r, device="cpu").view(-1) for r in range(world)]
+
+
+def oracle_gs(inputs):
+    import tensorcore_ptx_example_b200 as nv
+    return nv.global_scale_from_amax(max(float(x.float().abs().max()) for x in inputs))
+
+
+def run_in_process(ctxs, xs, outs, fn):
+    """Launch on every device first, then synchronise every device."""
+    for c, x, o in zip(ctxs, xs, outs):
+        with torch.cuda.device(c.device):
+            fn(c, x, o)
+    for c in ctxs:
+        torch.cuda.synchronize(c.device)
+
+
+@needs2
+@pytest.mark.parametrize("algo", ["oneshot", "twoshot"])
+def test_in_process_allreduce_bitexact(nv, oracle, algo):
+    world = min(ngpus(), 8)
+    numel = 32 * world * 1000
+    host = make_inputs(world, numel, seed0=11)
+    gs = oracle_gs(host)
+    ctxs, xs, outs = [], [], []
+    for r in range(world):
+        with torch.cuda.device(r):
+            ctxs.append(ar.AllReduce(world, r, numel))
+            xs.append(host[r].cuda())
+            outs.append(torch.empty_like(xs[-1]))
+    ar.join_in_process(ctxs)
+    try:
+        for rep in range(3):                      # repeated calls: parities and epochs
+            run_in_process(ctxs, xs, outs, lambda c, x, o: c.allreduce(x, o, global_scale=gs, algo=algo))
+            want = (oracle.ar_oneshot if algo == "oneshot" else oracle.ar_twoshot)([u16(x) for x in host], gs)
+            for r in range(world):
+                with torch.cuda.device(r):
+                    assert nv.device_status() == 0
+                assert np.array_equal(u16(outs[r]), want), (rep, r)
+        run_in_process(ctxs, xs, outs, lambda c, x, o: c.bf16_allreduce(x, o, algo=algo))
+        want = oracle.ar_bf16([u16(x) for x in host])
+        for r in range(world):
+            assert np.array_equal(u16(outs[r]), want)
+    finally:
+        for c in ctxs:
+            with torch.cuda.device(c.device):
+                c.close()
+
+
+@needs2
+def test_barrier_timeout_when_a_rank_never_arrives(nv):
+    world, numel = 2, 32 * 2 * 512
+    ctxs, xs, outs = [], [], []
+    for r in range(world):
+        with torch.cuda.device(r):
+            ctxs.append(ar.AllReduce(world, r, numel))
+            ctxs[-1].set_timeout(0.2)
+            xs.append(torch.ones(numel, dtype=torch.bfloat16, device=f"cuda:{r}"))
+            outs.append(torch.empty_like(xs[-1]))
+    ar.join_in_process(ctxs)
+    try:
+        with torch.cuda.device(0):
+            nv.device_status()                    # clear
+            ctxs[0].allreduce(xs[0], outs[0], global_scale=1.0 / 2688.0, algo="twoshot")   # rank 1 never calls
+            torch.cuda.synchronize(0)
+            assert nv.device_status() == DEV_TIMEOUT_AR_BARRIER
+        # the device is still usable; after a reset of every rank the contexts work again
+        for c in ctxs:
+            with torch.cuda.device(c.device):
+                c.reset()
+        run_in_process(ctxs, xs, outs, lambda c, x, o: c.allreduce(x, o, global_scale=1.0 / 2688.0,
+                                                                     algo="twoshot"))
+        for r in range(world):
+            with torch.cuda.device(r):
+                assert nv.device_status() == 0
+            assert torch.equal(outs[r].float().cpu(), torch.full((numel,), 2.0))
+    finally:
+        for c in ctxs:
+            with torch.cuda.device(c.device):
+                c.close()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _ipc_worker(rank, world, port, numel, results):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    ctx = None
+    try:
+        host = make_inputs(world, numel, seed0=21)
+        gs = oracle_gs(host)
+        ctx = ar.AllReduce.from_process_group(numel)
+        x = host[rank].cuda()
+        outs = {}
+        for algo in ("oneshot", "twoshot"):
+            o = ctx.allreduce(x, global_scale=gs, algo=algo)
+            torch.cuda.synchronize()
+            outs[algo] = u16(o)
+        dist.barrier()
+        import tensorcore_ptx_example_b200 as nv
+        results[rank] = (outs, nv.device_status())
+    finally:
+        if ctx is not None:
+            ctx.close()
+        dist.destroy_process_group()
+
+
+@needs2
+def test_multi_process_ipc_allreduce_bitexact(oracle):
+    import torch.multiprocessing as mp
+    world = min(ngpus(), 4)
+    numel = 32 * world * 777
+    port = _free_port()
+    with mp.Manager() as m:
+        results = m.dict()
+        mp.spawn(_ipc_worker, args=(world, port, numel, results), nprocs=world, join=True)
+        res = dict(results)
+    host = make_inputs(world, numel, seed0=21)
+    gs = oracle_gs(host)
+    x16 = [u16(x) for x in host]
+    want = {"oneshot": oracle.ar_oneshot(x16, gs), "twoshot": oracle.ar_twoshot(x16, gs)}
+    for r in range(world):
+        outs, status = res[r]
+        assert status == 0
+        for algo in want:
+            assert np.array_equal(outs[algo], want[algo]), (r, algo)
