@@ -120,6 +120,7 @@ def dist_setup(args):
     if world > 1:
         import datetime
         import torch.distributed as dist
+        os.environ.setdefault("NCCL_DEBUG", "WARN")     # keep NCCL's banner off stdout (one JSON line)
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
@@ -304,11 +305,7 @@ def run_ours(args):
         except Exception as e:  # reported, not fatal
             extra["quantize"] = {"error": str(e)}
     if world > 1:
-        try:
-            from tensorcore_ptx_example_b200 import allreduce  # noqa: F401
-            extra["allreduce"] = allreduce_bench(nv, world, rank, args)
-        except ImportError:
-            pass
+        extra["allreduce"] = allreduce_bench(nv, world, rank, args, flush=flush)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -331,7 +328,7 @@ def run_ours(args):
         "config": {"workload": "cfg3 NVFP4 GEMM M=N=K=8192, bf16 out", "M": M_, "N": N_, "K": K_,
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "flushed between timed steps (256 MB write)",
-                   "tile": "1-CTA 128x256, BK=256, 4 stages, persistent"},
+                   "tile": "CTA pair (tcgen05 cta_group::2) 256x256, BK=256, 5 stages, persistent"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(fp4_peak, 1),
                      "unit": "TFLOP/s", "frac": round(achieved / fp4_peak, 4),
                      "peak_source": f"4 x {peak_kind} cuBLAS bf16 burst ({peaks.get('bf16_tflops')}) = dense FP4 rate",
@@ -354,8 +351,130 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def allreduce_bench(nv, world, rank, args):   # replaced when the all-reduce module lands
-    return None
+NVLINK_PEER_GBS = 770.0      # measured peer copy per direction per GPU on this pool (900 nominal)
+
+
+def _ar_time(fn, steps, warmup, flush, world):
+    """Per-call device time (ms) of an all-reduce, max over ranks of the per-rank mean."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    ts = timed_steps(fn, steps, flush)
+    barrier(world)
+    return max_over_ranks(sum(ts) / len(ts), world)
+
+
+def _ar_entry(name, numel, world, ms, payload_bytes_per_elt):
+    """bf16-equivalent algbw / busbw (nccl-tests convention) and wire rate of one algorithm."""
+    t = ms * 1e-3
+    algbw = 2.0 * numel / t / 1e9
+    busbw = algbw * 2.0 * (world - 1) / world
+    two = "twoshot" in name
+    wire = (2.0 * (world - 1) / world if two else (world - 1)) * payload_bytes_per_elt * numel
+    return {"us": round(ms * 1e3, 2), "algbw_gbs": round(algbw, 1), "busbw_gbs": round(busbw, 1),
+            "wire_bytes_per_rank": int(wire), "wire_gbs_per_rank": round(wire / t / 1e9, 1),
+            "frac_of_nvlink_770": round(wire / t / 1e9 / NVLINK_PEER_GBS, 4)}
+
+
+def allreduce_bench(nv, world, rank, args, numel=None, steps=None, flush=None):
+    """cfg4: every rank holds 4096 x 7168 bf16 N(0, 1), seed = rank.  NVFP4 two-shot / one-shot
+    and the in-house bf16 P2P all-reduce, device time per call (max over ranks), L2 flushed
+    between calls; plus the NVFP4 error against the exact sum and an end-to-end number through
+    the public API with the input copied from pinned host memory and the result copied back."""
+    import torch
+    import torch.distributed as dist
+
+    from tensorcore_ptx_example_b200 import allreduce as ar
+    from tensorcore_ptx_example_b200 import workloads
+    rows, cols = workloads.CFG4_SHAPE
+    numel = numel or rows * cols
+    steps = steps or max(5, min(args.steps, 20))
+    x = workloads.gaussian(1, numel, seed=rank).view(-1)
+    gs = ar.agree_global_scale(float(nv.amax(x).item()))
+    ctx = ar.AllReduce.from_process_group(numel)
+    out = torch.empty_like(x)
+    res = {"workload": f"cfg4 all-reduce {numel} bf16 elements per rank (N(0,1), seed = rank)",
+           "world": world, "global_scale": gs, "l2": "flushed between calls" if flush is not None else "not flushed"}
+    try:
+        runs = [("nvfp4_twoshot", lambda: ctx.allreduce(x, out, global_scale=gs, algo="twoshot"), 0.5625),
+                ("nvfp4_oneshot", lambda: ctx.allreduce(x, out, global_scale=gs, algo="oneshot"), 0.5625),
+                ("bf16_twoshot", lambda: ctx.bf16_allreduce(x, out, algo="twoshot"), 2.0),
+                ("bf16_oneshot", lambda: ctx.bf16_allreduce(x, out, algo="oneshot"), 2.0)]
+        for name, fn, bpe in runs:
+            ms = _ar_time(fn, steps, 3, flush, world)
+            res[name] = _ar_entry(name, numel, world, ms, bpe)
+        # accuracy of both NVFP4 algorithms against the exact (fp32, NCCL) sum
+        exact = x.float().clone()
+        dist.all_reduce(exact)
+        for algo in ("twoshot", "oneshot"):
+            o = ctx.allreduce(x, out, global_scale=gs, algo=algo).float()
+            res[f"nvfp4_{algo}"]["rel_rmse_vs_fp32_sum"] = round(float((o - exact).norm() / exact.norm()), 5)
+        torch.cuda.synchronize()
+        res["device_status"] = nv.device_status()
+        # end to end: pinned host input -> device, all-reduce (two-shot), device -> pinned host
+        hx = x.cpu().pin_memory()
+        ho = torch.empty_like(hx).pin_memory()
+
+        def e2e():
+            x.copy_(hx, non_blocking=True)
+            ctx.allreduce(x, out, global_scale=gs, algo="twoshot")
+            ho.copy_(out, non_blocking=True)
+        e2e_ms = _ar_time(e2e, max(3, steps // 2), 2, None, world)
+        res["e2e_nvfp4_twoshot"] = {"us": round(e2e_ms * 1e3, 2),
+                                    "algbw_gbs": round(2.0 * numel / (e2e_ms * 1e-3) / 1e9, 1),
+                                    "h2d_bytes_per_step": numel * 2, "d2h_bytes_per_step": numel * 2}
+        res["gpu_launches_per_call"] = 1
+    finally:
+        torch.cuda.synchronize()
+        barrier(world)
+        ctx.close()
+    return res
+
+
+def allreduce_sweep(args):
+    """cfg5: 16 KB .. 256 MB of bf16 per rank (doubling), NVFP4 one-shot / two-shot and bf16
+    one-shot / two-shot, max over ranks of the mean device time per call."""
+    import torch
+
+    import tensorcore_ptx_example_b200 as nv
+    from tensorcore_ptx_example_b200 import allreduce as ar
+    from tensorcore_ptx_example_b200 import workloads
+    world, rank, local = dist_setup(args)
+    sizes = [b for b in workloads.sweep_sizes_bytes() if (b // 2) % (32 * world) == 0]
+    max_numel = max(sizes) // 2
+    ctx = ar.AllReduce.from_process_group(max_numel)
+    xfull = workloads.gaussian(1, max_numel, seed=rank).view(-1)
+    gs = ar.agree_global_scale(float(nv.amax(xfull).item()))
+    ofull = torch.empty_like(xfull)
+    rows = []
+    try:
+        for b in sizes:
+            n = b // 2
+            x, o = xfull[:n], ofull[:n]
+            steps = 20 if b <= (16 << 20) else 8
+            row = {"bytes": b, "numel": n}
+            for name, fn, bpe in [
+                    ("nvfp4_oneshot", lambda: ctx.allreduce(x, o, global_scale=gs, algo="oneshot"), 0.5625),
+                    ("nvfp4_twoshot", lambda: ctx.allreduce(x, o, global_scale=gs, algo="twoshot"), 0.5625),
+                    ("bf16_oneshot", lambda: ctx.bf16_allreduce(x, o, algo="oneshot"), 2.0),
+                    ("bf16_twoshot", lambda: ctx.bf16_allreduce(x, o, algo="twoshot"), 2.0)]:
+                ms = _ar_time(fn, steps, 3, None, world)
+                e = _ar_entry(name, n, world, ms, bpe)
+                row[name] = {"us": e["us"], "algbw_gbs": e["algbw_gbs"], "busbw_gbs": e["busbw_gbs"]}
+            rows.append(row)
+        torch.cuda.synchronize()
+        status = nv.device_status()
+    finally:
+        barrier(world)
+        ctx.close()
+    if rank == 0:
+        print(json.dumps({"sweep": "cfg5 all-reduce message sizes", "world": world, "device_status": status,
+                          "l2": "not flushed (back-to-back calls)", "rows": rows}), flush=True)
+    import torch.distributed as dist
+    if world > 1:
+        dist.destroy_process_group()
 
 
 def read_profile_traffic(name):
@@ -411,6 +530,24 @@ def run_only(args):
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     if args.only == "quantize":
         out = quantize_bench(nv, args.steps, args.warmup, flush)
+    elif args.only == "ar-emulated":
+        # the all-reduce data path of 8 ranks on this one GPU, phase by phase (no cross-GPU
+        # waits): for profiling the phase kernels' memory traffic on a single device
+        from tensorcore_ptx_example_b200 import allreduce as ar
+        from tensorcore_ptx_example_b200 import workloads
+        world, numel = 8, args.numel
+        ins = [workloads.gaussian(1, numel, seed=r).view(-1) for r in range(world)]
+        gs = nv.global_scale_from_amax(max(float(nv.amax(x).item()) for x in ins))
+        ctxs = [ar.AllReduce(world, r, numel) for r in range(world)]
+        ar.join_in_process(ctxs)
+        for algo in ("twoshot", "oneshot"):
+            for _ in range(args.warmup + args.steps):
+                ar.emulated_allreduce(ins, gs, algo, contexts=ctxs)
+        torch.cuda.synchronize()
+        for c in ctxs:
+            c.close()
+        out = {"workload": f"emulated 8-rank all-reduce, {numel} elements per rank", "launches_per_call":
+               "twoshot 3 phases x 8 ranks, oneshot 2 phases x 8 ranks"}
     else:
         pa, sa, pb, sb, alpha, d = gemm_setup(nv, 0)
         fn = lambda: nv.gemm(pa, sa, pb, sb, M_, N_, K_, alpha=alpha, out=d)  # noqa: E731
@@ -432,13 +569,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["gemm", "quantize"], default=None,
+    ap.add_argument("--numel", type=int, default=4 << 20, help="elements per rank for --only ar-emulated")
+    ap.add_argument("--only", choices=["gemm", "quantize", "ar-sweep", "ar-emulated"], default=None,
                     help="profiling mode: run one workload (warmup + steps launches) and print its "
                          "timings; not the benchmark line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.only:
+    if args.only == "ar-sweep":
+        allreduce_sweep(args)
+    elif args.only:
         run_only(args)
     elif args.impl == "reference":
         run_reference(args)

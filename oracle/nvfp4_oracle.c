@@ -139,7 +139,9 @@ float orc_amax_f32(const float* x, int64_t n) {
 void orc_q16(const float* v, float gs_inv, uint8_t* nib, uint8_t* sf) {
     float amax = 0.0f;
     for (int i = 0; i < 16; i++) amax = fmaxf(amax, fabsf(v[i]));
-    const float t = amax / 6.0f;
+    /* fp32(1/6) rounded to nearest (0x3E2AAAAB) */
+    const float rcp6 = 0.16666667163372039794921875f;
+    const float t = amax * rcp6;
     const float s = t * gs_inv;
     const uint8_t code = orc_e4m3_encode(s);
     const float sq = orc_e4m3_decode(code);
@@ -148,7 +150,7 @@ void orc_q16(const float* v, float gs_inv, uint8_t* nib, uint8_t* sf) {
         for (int i = 0; i < 16; i++) nib[i] = 0;
         return;
     }
-    const float inv = gs_inv / sq;
+    const float inv = gs_inv * (1.0f / sq);
     for (int i = 0; i < 16; i++) {
         const float y = v[i] * inv;
         nib[i] = orc_e2m1_encode(y);

@@ -17,7 +17,7 @@
  *   - the quantizer, dequantizer and all-reduce sums follow the reference's q16 /
  *     dq32_acc / fused-kernel data flow (blackwell/allreduce_sm100_sm120/
  *     nvfp4_allreduce.cuh:272-317, :498-619) with the reference's approximate
- *     reciprocals replaced by IEEE division so that CPU and GPU agree bit for bit.
+ *     reciprocals replaced by correctly rounded ones so that CPU and GPU agree bit for bit.
  *
  * Every function below is pure host C with no CUDA dependency.
  */
@@ -74,12 +74,13 @@ float orc_amax_bf16(const uint16_t* x, int64_t n);
 float orc_amax_f32(const float* x, int64_t n);
 
 /* One 16-element block: nib[i] = E2M1 code of element i, *sf = UE4M3 block scale.
- *   t   = amax / 6            (IEEE div)
- *   s   = t * gs_inv          (IEEE mul)
+ *   t   = amax * fp32(1/6)           (IEEE mul; fp32(1/6) = 0x3E2AAAAB, round to nearest)
+ *   s   = t * gs_inv                 (IEEE mul)
  *   sf  = e4m3(s)
- *   inv = gs_inv / decode(sf) (IEEE div); sf == 0 -> every code is 0
- *   nib = e2m1(v * inv)       (IEEE mul, then RNE)
- * Follows q16 (nvfp4_allreduce.cuh:272-290) with rcp.approx replaced by division. */
+ *   inv = gs_inv * (1 / decode(sf))  (IEEE div then mul); sf == 0 -> every code is 0
+ *   nib = e2m1(v * inv)              (IEEE mul, then RNE)
+ * Follows q16 (nvfp4_allreduce.cuh:272-290), whose two approximate reciprocals
+ * (rcp.approx.ftz of 6 and of the stored scale) become correctly rounded ones. */
 void orc_q16(const float* v, float gs_inv, uint8_t* nib, uint8_t* sf);
 
 /* Quantize a row-major rows x cols tensor (cols % 16 == 0).

@@ -103,14 +103,7 @@ __device__ __forceinline__ void tma_load_pair(uint32_t dst, const void* tmap, in
         "l"(tmap), "r"(x), "r"(y), "r"(bar)
         : "memory");
 }
-__device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int32_t x, int32_t y) {
-    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap), "r"(src),
-                 "r"(x), "r"(y)
-                 : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 __device__ __forceinline__ void tc_mma2(uint32_t d, uint64_t a, uint64_t b, uint32_t sfa, uint32_t sfb,
                                         uint32_t accumulate) {

@@ -109,14 +109,18 @@ __device__ __forceinline__ void global_scale_from_amax(float amax, float& gs, fl
 }
 
 // Block scale of one 16-element block from its amax:
-//   s = (amax / 6) * gs_inv, stored as E4M3; inv = gs_inv / decode(stored) (0 when the
-//   stored scale is 0).  Returns the scale byte, writes inv.
+//   s = (amax * RCP6) * gs_inv, stored as E4M3; inv = gs_inv * rcp(decode(stored)) (0 when the
+//   stored scale is 0).  RCP6 is 1/6 rounded to fp32 and rcp is the correctly rounded
+//   reciprocal, so every step is one IEEE operation a CPU reproduces bit for bit (the
+//   reference, nvfp4_allreduce.cuh:272-290, uses rcp.approx.ftz for both reciprocals).
+//   Returns the scale byte, writes inv.
+constexpr uint32_t RCP6_BITS = 0x3E2AAAABu;    // fp32(1/6), round to nearest
 __device__ __forceinline__ uint32_t block_scale(float amax, float gs_inv, float& inv) {
-    const float t = __fdiv_rn(amax, 6.0f);
+    const float t = __fmul_rn(amax, __uint_as_float(RCP6_BITS));
     const float s = __fmul_rn(t, gs_inv);
     const uint32_t code = e4m3_encode(s);
     const float sq = e4m3_decode(code);
-    inv = (sq != 0.0f) ? __fdiv_rn(gs_inv, sq) : 0.0f;
+    inv = (sq != 0.0f) ? __fmul_rn(gs_inv, __frcp_rn(sq)) : 0.0f;
     return code;
 }
 
@@ -136,6 +140,28 @@ __device__ __forceinline__ uint32_t q16(const float* v, float gs_inv, uint32_t& 
     return code;
 }
 
+// The same for 16 bf16 values packed two per word (element 2i in the low half of word i).
+// The amax is taken on the bit patterns: for finite bf16, |x| orders like (bits & 0x7FFF),
+// which two-lane 16-bit max instructions reduce four words at a time.
+__device__ __forceinline__ uint32_t q16_bf16(const uint32_t* w, float gs_inv, uint32_t& w0, uint32_t& w1) {
+    uint32_t m = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) m = __vmaxu2(m, w[i] & 0x7FFF7FFFu);
+    const float amax = __uint_as_float(((m >> 16) > (m & 0xFFFFu) ? (m >> 16) : (m & 0xFFFFu)) << 16);
+    float inv;
+    const uint32_t code = block_scale(amax, gs_inv, inv);
+    float y[16];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        y[2 * i] = __fmul_rn(__uint_as_float(w[i] << 16), inv);
+        y[2 * i + 1] = __fmul_rn(__uint_as_float(w[i] & 0xFFFF0000u), inv);
+    }
+    w0 = e2m1x8(y);
+    w1 = e2m1x8(y + 8);
+    if (inv == 0.0f) { w0 = 0u; w1 = 0u; }
+    return code;
+}
+
 // ------------------------------------------------------------- PTX basics ----
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -147,6 +173,13 @@ __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                  : "l"(p));
     return r;
+}
+
+// 32-byte load (sm_100 256-bit vector load); p must be 32-byte aligned.
+__device__ __forceinline__ void ld_nc_v8(const void* p, uint32_t* r) {
+    asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "l"(p));
 }
 
 __device__ __forceinline__ void st_v4(void* p, uint4 v) {
@@ -213,6 +246,23 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
         "l"(src), "r"(bytes), "r"(bar)
         : "memory");
+}
+
+// 2D TMA store from this CTA's shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap), "r"(src),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read_n() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {

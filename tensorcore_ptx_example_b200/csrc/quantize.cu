@@ -2,84 +2,37 @@
 //
 // Data movement (HBM-bound; algorithmic bytes per element: read 2, write 0.5 packed +
 // 0.0625 scale = 2.5625 B):
-//   The unit of work is one scale-factor atom: 128 rows x 64 columns.  A persistent CTA
-//   (two per SM) streams its atoms' bf16 tiles (128 rows x 128 bytes) into a 6-stage shared
-//   memory ring with one 2D TMA load each (SWIZZLE_128B, so the per-row reads below are bank
-//   conflict free); a producer warp issues the loads, four consumer warps quantize.
-//   Consumer thread t handles row (t % 4) * 32 + t / 4 of the atom, so the 32-bit word of
-//   four block scales it produces sits at word t of the 512-byte atom and the warps write
-//   the atom with fully coalesced stores; each thread writes its 32 packed bytes with two
-//   16-byte stores.  CTAs walk atoms in memory order (k-atom fastest).
+//   The tensor is swept in flat element order, one 16-element block per thread: lane l of a
+//   warp reads bytes [32 l, 32 l + 32) of a 1 KB stretch (one 32-byte load) and writes the
+//   block's 8 packed bytes (a warp writes 256 contiguous bytes), so at any moment the grid
+//   reads one contiguous stretch of memory.  Each thread has QR_UNROLL blocks (64 bytes) of
+//   loads in flight before any arithmetic.  The 4 lanes of one row's 64-column group assemble
+//   the 32-bit word of their four block scales and the first of them stores it at its place in
+//   the tcgen05 layout; (row, column) are tracked incrementally, without divisions.
+//   Measured against the alternatives on B200 (cfg2, 8192 x 7168): a 128 x 64 TMA-tile ring
+//   read at ~4 TB/s even with the arithmetic and stores removed (38 us in all), 8 elements per
+//   thread (a block split across a lane pair) doubled the per-element arithmetic (51-67 us);
+//   this kernel: ~37 us with 2 blocks in flight per thread (4 or 8 were slower).
 //
 // Arithmetic (per 16-element block; bit-exact against oracle/nvfp4_oracle.c orc_q16):
-//   amax -> s = (amax / 6) * gs_inv -> e4m3(s) -> inv = gs_inv / e4m3(s) -> e2m1(v * inv).
+//   amax -> s = (amax * fp32(1/6)) * gs_inv -> e4m3(s) -> inv = gs_inv * rcp(e4m3(s))
+//   -> e2m1(v * inv), every step one correctly rounded IEEE operation.
 //   Reference: nvfp4_allreduce.cuh:272-290 (q16) and :427-454 (quantize_kernel, which
 //   writes a linear scale layout instead of the tcgen05 one).
 #include "capi_internal.h"
 #include "nvfp4_common.cuh"
-#include "tma_host.h"
 
 namespace nvfp4 {
 
 constexpr int QTHREADS = 128;                 // dequantizer CTA
-constexpr int QT_STAGES = 6;                  // quantizer ring depth
-constexpr int QT_TILE = 128 * 128;            // 128 rows x 64 bf16
-constexpr int QT_THREADS = 160;               // warps 0-3 consume, warp 4 loads
-constexpr int QT_SMEM = 1024 + QT_STAGES * QT_TILE + 2 * QT_STAGES * 8;
-constexpr uint64_t QT_WAIT_NS = 2000000000ull;
+constexpr int QR_THREADS = 256;               // quantizer CTA
+constexpr int QR_UNROLL = 2;                  // 16-element blocks (32 bytes) in flight per thread
 
-// Scale word for one (row, 64-column group): four block scales, kblock j in byte j.
-template <bool kDevScale>
-__global__ void __launch_bounds__(QT_THREADS)
-quantize_kernel(const __grid_constant__ CUtensorMap tmap_x, int64_t rows, int64_t cols, float gs_host,
-                const uint32_t* __restrict__ amax_word, float* __restrict__ gs_out,
-                uint8_t* __restrict__ packed, uint32_t* __restrict__ sf_words, int64_t units) {
-    extern __shared__ uint8_t qsmem_raw[];
-    const uint32_t raw_addr = smem_u32(qsmem_raw);
-    const uint32_t base = (raw_addr + 1023u) & ~1023u;
-    const uint8_t* tiles = qsmem_raw + (base - raw_addr);
-    const uint32_t bar0 = base + QT_STAGES * QT_TILE;
-    auto full_bar = [&](int s) { return bar0 + 8u * s; };
-    auto empty_bar = [&](int s) { return bar0 + 8u * (QT_STAGES + s); };
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t katoms = cols / 64;
-
-    if (warp == 4 && lane == 0) {
-        prefetch_tmap(&tmap_x);
-        for (int s = 0; s < QT_STAGES; s++) {
-            mbar_init(full_bar(s), 1);
-            mbar_init(empty_bar(s), 128);
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    }
-    __syncthreads();
-
-    if (warp == 4) {
-        // ---------------------------------------------------------------- loads ----
-        if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0, pending = 0;
-            bool ok = true;
-            for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
-                if (!mbar_wait(empty_bar(stage), phase ^ 1u, QT_WAIT_NS, DEV_TIMEOUT_QUANT)) { ok = false; break; }
-                pending &= ~(1u << stage);
-                const int64_t rg = u / katoms, kg = u - rg * katoms;
-                mbar_arrive_expect_tx(full_bar(stage), QT_TILE);
-                tma_load_2d(base + stage * QT_TILE, &tmap_x, (int32_t)(kg * 64), (int32_t)(rg * 128), full_bar(stage));
-                pending |= 1u << stage;
-                if (++stage == QT_STAGES) { stage = 0; phase ^= 1u; }
-            }
-            if (!ok)   // never release shared memory with loads still landing in it
-                for (int s = 0; s < QT_STAGES; s++)
-                    if (pending & (1u << s))
-                        mbar_wait(full_bar(s), s < stage ? phase : (phase ^ 1u), QT_WAIT_NS, DEV_TIMEOUT_QUANT);
-        }
-        __syncwarp();
-        return;
-    }
-
-    // ------------------------------------------------------------------ consumers ----
+template <bool kDevScale, bool kLoad32>
+__global__ void __launch_bounds__(QR_THREADS)
+quantize_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t cols, float gs_host,
+                const uint32_t* __restrict__ amax_word, float* __restrict__ gs_out, uint8_t* __restrict__ packed,
+                uint8_t* __restrict__ sf) {
     float gs = gs_host, gs_inv;
     if constexpr (kDevScale) {
         global_scale_from_amax(__uint_as_float(*amax_word), gs, gs_inv);
@@ -87,53 +40,68 @@ quantize_kernel(const __grid_constant__ CUtensorMap tmap_x, int64_t rows, int64_
     } else {
         gs_inv = __fdiv_rn(1.0f, gs);
     }
-    const int t = threadIdx.x;
-    const int r_in_atom = (t & 3) * 32 + (t >> 2);
-    int stage = 0;
-    uint32_t phase = 0;
+    const int lane = threadIdx.x & 31;
+    const int64_t katoms = cols / 64;
+    const int64_t nblocks = rows * cols / 16;
+    const int64_t step = (int64_t)gridDim.x * QR_THREADS;    // blocks between a thread's loads
+    // (row, col) of this thread's block, tracked incrementally (no division in the loop)
+    const int64_t e_step = step * 16;
+    const int64_t dr = e_step / cols, dc = e_step - dr * cols;
+    int64_t b0 = (int64_t)blockIdx.x * QR_THREADS + threadIdx.x;
+    int64_t row = (b0 * 16) / cols, col = b0 * 16 - row * cols;
+    const uint8_t* xb = reinterpret_cast<const uint8_t*>(x);
 #pragma unroll 1
-    for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
-        if (!mbar_wait(full_bar(stage), phase, QT_WAIT_NS, DEV_TIMEOUT_QUANT)) break;
-        // Row r_in_atom of the tile: 16-byte chunk c sits at chunk c ^ (row % 8) (SWIZZLE_128B).
-        const uint8_t* srow = tiles + stage * QT_TILE + r_in_atom * 128;
-        uint4 raw[8];
+    for (; b0 - lane < nblocks; b0 += step * QR_UNROLL) {
+        uint32_t raw[QR_UNROLL][8];
 #pragma unroll
-        for (int c = 0; c < 8; c++)
-            raw[c] = *reinterpret_cast<const uint4*>(srow + ((c ^ (r_in_atom & 7)) << 4));
-        // The stage is released only after the values read from it have been consumed (a
-        // register dependency): an arrive issued right after the shared-memory loads let the
-        // next TMA write overtake them (measured on B200 as rare corrupted rows).
-        const uint32_t my_stage = stage;
-        if (++stage == QT_STAGES) { stage = 0; phase ^= 1u; }
-
-        const int64_t rg = u / katoms, kg = u - rg * katoms;
-        const int64_t row = rg * 128 + r_in_atom;
-        uint32_t word = 0;
-        if (row < rows) {
-            uint32_t nib[8];
-#pragma unroll
-            for (int b = 0; b < 4; b++) {
-                float v[16];
-#pragma unroll
-                for (int i = 0; i < 2; i++) {
-                    const uint32_t w[4] = {raw[2 * b + i].x, raw[2 * b + i].y, raw[2 * b + i].z,
-                                           raw[2 * b + i].w};
-#pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        v[i * 8 + 2 * j] = __uint_as_float(w[j] << 16);
-                        v[i * 8 + 2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
-                    }
+        for (int i = 0; i < QR_UNROLL; i++) {
+            const int64_t b = b0 + i * step;
+            if (b < nblocks) {
+                if constexpr (kLoad32) {
+                    ld_nc_v8(xb + b * 32, raw[i]);          // one 32-byte load per block
+                } else {
+                    const uint4 lo = ld_nc_v4(xb + b * 32), hi = ld_nc_v4(xb + b * 32 + 16);
+                    raw[i][0] = lo.x; raw[i][1] = lo.y; raw[i][2] = lo.z; raw[i][3] = lo.w;
+                    raw[i][4] = hi.x; raw[i][5] = hi.y; raw[i][6] = hi.z; raw[i][7] = hi.w;
                 }
-                const uint32_t code = q16(v, gs_inv, nib[2 * b], nib[2 * b + 1]);
-                word |= code << (8 * b);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; j++) raw[i][j] = 0u;
             }
-            mbar_arrive(empty_bar(my_stage));
-            uint8_t* dst = packed + row * (cols / 2) + kg * 32;
-            st_v4(dst, make_uint4(nib[0], nib[1], nib[2], nib[3]));
-            st_v4(dst + 16, make_uint4(nib[4], nib[5], nib[6], nib[7]));
         }
-        else mbar_arrive(empty_bar(my_stage));
-        sf_words[u * 128 + t] = word;
+#pragma unroll
+        for (int i = 0; i < QR_UNROLL; i++) {
+            const int64_t b = b0 + i * step;
+            uint32_t n0, n1;
+            const uint32_t code = q16_bf16(raw[i], gs_inv, n0, n1);
+            const uint32_t c1 = __shfl_down_sync(0xFFFFFFFFu, code, 1);
+            const uint32_t c2 = __shfl_down_sync(0xFFFFFFFFu, code, 2);
+            const uint32_t c3 = __shfl_down_sync(0xFFFFFFFFu, code, 3);
+            if (b < nblocks) {
+                *reinterpret_cast<uint2*>(packed + b * 8) = make_uint2(n0, n1);
+                if ((lane & 3) == 0) {                // first block of a row's 64-column group
+                    const int64_t off = ((row >> 7) * katoms + (col >> 6)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4;
+                    *reinterpret_cast<uint32_t*>(sf + off) = code | (c1 << 8) | (c2 << 16) | (c3 << 24);
+                }
+            }
+            row += dr;
+            col += dc;
+            if (col >= cols) { col -= cols; row++; }
+        }
+    }
+}
+
+// Scale words of the padding rows of the last 128-row group (rows .. ceil(rows/128)*128 - 1):
+// zero, as the layout requires for rows that do not exist.
+__global__ void sf_pad_kernel(uint8_t* __restrict__ sf, int64_t rows, int64_t cols) {
+    const int64_t katoms = cols / 64;
+    const int64_t rg = rows >> 7;
+    const int64_t pad = (rg + 1) * 128 - rows;   // 1..127 (only launched when rows % 128 != 0)
+    const int64_t n = pad * katoms;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = rows + i / katoms, ka = i % katoms;
+        const int64_t off = (rg * katoms + ka) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4;
+        *reinterpret_cast<uint32_t*>(sf + off) = 0u;
     }
 }
 
@@ -208,30 +176,29 @@ static int quant_grid(int64_t units) {
     return (int)(units < cap ? units : cap);
 }
 
-// Launch the TMA quantizer (kDevScale: the global scale comes from *amax_word).
+// Launch the quantizer (kDevScale: the global scale comes from *amax_word).
 template <bool kDevScale>
 static nvfp4_status_t launch_quantize(const void* x, int64_t rows, int64_t cols, float gs, const uint32_t* amax_word,
                                       float* gs_out, void* packed, void* sf, cudaStream_t s) {
-    const int64_t units = ((rows + 127) / 128) * (cols / 64);
-    if (units == 0) return NVFP4_OK;
-    CUtensorMap tm;
-    nvfp4_status_t st = make_tmap_2d(&tm, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, cols, rows, cols * 2, 64, 128,
-                                     CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st != NVFP4_OK) return st;
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(quantize_kernel<kDevScale>, cudaFuncAttributeMaxDynamicSharedMemorySize, QT_SMEM);
-        if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "quantize: smem attribute: %s", cudaGetErrorString(e));
-        if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
-    const int64_t cap = (int64_t)sm_count() * 2;
-    const int grid = (int)(units < cap ? units : cap);
-    quantize_kernel<kDevScale><<<grid, QT_THREADS, QT_SMEM, s>>>(tm, rows, cols, gs, amax_word, gs_out,
-                                                                reinterpret_cast<uint8_t*>(packed),
-                                                                reinterpret_cast<uint32_t*>(sf), units);
-    return check_launch("quantize_kernel");
+    const int64_t nblocks = rows * cols / 16;
+    if (nblocks == 0) return NVFP4_OK;
+    const int64_t per_cta = (int64_t)QR_THREADS * QR_UNROLL;
+    const int64_t cap = (int64_t)sm_count() * 4;
+    int64_t grid = (nblocks + per_cta - 1) / per_cta;
+    if (grid > cap) grid = cap;
+    // 32-byte loads when the input allows them (16-byte alignment is the API's minimum)
+    if ((reinterpret_cast<uintptr_t>(x) & 31) == 0)
+        quantize_kernel<kDevScale, true><<<(unsigned)grid, QR_THREADS, 0, s>>>(
+            reinterpret_cast<const __nv_bfloat16*>(x), rows, cols, gs, amax_word, gs_out,
+            reinterpret_cast<uint8_t*>(packed), reinterpret_cast<uint8_t*>(sf));
+    else
+        quantize_kernel<kDevScale, false><<<(unsigned)grid, QR_THREADS, 0, s>>>(
+            reinterpret_cast<const __nv_bfloat16*>(x), rows, cols, gs, amax_word, gs_out,
+            reinterpret_cast<uint8_t*>(packed), reinterpret_cast<uint8_t*>(sf));
+    nvfp4_status_t st = check_launch("quantize_kernel");
+    if (st != NVFP4_OK || rows % 128 == 0) return st;
+    sf_pad_kernel<<<64, 256, 0, s>>>(reinterpret_cast<uint8_t*>(sf), rows, cols);
+    return check_launch("sf_pad_kernel");
 }
 
 static nvfp4_status_t launch_amax(const void* x, int64_t numel, uint32_t* word, cudaStream_t s) {

@@ -118,7 +118,7 @@ def test_handle_exchange_and_scale_agreement_on_gloo_ranks():
     import torch.multiprocessing as mp
     world = 2
     port = _free_port()
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:
         results = m.dict()
         mp.spawn(_gloo_worker, args=(world, port, results), nprocs=world, join=True)
         res = dict(results)

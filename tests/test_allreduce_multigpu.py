@@ -160,7 +160,7 @@ def test_multi_process_ipc_allreduce_bitexact(oracle):
     world = min(ngpus(), 4)
     numel = 32 * world * 777
     port = _free_port()
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:
         results = m.dict()
         mp.spawn(_ipc_worker, args=(world, port, numel, results), nprocs=world, join=True)
         res = dict(results)
