@@ -175,14 +175,22 @@ class L2Flush:
         self.r.sum()
 
 
-def timed_steps(fn, steps, flush):
-    """Per-step CUDA-event timing on the current stream with an L2 flush between steps."""
+HIDE_HOST_CYCLES = 400_000       # ~200 us of GPU spin before each timed step
+
+
+def timed_steps(fn, steps, flush, hide_host=True):
+    """Per-step CUDA-event timing on the current stream with an L2 flush between steps.
+    With hide_host the GPU spins for a while before each step's start event, so the host's
+    launch work for the step is done before the GPU reaches the event: the region then holds
+    device time only, even for calls shorter than their launch overhead."""
     import torch
     s = torch.cuda.current_stream()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     for i in range(steps):
         if flush is not None:
             flush()
+        if hide_host:
+            torch.cuda._sleep(HIDE_HOST_CYCLES)
         evs[i][0].record(s)
         fn()
         evs[i][1].record(s)
@@ -226,6 +234,36 @@ def quantize_bench(nv, steps, warmup, flush):
         "amax_us": round(sum(ts_amax) / len(ts_amax) * 1e3, 2),
         "auto_scale_total_us": round(sum(ts_auto) / len(ts_auto) * 1e3, 2),
     }
+
+
+def decode_bench(nv, steps, warmup, flush):
+    """cfg3 decode shape M16 N7168 K8192 (HBM-bound: the kernel streams B once)."""
+    import torch
+    from tensorcore_ptx_example_b200 import workloads
+    M, N, K = workloads.CFG3_DECODE_SHAPE
+    a = workloads.activations(M, K, seed=5)
+    b = workloads.gaussian(N, K, seed=6, std=0.02)
+    pa, sa, gsa = nv.quantize(a, None)
+    pb, sb, gsb = nv.quantize(b, None)
+    torch.cuda.synchronize()
+    alpha = float(gsa.item()) * float(gsb.item())
+    d = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    fn = lambda: nv.gemm(pa, sa, pb, sb, M, N, K, alpha=alpha, out=d)  # noqa: E731
+    for _ in range(warmup):
+        fn()
+    ts = timed_steps(fn, steps, flush)
+    ms = sum(ts) / len(ts)
+    # algorithmic bytes: B and its scales, A and its scales, D
+    byts = N * K // 2 + N * K // 16 + M * K // 2 + nv.sf_bytes(M, K) + M * N * 2
+    peaks, peak_kind = load_peaks()
+    hbm = float(peaks.get("hbm_gbs", HBM_FALLBACK_GBS))
+    gbs = byts / (ms * 1e-3) / 1e9
+    return {"workload": "cfg3 decode GEMM M16 N7168 K8192 (split-K over 128-row tiles of B)",
+            "us": round(ms * 1e3, 2), "tflops": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1),
+            "bytes_per_call": int(byts),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gbs / hbm, 4), "peak_source": f"{peak_kind} HBM copy"},
+            "launches_per_call": 2}
 
 
 def cpu_baseline_gemm(target_s=8.0):
@@ -325,6 +363,10 @@ def run_ours(args):
             extra["quantize"] = quantize_bench(nv, max(5, args.steps), 3, flush)
         except Exception as e:  # reported, not fatal
             extra["quantize"] = {"error": str(e)}
+        try:
+            extra["gemm_decode"] = decode_bench(nv, max(5, args.steps), 3, flush)
+        except Exception as e:  # reported, not fatal
+            extra["gemm_decode"] = {"error": str(e)}
     if world > 1:
         extra["allreduce"] = allreduce_bench(nv, world, rank, args, flush=flush)
 
@@ -551,6 +593,8 @@ def run_only(args):
     flush = L2Flush()
     if args.only == "quantize":
         out = quantize_bench(nv, args.steps, args.warmup, flush)
+    elif args.only == "gemm-decode":
+        out = decode_bench(nv, args.steps, args.warmup, flush)
     elif args.only == "ar-emulated":
         # the all-reduce data path of 8 ranks on this one GPU, phase by phase (no cross-GPU
         # waits): for profiling the phase kernels' memory traffic on a single device
@@ -591,7 +635,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--numel", type=int, default=4 << 20, help="elements per rank for --only ar-emulated")
-    ap.add_argument("--only", choices=["gemm", "quantize", "ar-sweep", "ar-emulated"], default=None,
+    ap.add_argument("--only", choices=["gemm", "gemm-decode", "quantize", "ar-sweep", "ar-emulated"], default=None,
                     help="profiling mode: run one workload (warmup + steps launches) and print its "
                          "timings; not the benchmark line")
     args = ap.parse_args()

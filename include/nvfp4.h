@@ -126,9 +126,18 @@ NVFP4_API nvfp4_status_t nvfp4_dequantize_bf16(const void* packed, const void* s
 /* D[M][N] = bf16(alpha * sum_k A[m][k] B[n][k] sfa sfb), fp32 accumulation in TMEM.
  * A: packed M x K, sfa: nvfp4_sf_bytes(M, K); B: packed N x K (weights, K-major),
  * sfb: nvfp4_sf_bytes(N, K); D: bf16 row-major M x N.  alpha = gsA * gsB.
- * Requires M % 128 == 0, N % 256 == 0, K % 256 == 0, 16-byte aligned buffers. */
+ * Requires K % 256 == 0, 16-byte aligned buffers, and either M % 128 == 0 with N % 256 == 0
+ * (tiled kernels), or 0 < M < 128 with N % 128 == 0 (decode shapes: a split-K kernel over
+ * 128-row tiles of B; its fp32 partials go to a workspace -- a buffer the library allocates once
+ * per device for nvfp4_gemm_bf16, or the caller's for nvfp4_gemm_bf16_ws -- and are summed in
+ * split order 0..S-1 before alpha and the bf16 rounding). */
 NVFP4_API nvfp4_status_t nvfp4_gemm_bf16(const void* A, const void* sfa, const void* B, const void* sfb,
                                float alpha, void* D, int64_t M, int64_t N, int64_t K, void* stream);
+/* Workspace bytes nvfp4_gemm_bf16_ws needs for this shape (0 for M % 128 == 0). */
+NVFP4_API size_t nvfp4_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
+NVFP4_API nvfp4_status_t nvfp4_gemm_bf16_ws(const void* A, const void* sfa, const void* B, const void* sfb,
+                                  float alpha, void* D, int64_t M, int64_t N, int64_t K, void* workspace,
+                                  size_t workspace_bytes, void* stream);
 /* Same kernel, raw fp32 accumulators (no alpha) into D (fp32 row-major M x N). */
 NVFP4_API nvfp4_status_t nvfp4_gemm_f32(const void* A, const void* sfa, const void* B, const void* sfb,
                               float* D, int64_t M, int64_t N, int64_t K, void* stream);

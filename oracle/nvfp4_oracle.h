@@ -122,6 +122,10 @@ enum {
  * sfa / sfb in the tcgen05 layout.  Output D row-major M x N fp32. */
 void orc_gemm_f32(const uint8_t* A, const uint8_t* sfa, const uint8_t* B, const uint8_t* sfb,
                   int64_t M, int64_t N, int64_t K, int model, float* D, int nthreads);
+/* Split-K with the tcgen05 model (the small-M kernel's arithmetic): the model over each K range
+ * of ks elements (ks % 64 == 0), partials summed in split order 0..K/ks-1 in fp32 from 0. */
+void orc_gemm_splitk_f32(const uint8_t* A, const uint8_t* sfa, const uint8_t* B, const uint8_t* sfb,
+                         int64_t M, int64_t N, int64_t K, int64_t ks, float* D, int nthreads);
 /* Same, but only the listed (m, n) outputs (for spot checks of large GEMMs). */
 void orc_gemm_f32_points(const uint8_t* A, const uint8_t* sfa, const uint8_t* B,
                          const uint8_t* sfb, int64_t M, int64_t N, int64_t K, int model,

@@ -70,6 +70,7 @@ def _bind(L):
         "orc_dequantize_bf16": (None, [P, P, I64, I64, F, P]),
         "orc_gemm_f32": (None, [P, P, P, P, I64, I64, I64, ctypes.c_int, P, ctypes.c_int]),
         "orc_gemm_f32_points": (None, [P, P, P, P, I64, I64, I64, ctypes.c_int, P, P, I64, P]),
+        "orc_gemm_splitk_f32": (None, [P, P, P, P, I64, I64, I64, I64, P, ctypes.c_int]),
         "orc_gemm_epilogue_bf16": (ctypes.c_uint16, [F, F]),
         "orc_ar_oneshot": (None, [P, ctypes.c_int, I64, F, P, ctypes.c_int]),
         "orc_ar_twoshot": (None, [P, ctypes.c_int, I64, F, P, ctypes.c_int]),
@@ -198,6 +199,15 @@ def gemm_f32(A, sfa, B, sfb, M, N, K, model=ACC_EXACT_PER_MMA, nthreads=None):
     lib().orc_gemm_f32(_p(np.ascontiguousarray(A)), _p(np.ascontiguousarray(sfa)),
                        _p(np.ascontiguousarray(B)), _p(np.ascontiguousarray(sfb)),
                        M, N, K, model, _p(D), nthreads or nthreads_default())
+    return D
+
+
+def gemm_splitk_f32(A, sfa, B, sfb, M, N, K, ks, nthreads=None):
+    """Split-K tcgen05 model: per-split chains of ks elements summed in split order (fp32)."""
+    D = np.zeros((M, N), dtype=np.float32)
+    lib().orc_gemm_splitk_f32(_p(np.ascontiguousarray(A)), _p(np.ascontiguousarray(sfa)),
+                              _p(np.ascontiguousarray(B)), _p(np.ascontiguousarray(sfb)),
+                              M, N, K, ks, _p(D), nthreads or nthreads_default())
     return D
 
 

@@ -40,6 +40,8 @@ SIGNATURES = {
     "nvfp4_dequantize_bf16": (_I, [_P, _P, _I64, _I64, _F, _P, _P]),
     "nvfp4_gemm_bf16": (_I, [_P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _P]),
     "nvfp4_gemm_f32": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
+    "nvfp4_gemm_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64]),
+    "nvfp4_gemm_bf16_ws": (_I, [_P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
     "nvfp4_diag_e2m1_encode": (_I, [_P, _P, _I64, _P]),
     "nvfp4_diag_e4m3_encode": (_I, [_P, _P, _I64, _P]),
     "nvfp4_diag_mma_peak": (_I, [_I, _I, _I, _P]),

@@ -192,6 +192,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
     auto sf_full = [&](int k) { return drain_bar + 8u + 8u * k; };
     auto sf_landed = [&](int st) { return drain_bar + 8u + 8u * (SF_SLOTS + st); };
     uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + OFF_TMEM_PTR);
+    volatile uint32_t* abort_flag = tmem_ptr + 1;
 
     const int num_m = M / 256, num_n = N / BN, tiles = num_m * num_n;
     const int nkb = K / BK;
@@ -211,6 +212,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
         mbar_init(tmem_full, 1);
         mbar_init(tmem_empty, 8);                      // one elected lane of 4 epilogue warps x 2 CTAs
         mbar_init(drain_bar, 1);
+        *abort_flag = 0u;
         for (int k = 0; k < SF_SLOTS; k++) mbar_init(sf_full(k), 8);   // 4 scale warps x 2 CTAs
         for (int st = 0; st < STAGES; st++) mbar_init(sf_landed(st), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -400,7 +402,13 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
         int iter = 0;
         for (int tile = pair; tile < ntiles; tile += npairs, iter++) {
             const int tm = tile % num_m, tn = tile / num_m;
-            if (!PROF_WAIT((warp == 2 && lane == 0) ? 6 : 7, mbar_wait(tmem_full, (uint32_t)(iter & 1), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_EPILOGUE))) break;
+            // The four epilogue warps give up together (they meet at named barriers below).
+            const bool ok = __all_sync(0xFFFFFFFFu, PROF_WAIT((warp == 2 && lane == 0) ? 6 : 7,
+                                                              mbar_wait(tmem_full, (uint32_t)(iter & 1), WAIT_LIMIT_NS,
+                                                                        DEV_TIMEOUT_GEMM_EPILOGUE)));
+            if (!ok && lane == 0) *abort_flag = 1u;
+            epi_bar();
+            if (*abort_flag) break;
             tc_fence_after();
             const uint32_t dcol = (iter & 1) ? ACC1_COL : 0;
             const int m0 = tm * 256 + (int)rank * BM;

@@ -1,16 +1,23 @@
 // gemm_api.cu -- C ABI of the NVFP4 GEMM: shape checks and kernel choice.
-//   M % 256 == 0: CTA-pair kernel (gemm_2sm.cu, tcgen05 cta_group::2, 256x256 pair tiles)
-//   otherwise   : single-CTA kernel (gemm.cu, 128x256 tiles)
+//   M <= 128, M % 128 != 0 : small-M split-K kernel (gemm_small.cu; decode shapes), N % 128 == 0
+//   M % 256 == 0            : CTA-pair kernel (gemm_2sm.cu, tcgen05 cta_group::2, 256x256 pair tiles)
+//   M % 128 == 0            : single-CTA kernel (gemm.cu, 128x256 tiles)
+#include <mutex>
+
 #include "capi_internal.h"
 
 namespace nvfp4 {
 namespace gemm {
 
+static bool small_m(int64_t M) { return M > 0 && M < 128; }
+
 static nvfp4_status_t check_args(const void* A, const void* sfa, const void* B, const void* sfb, const void* D,
                                  int64_t M, int64_t N, int64_t K) {
     if (!A || !sfa || !B || !sfb || !D) return fail(NVFP4_ERR_INVALID_ARG, "gemm: null pointer");
-    if (M <= 0 || N <= 0 || K <= 0 || M % 128 || N % 256 || K % 256)
-        return fail(NVFP4_ERR_INVALID_ARG, "gemm: need M %% 128 == 0, N %% 256 == 0, K %% 256 == 0 (got %lld %lld %lld)",
+    if (M <= 0 || N <= 0 || K <= 0 || K % 256 || (small_m(M) ? N % 128 : (M % 128 || N % 256)))
+        return fail(NVFP4_ERR_INVALID_ARG,
+                    "gemm: need K %% 256 == 0 and either M < 128 with N %% 128 == 0, or M %% 128 == 0 with "
+                    "N %% 256 == 0 (got %lld %lld %lld)",
                     (long long)M, (long long)N, (long long)K);
     if (M > (1ll << 30) || N > (1ll << 30) || K > (1ll << 30)) return fail(NVFP4_ERR_INVALID_ARG, "gemm: dimension too large");
     if (!aligned16(A) || !aligned16(B) || !aligned16(sfa) || !aligned16(sfb) || !aligned16(D))
@@ -18,11 +25,46 @@ static nvfp4_status_t check_args(const void* A, const void* sfa, const void* B, 
     return NVFP4_OK;
 }
 
+// Split-K workspace of the small-M path when the caller gives none: one buffer per device,
+// allocated on first use and grown when a larger one is needed (cudaFree synchronises the device,
+// so a buffer still in use by an earlier launch is never released under it).
+static nvfp4_status_t internal_workspace(size_t need, void** out) {
+    static std::mutex mu;
+    static void* buf[64] = {};
+    static size_t size[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return fail(NVFP4_ERR_UNSUPPORTED, "gemm: device ordinal %d", dev);
+    std::lock_guard<std::mutex> g(mu);
+    if (size[dev] < need) {
+        if (buf[dev]) cudaFree(buf[dev]);
+        buf[dev] = nullptr;
+        size[dev] = 0;
+        cudaError_t e = cudaMalloc(&buf[dev], need);
+        if (e != cudaSuccess) {
+            buf[dev] = nullptr;
+            return fail(NVFP4_ERR_CUDA, "gemm: workspace of %zu bytes: %s", need, cudaGetErrorString(e));
+        }
+        size[dev] = need;
+    }
+    *out = buf[dev];
+    return NVFP4_OK;
+}
+
 template <bool kOutF32>
 static nvfp4_status_t dispatch(const void* A, const void* sfa, const void* B, const void* sfb, float alpha, void* D,
-                               int64_t M, int64_t N, int64_t K, cudaStream_t s) {
+                               int64_t M, int64_t N, int64_t K, void* ws, size_t ws_bytes, cudaStream_t s) {
     nvfp4_status_t st = check_args(A, sfa, B, sfb, D, M, N, K);
     if (st != NVFP4_OK) return st;
+    if (small_m(M)) {
+        if (!ws) {
+            ws_bytes = gsmall::workspace_bytes(M, N, K);
+            if ((st = internal_workspace(ws_bytes, &ws))) return st;
+        } else if (!aligned16(ws)) {
+            return fail(NVFP4_ERR_INVALID_ARG, "gemm: workspace must be 16-byte aligned");
+        }
+        return gsmall::launch<kOutF32>(A, sfa, B, sfb, alpha, D, M, N, K, ws, ws_bytes, s);
+    }
     if (M % 256 == 0) return gemm2::launch<kOutF32>(A, sfa, B, sfb, alpha, D, M, N, K, s);
     return launch<kOutF32>(A, sfa, B, sfb, alpha, D, M, N, K, s);
 }
@@ -37,13 +79,25 @@ extern "C" {
 nvfp4_status_t nvfp4_gemm_bf16(const void* A, const void* sfa, const void* B, const void* sfb, float alpha, void* D,
                                int64_t M, int64_t N, int64_t K, void* stream) {
     clear_error();
-    return gemm::dispatch<false>(A, sfa, B, sfb, alpha, D, M, N, K, (cudaStream_t)stream);
+    return gemm::dispatch<false>(A, sfa, B, sfb, alpha, D, M, N, K, nullptr, 0, (cudaStream_t)stream);
+}
+
+size_t nvfp4_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+    return (M > 0 && M < 128) ? gsmall::workspace_bytes(M, N, K) : 0;
+}
+
+nvfp4_status_t nvfp4_gemm_bf16_ws(const void* A, const void* sfa, const void* B, const void* sfb, float alpha, void* D,
+                                  int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes,
+                                  void* stream) {
+    clear_error();
+    if (M > 0 && M < 128 && !workspace) return fail(NVFP4_ERR_INVALID_ARG, "gemm_ws: null workspace");
+    return gemm::dispatch<false>(A, sfa, B, sfb, alpha, D, M, N, K, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 nvfp4_status_t nvfp4_gemm_f32(const void* A, const void* sfa, const void* B, const void* sfb, float* D, int64_t M,
                               int64_t N, int64_t K, void* stream) {
     clear_error();
-    return gemm::dispatch<true>(A, sfa, B, sfb, 1.0f, D, M, N, K, (cudaStream_t)stream);
+    return gemm::dispatch<true>(A, sfa, B, sfb, 1.0f, D, M, N, K, nullptr, 0, (cudaStream_t)stream);
 }
 
 }  // extern "C"

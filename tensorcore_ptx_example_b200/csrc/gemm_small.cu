@@ -1,0 +1,354 @@
+// gemm_small.cu -- NVFP4 block-scaled GEMM for small M (decode shapes, M <= 128), sm_100a.
+//
+//   D[M][N] = alpha * sum_k A[m][k] B[n][k] sfa sfb      (same contract as nvfp4_gemm_bf16)
+//
+// With M = 16 the GEMM is a stream over B (N x K E2M1 + scales, 33 MB at N = 7168, K = 8192) and
+// is HBM-bound.  The kernel swaps the operands so that the 128-row tensor-core tile runs over N:
+// the MMA computes D^T tiles [128 n][Mp m] (Mp = M rounded up to 16) with B as the M-side operand
+// and A as the N-side operand of tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X.
+// Split-K gives enough work units to stream B from every SM: unit (n-tile, s) covers K range
+// [s * Ks, (s + 1) * Ks) and writes its fp32 partial tile to a workspace.  A second kernel (one
+// thread per output, all S partial loads in flight) sums the partials in split order 0..S-1
+// (fp32, round to nearest) and applies alpha -> bf16.  (Summing in the CTA that finishes a
+// tile's last unit was measured slower: the sum then runs on 56 CTAs at the tail.)
+//
+// Persistent CTAs (one per SM, 320 threads) walk the work units (n-tile, split), split fastest
+// so that the SMs stream neighbouring stretches of B:
+//   warp 0      TMA producer: per 256-K stage one box of B (128 rows x 128 B), one box of A
+//               (Mp rows x 128 B), both SWIZZLE_128B, and the stage's scale atoms of B and A
+//               (2 KB each, bulk copies), on the stage's "full" barrier;
+//   warp 1      MMA issuer: per stage four tcgen05.mma (M128 N=Mp K64), then one commit that
+//               releases the stage; after a unit's last stage a commit to its accumulator buffer;
+//   warps 2-5   epilogue: tcgen05.ld of a finished unit's D^T tile, fp32 partial -> workspace;
+//   warps 6-9   scale warps: the stage's scale atoms shared memory -> registers -> TMEM slot of
+//               the same index (tcgen05.st, lane quadrant warp % 4).  A slot is rewritten only
+//               after its stage was refilled, which the producer does only after the MMAs that
+//               read the slot completed, so the slots need no barrier of their own.
+// TMEM (512 columns): two accumulator buffers at columns [0, 128) and [128, 256); scale slots
+// from column 256, 32 columns per stage: B scales (MMA M side) +0..15, A scales +16..31.
+#include "capi_internal.h"
+#include "nvfp4_common.cuh"
+#include "tma_host.h"
+
+namespace nvfp4 {
+namespace gsmall {
+
+using gemm::desc_sw128;
+
+constexpr int THREADS = 320;
+constexpr int TMEM_COLS = 512;
+constexpr int ACC_COLS = 128;                         // per accumulator buffer (Mp <= 128)
+constexpr int SF_COL0 = 2 * ACC_COLS;
+constexpr int SF_SLOT_COLS = 32;
+constexpr int MAX_STAGES = 8;
+static_assert(SF_COL0 + SF_SLOT_COLS * MAX_STAGES <= TMEM_COLS, "scale slots fit in TMEM");
+constexpr int B_BOX = 128 * 128;                      // 128 rows x 128 B (256 K)
+constexpr int SF_STAGE = 2 * 4 * 512;                 // scale atoms of B and of A for 256 K
+constexpr int SMEM_BUDGET = 200 * 1024;
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
+
+__host__ __device__ constexpr int stage_bytes(int mp) { return B_BOX + mp * 128 + SF_STAGE; }
+__host__ __device__ constexpr int num_stages(int mp) {
+    return SMEM_BUDGET / stage_bytes(mp) < MAX_STAGES ? SMEM_BUDGET / stage_bytes(mp) : MAX_STAGES;
+}
+// [stages][full, empty, sf_full per stage][acc_full 2][acc_empty 2][drain][tmem slot]
+__host__ __device__ constexpr int smem_bytes(int mp) {
+    return 1024 + num_stages(mp) * stage_bytes(mp) + (3 * MAX_STAGES + 5) * 8 + 16;
+}
+
+__device__ __forceinline__ void tc_st_x16(uint32_t taddr, const uint4* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(v[0].x), "r"(v[0].y), "r"(v[0].z), "r"(v[0].w), "r"(v[1].x), "r"(v[1].y), "r"(v[1].z), "r"(v[1].w),
+        "r"(v[2].x), "r"(v[2].y), "r"(v[2].z), "r"(v[2].w), "r"(v[3].x), "r"(v[3].y), "r"(v[3].z), "r"(v[3].w)
+        : "memory");
+}
+__device__ __forceinline__ void tc_ld_x16(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tc_mma_rt(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t sfa,
+                                          uint32_t sfb, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+        : "memory");
+}
+
+// ws[s][m][n] = partial of split s (fp32, the tensor core's accumulation over that K range);
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                  const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, float* __restrict__ ws, int M,
+                  int N, int K, int ks, int mp) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    const uint32_t base = (raw_addr + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (base - raw_addr);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = num_stages(mp), SB = stage_bytes(mp);
+    const int n_tiles = N / 128, splits = K / ks, units = n_tiles * splits;
+    const int katoms = K / 64, nbox = ks / 256;
+    const uint32_t bar0 = base + S * SB;
+    auto full_bar = [&](int st) { return bar0 + 8u * st; };
+    auto empty_bar = [&](int st) { return bar0 + 8u * (MAX_STAGES + st); };
+    auto sf_full = [&](int st) { return bar0 + 8u * (2 * MAX_STAGES + st); };
+    const uint32_t acc_full = bar0 + 8u * (3 * MAX_STAGES), acc_empty = acc_full + 16, drain = acc_full + 32;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S * SB + (3 * MAX_STAGES + 5) * 8);
+    uint32_t* abort_flag = tmem_slot + 1;       // the epilogue warps give up together
+
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmap_a);
+        prefetch_tmap(&tmap_b);
+        for (int st = 0; st < S; st++) {
+            mbar_init(full_bar(st), 1);
+            mbar_init(empty_bar(st), 1);
+            mbar_init(sf_full(st), 4);                 // the four scale warps
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(acc_full + 8 * b, 1);
+            mbar_init(acc_empty + 8 * b, 4);           // the four epilogue warps
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer ----
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            long fills = 0;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+                const int sp = u % splits, nt = u / splits;
+                for (int b = 0; b < nbox; b++) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    const int k = sp * ks + 256 * b;
+                    const uint32_t sbase = base + stage * SB, fb = full_bar(stage);
+                    mbar_arrive_expect_tx(fb, (uint32_t)SB);
+                    tma_load_2d(sbase, &tmap_b, k / 2, nt * 128, fb);
+                    tma_load_2d(sbase + B_BOX, &tmap_a, k / 2, 0, fb);
+                    bulk_load(sbase + B_BOX + mp * 128, sfb + ((int64_t)nt * katoms + k / 64) * 512, 2048, fb);
+                    bulk_load(sbase + B_BOX + mp * 128 + 2048, sfa + (int64_t)(k / 64) * 512, 2048, fb);
+                    fills++;
+                    if (++stage == S) { stage = 0; phase ^= 1u; }
+                }
+            }
+            // Tail: every filled stage is released by an MMA commit before the CTA exits.
+            for (int st = 0; st < S && st < fills && ok; st++)
+                if (!mbar_wait(empty_bar(st), st < stage ? phase : (phase ^ 1u), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_TEARDOWN))
+                    break;
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------------------------------------------------- MMA issuer ----
+        if (lane == 0) {
+            const uint32_t idesc = (1u << 7) | (1u << 10) | ((uint32_t)(mp >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int iter = 0;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x, iter++) {
+                const int buf = iter & 1;
+                if (iter >= 2 &&
+                    !mbar_wait(acc_empty + 8 * buf, (uint32_t)(((iter >> 1) - 1) & 1), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + ACC_COLS * buf;
+                for (int b = 0; b < nbox; b++) {
+                    if (!mbar_wait(full_bar(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA) ||
+                        !mbar_wait(sf_full(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sbase = base + stage * SB;
+                    const uint32_t slot = tmem + SF_COL0 + SF_SLOT_COLS * stage;
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++)
+                        tc_mma_rt(d, desc_sw128(sbase + 32 * kk), desc_sw128(sbase + B_BOX + 32 * kk), idesc,
+                                  slot + 4 * kk, slot + 16 + 4 * kk, (b | kk) != 0);
+                    tc_commit(empty_bar(stage));
+                    if (++stage == S) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                tc_commit(acc_full + 8 * buf);
+            }
+            tc_commit(drain);
+            mbar_wait(drain, 0, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_TEARDOWN);
+        }
+        __syncwarp();
+    } else if (warp >= 6) {
+        // -------------------------------------------------------- scale warps ----
+        const uint32_t lane_base = ((uint32_t)(warp & 3) * 32u) << 16;
+        int stage = 0;
+        uint32_t phase = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x) {
+            bool ok = true;
+            for (int b = 0; b < nbox; b++) {
+                if (!__all_sync(0xFFFFFFFFu, mbar_wait(full_bar(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_SF))) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* sf = smem + stage * SB + B_BOX + mp * 128 + 16 * lane;
+                uint4 vb[4], va[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    vb[j] = *reinterpret_cast<const uint4*>(sf + 512 * j);
+                    va[j] = *reinterpret_cast<const uint4*>(sf + 2048 + 512 * j);
+                }
+                const uint32_t slot = tmem + lane_base + SF_COL0 + SF_SLOT_COLS * stage;
+                tc_st_x16(slot, vb);
+                tc_st_x16(slot + 16, va);
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(sf_full(stage));
+                if (++stage == S) { stage = 0; phase ^= 1u; }
+            }
+            if (!ok) break;
+        }
+    } else {
+        // ----------------------------------------------------------- epilogue ----
+        const uint32_t q = (uint32_t)(warp & 3);
+        const uint32_t lane_base = (q * 32u) << 16;
+        int iter = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, iter++) {
+            const int buf = iter & 1;
+            const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(acc_full + 8 * buf, (uint32_t)((iter >> 1) & 1),
+                                                              WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_EPILOGUE));
+            if (!ok && lane == 0) *abort_flag = 1u;
+            tc_fence_after();
+            const int sp = u % splits, nt = u / splits;
+            const int n = nt * 128 + (int)q * 32 + lane;  // TMEM lane = row n of the D^T tile
+            if (ok) {
+                float* dst = ws + (int64_t)sp * M * N + n;
+                for (int c = 0; c < mp; c += 16) {
+                    uint32_t r[16];
+                    tc_ld_x16(tmem + lane_base + ACC_COLS * buf + c, r);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                    for (int i = 0; i < 16; i++)
+                        if (c + i < M) dst[(int64_t)(c + i) * N] = __uint_as_float(r[i]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(acc_empty + 8 * buf);
+            }
+            named_bar_sync(1, 128);
+            if (*abort_flag) break;                         // every epilogue warp sees the same flag
+        }
+    }
+
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+}
+
+// out[m][n] = bf16(alpha * (((ws[0] + ws[1]) + ws[2]) + ...)) (or the fp32 sum for kOutF32); one
+// thread per output, the partial loads of up to 16 splits issued before the ordered adds.
+template <bool kOutF32>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, void* __restrict__ out,
+                                                            int64_t mn, int splits, float alpha) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < mn; i += (int64_t)gridDim.x * blockDim.x) {
+        float acc = 0.0f;
+        for (int t0 = 0; t0 < splits; t0 += 16) {
+            float v[16];
+#pragma unroll
+            for (int t = 0; t < 16; t++) v[t] = (t0 + t < splits) ? __ldcg(ws + (int64_t)(t0 + t) * mn + i) : 0.0f;
+#pragma unroll
+            for (int t = 0; t < 16; t++)
+                if (t0 + t < splits) acc = __fadd_rn(acc, v[t]);
+        }
+        if constexpr (kOutF32)
+            reinterpret_cast<float*>(out)[i] = acc;
+        else
+            reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(__fmul_rn(acc, alpha));
+    }
+}
+
+// K per split: 512 when it divides K, else 256 (whole stages; enough units to spread over the
+// SMs evenly at decode shapes: N 7168, K 8192 gives 896 units).
+inline int split_k(int64_t K) {
+    if (K % 512 == 0) return 512;
+    if (K % 256 == 0) return 256;
+    return 0;
+}
+
+// Workspace: the fp32 partials [splits][M][N].
+inline size_t workspace_bytes(int64_t M, int64_t N, int64_t K) {
+    const int ks = split_k(K);
+    return ks ? (size_t)(K / ks) * (size_t)M * (size_t)N * sizeof(float) : 0;
+}
+
+template <bool kOutF32>
+nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void* sfb, float alpha, void* D,
+                      int64_t M, int64_t N, int64_t K, void* ws, size_t ws_bytes, cudaStream_t s) {
+    const int ks = split_k(K);
+    if (ks == 0) return fail(NVFP4_ERR_INVALID_ARG, "gemm (small M): K %% 256 != 0");
+    if (N % 128 != 0) return fail(NVFP4_ERR_INVALID_ARG, "gemm (small M): N %% 128 != 0");
+    if (ws_bytes < workspace_bytes(M, N, K))
+        return fail(NVFP4_ERR_INVALID_ARG, "gemm (small M): workspace of %zu bytes, need %zu", ws_bytes,
+                    workspace_bytes(M, N, K));
+    const int mp = (int)((M + 15) / 16 * 16);
+    const int splits = (int)(K / ks);
+    CUtensorMap ta, tb;
+    nvfp4_status_t st;
+    if ((st = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, M, K / 2, 128, mp, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+    if ((st = make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+    const int smem = smem_bytes(mp);
+    // the attribute is set once per device, to the largest footprint of any Mp
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        int most = 0;
+        for (int m = 16; m <= 128; m += 16)
+            if (smem_bytes(m) > most) most = smem_bytes(m);
+        cudaError_t e = cudaFuncSetAttribute(gemm_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+        if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "gemm (small M): smem attribute: %s", cudaGetErrorString(e));
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    const int units = (int)(N / 128) * splits;
+    const int grid = units < sm_count() ? units : sm_count();
+    float* w = reinterpret_cast<float*>(ws);
+    gemm_small_kernel<<<grid, THREADS, smem, s>>>(ta, tb, reinterpret_cast<const uint8_t*>(sfa),
+                                                  reinterpret_cast<const uint8_t*>(sfb), w, (int)M, (int)N, (int)K, ks, mp);
+    if ((st = check_launch("gemm_small_kernel"))) return st;
+    const int64_t mn = M * N;
+    int64_t rg = (mn + 255) / 256;
+    const int64_t cap = (int64_t)sm_count() * 8;
+    if (rg > cap) rg = cap;
+    splitk_reduce_kernel<kOutF32><<<(unsigned)rg, 256, 0, s>>>(w, D, mn, splits, alpha);
+    return check_launch("splitk_reduce_kernel");
+}
+
+}  // namespace gsmall
+}  // namespace nvfp4

@@ -5,6 +5,7 @@
 #include "quantize_noalloc.cu"
 #include "gemm.cu"
 #include "gemm_2sm.cu"
+#include "gemm_small.cu"
 #include "gemm_api.cu"
 #include "diag_mma.cu"
 #include "allreduce.cu"

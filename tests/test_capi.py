@@ -73,8 +73,12 @@ def test_argument_checks_reject_before_launch(nv):
     unaligned = ctypes.c_void_p((1 << 20) + 4)
     msg = _err(nv, L.nvfp4_quantize_bf16(unaligned, 128, 128, ctypes.c_float(1.0), fake, fake, None))
     assert "aligned" in msg
-    msg = _err(nv, L.nvfp4_gemm_bf16(fake, fake, fake, fake, ctypes.c_float(1.0), fake, 100, 256, 256, None))
+    msg = _err(nv, L.nvfp4_gemm_bf16(fake, fake, fake, fake, ctypes.c_float(1.0), fake, 200, 256, 256, None))
     assert "M % 128" in msg
+    msg = _err(nv, L.nvfp4_gemm_bf16(fake, fake, fake, fake, ctypes.c_float(1.0), fake, 16, 200, 256, None))
+    assert "N % 128" in msg
+    msg = _err(nv, L.nvfp4_gemm_bf16_ws(fake, fake, fake, fake, ctypes.c_float(1.0), fake, 16, 256, 256, None, 0, None))
+    assert "workspace" in msg
     msg = _err(nv, L.nvfp4_gemm_f32(fake, fake, fake, fake, fake, 128, 256, 100, None))
     assert "K % 256" in msg
     msg = _err(nv, L.nvfp4_amax_bf16(fake, 7, fake, None))

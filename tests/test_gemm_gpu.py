@@ -8,6 +8,7 @@
     spot-checked bit-exact at the full 8192^3 size, with the relative error against an
     fp32 matmul of the dequantized operands also bounded.
 """
+import ctypes
 import os
 import subprocess
 
@@ -135,3 +136,55 @@ def dequant_f32(oracle, packed, sf, rows, cols, gs):
     offs = torch.from_numpy(oracle.sf_offsets(rows, cols)).cuda()
     bs = e4m3[sf.long()[offs]] * torch.tensor(gs, dtype=torch.float32, device="cuda")
     return e2m1[codes] * bs.repeat_interleave(16, dim=1)
+
+
+def split_size(K):
+    """K per split of the small-M kernel: the largest of 1024 / 512 / 256 dividing K."""
+    for ks in (1024, 512, 256):
+        if K % ks == 0:
+            return ks
+    raise ValueError(K)
+
+
+@pytest.mark.parametrize("M,N,K", [(16, 256, 256), (16, 384, 2048), (1, 128, 512), (48, 256, 768),
+                                   (100, 640, 4096), (32, 128, 8192)])
+def test_gemm_small_m_bitexact(nv, oracle, M, N, K):
+    """Decode shapes (M < 128): split-K over 128-row tiles of B, partials summed in split order."""
+    pa, sa, pb, sb, gsa, gsb = quantized_operands(nv, oracle, M, N, K, seed=7 * M + N + K)
+    alpha = float(np.float32(gsa) * np.float32(gsb))
+    D = nv.gemm(pa, sa, pb, sb, M, N, K, alpha=alpha)
+    Df = nv.gemm_f32(pa, sa, pb, sb, M, N, K)
+    torch.cuda.synchronize()
+    assert nv.device_status() == 0
+    acc = oracle.gemm_splitk_f32(pa.cpu().numpy(), sa.cpu().numpy(), pb.cpu().numpy(), sb.cpu().numpy(),
+                                 M, N, K, split_size(K))
+    assert np.array_equal(Df.cpu().numpy().view(np.uint32), acc.view(np.uint32))
+    want = oracle.gemm_epilogue_bf16(acc, alpha)
+    got = D.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    assert np.count_nonzero(got != want) == 0
+    # a single split (K <= 1024) is exactly the tiled kernels' arithmetic
+    if K <= 1024:
+        ref = oracle.gemm_f32(pa.cpu().numpy(), sa.cpu().numpy(), pb.cpu().numpy(), sb.cpu().numpy(), M, N, K,
+                              model=MODEL)
+        assert np.array_equal(ref.view(np.uint32), acc.view(np.uint32))
+
+
+def test_gemm_decode_cfg3_full_size(nv, oracle):
+    """cfg3 decode shape M16 N7168 K8192, bit-exact everywhere against the split-K model, and the
+    caller-workspace entry point gives the same bytes."""
+    M, N, K = workloads.CFG3_DECODE_SHAPE
+    pa, sa, pb, sb, gsa, gsb = quantized_operands(nv, oracle, M, N, K, seed=11)
+    alpha = float(np.float32(gsa) * np.float32(gsb))
+    D = nv.gemm(pa, sa, pb, sb, M, N, K, alpha=alpha)
+    ws = torch.empty(int(nv.lib().nvfp4_gemm_workspace_bytes(M, N, K)), dtype=torch.uint8, device="cuda")
+    D2 = torch.empty_like(D)
+    nv.check(nv.lib().nvfp4_gemm_bf16_ws(nv._ptr(pa), nv._ptr(sa), nv._ptr(pb), nv._ptr(sb), ctypes.c_float(alpha),
+                                         nv._ptr(D2), M, N, K, nv._ptr(ws), ws.numel(), nv._stream()))
+    torch.cuda.synchronize()
+    assert nv.device_status() == 0
+    acc = oracle.gemm_splitk_f32(pa.cpu().numpy(), sa.cpu().numpy(), pb.cpu().numpy(), sb.cpu().numpy(),
+                                 M, N, K, split_size(K))
+    want = oracle.gemm_epilogue_bf16(acc, alpha)
+    got = D.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    assert np.count_nonzero(got != want) == 0
+    assert torch.equal(D, D2)
