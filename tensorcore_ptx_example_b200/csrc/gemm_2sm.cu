@@ -7,26 +7,34 @@
 //   memory, completing on a barrier of its own CTA.  The pair MMA reads both B halves, so each SM
 //   moves 38 KB per 128x256x256 block instead of the 54 KB of a single-CTA 128x256 tile.  No
 //   load uses multicast.
-//   Warp roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer (leader CTA), warps 2-5
-//   epilogue, warps 6-9 scale warps.  The scale warps (one per TMEM lane quadrant, in both
-//   CTAs) move the scale atoms shared memory -> registers -> TMEM with tcgen05.st into a ring of
-//   TMEM slots and hand each slot to the MMA warp through the leader's "sf_full" barrier.  The
-//   MMA warp issues four tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X
-//   (M256 N256 K64) per stage and releases the stage (shared memory and scale slot) in both
-//   CTAs with one tcgen05.commit carrying a CTA mask.
+//   Warp roles (448 threads): warp 0 TMA producer, warp 1 MMA issuer (leader CTA), warps 2-5
+//   epilogue, warps 6-13 scale warps in two sets of four (one per TMEM lane quadrant; set k takes
+//   the stages g with g % 2 == k).  The scale warps move the scale atoms shared memory ->
+//   registers -> TMEM with tcgen05.st into a ring of TMEM slots and then arrive (in both CTAs)
+//   on the leader's "full" barrier of the stage, which therefore completes when A/B have landed
+//   AND the scales are in TMEM: the MMA thread makes one wait per stage.  It issues four
+//   tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X (M256 N256 K64) per stage
+//   and releases the stage (shared memory and scale slot) in both CTAs with one tcgen05.commit
+//   carrying a CTA mask.
+//   Measured on B200 (probes of the MMA-issuing thread, M256 N256 K64 MMAs): an mbarrier wait in
+//   that thread costs tensor-pipe time even when the phase completed long ago -- with 4 MMAs per
+//   wait, try_wait runs the pipe at ~5.7 PFLOP/s and test_wait at ~6.8, against 8.1 without
+//   waits; with 8 MMAs per wait the loss is gone.  Hence one wait per stage, polled with
+//   test_wait.  The commit itself costs nothing.
 //   Scales do not go through tcgen05.cp: tcgen05 operations execute in issue order in the
 //   tensor pipe, so a copy issued by the MMA thread waits for every MMA queued before it and
 //   drains the pipe, and copies from another thread still occupy the pipe (measured on B200:
 //   3.3 PFLOP/s with 12 copies per stage in the MMA thread, 1.9 from a separate thread, 8.2 with
-//   tcgen05.st from other warps).
+//   tcgen05.st from other warps).  A scale slot must not be rewritten while MMAs that read it
+//   can still run: the scale warps wait for the MMA commit of the stage that last used it.
 //   Before exiting, every CTA waits until all of its stages have been released and the leader
 //   waits for the epilogues' last arrival, so no completion signal targets an exited CTA.
 //
-// TMEM (512 columns per CTA): accumulator buffer 0 = columns [0, 256), buffer 1 = [128, 384)
-// (the two overlap in [128, 256)); scale-factor ring from column 384: slots of one stage,
+// TMEM (512 columns per CTA): accumulator buffer 0 = columns [0, 256), buffer 1 = [64, 320)
+// (the two overlap in [64, 256)); scale-factor ring from column 320: 4 slots of one stage,
 // 48 columns each (per K step: SFA 4 columns, SFB 8 columns).  Tiles alternate accumulator
-// buffers.  The epilogue drains the overlapping 128 columns of a tile first and then signals the
-// leader, so the next tile's MMAs start after half of the drain instead of all of it.
+// buffers.  The epilogue drains the overlapping columns of a tile first and then signals the
+// leader, so the next tile's MMAs start before the drain has finished.
 //
 // Epilogue (warps 2..5 of both CTAs): tcgen05.ld 32x32b -> alpha * acc -> bf16 -> swizzled
 // shared-memory staging (2 x 16 KB) -> 2D TMA store, double buffered.
@@ -51,17 +59,22 @@ constexpr int SFA_BYTES = 4 * 512;                    // 2 KB: scale atoms of th
 constexpr int SFB_BYTES = 2 * 4 * 512;                // 4 KB: scale atoms of all 256 B rows
 constexpr int AB_BYTES = A_BYTES + B_BYTES;
 constexpr int EPI_BYTES = 128 * 128;                  // one staging buffer: 128 rows x 128 bytes
-constexpr int NUM_THREADS = 320;                      // 10 warps: TMA, MMA, 4 epilogue, 4 scale
+// Two sets of four scale warps (one warp per TMEM lane quadrant in each); set k handles the
+// stages g with g % 2 == k, so each set has two stages of time for its loads and stores.
+constexpr int SFW_SETS = 2;
+constexpr int NUM_THREADS = 192 + 128 * SFW_SETS;     // TMA, MMA, 4 epilogue, 8 scale warps
 constexpr int TMEM_COLS = 512;
 #ifndef GEMM2_ACC1_COL
-#define GEMM2_ACC1_COL 128
+#define GEMM2_ACC1_COL 64
 #endif
 constexpr int ACC1_COL = GEMM2_ACC1_COL;
 constexpr int OVL_COLS = 256 - ACC1_COL;              // columns shared by the two accumulator buffers
 constexpr int SF_RING_COL = ACC1_COL + 256;
 constexpr int SF_SLOT_COLS = 48;                      // one stage: 4 K steps x (SFA 4 + SFB 8 columns)
 constexpr int SF_SLOTS = (TMEM_COLS - SF_RING_COL) / SF_SLOT_COLS;
-static_assert(SF_SLOTS >= 2 && SF_SLOTS <= STAGES, "scale ring: at least two slots, no more than the stages");
+static_assert(SF_SLOTS >= 2 && SF_SLOTS < STAGES, "scale ring: at least two slots, fewer than the stages");
+// A scale-warp set may run up to SF_SLOTS stages ahead of the MMAs; its parity waits on the
+// per-stage scale buffers (STAGES of them) stay unambiguous only if SF_SLOTS < STAGES.
 static_assert(SF_RING_COL >= ACC1_COL + 256, "scale ring clear of the accumulators");
 static_assert(SF_RING_COL + SF_SLOT_COLS * SF_SLOTS <= TMEM_COLS, "scale ring fits in TMEM");
 
@@ -71,8 +84,8 @@ constexpr int OFF_SFA = OFF_B + STAGES * B_BYTES;
 constexpr int OFF_SFB = OFF_SFA + STAGES * SFA_BYTES;
 constexpr int OFF_EPI = OFF_SFB + STAGES * SFB_BYTES;
 constexpr int OFF_BAR = OFF_EPI + 2 * EPI_BYTES;
-// full, empty, tmem_full, tmem_empty, drain, sf_full, sf_landed
-constexpr int NUM_BARS = 2 * STAGES + 3 + SF_SLOTS + STAGES;
+// full, empty, tmem_full, tmem_empty, drain, sf_landed
+constexpr int NUM_BARS = 2 * STAGES + 3 + STAGES;
 constexpr int OFF_TMEM_PTR = OFF_BAR + NUM_BARS * 8;
 constexpr int SMEM_BYTES = 1024 + OFF_TMEM_PTR + 16;
 static_assert(OFF_EPI % 1024 == 0, "staging buffers must be 1024-byte aligned");
@@ -189,8 +202,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
     const uint32_t tmem_full = bar0 + 8u * (2 * STAGES);
     const uint32_t tmem_empty = tmem_full + 8u;
     const uint32_t drain_bar = tmem_full + 16u;
-    auto sf_full = [&](int k) { return drain_bar + 8u + 8u * k; };
-    auto sf_landed = [&](int st) { return drain_bar + 8u + 8u * (SF_SLOTS + st); };
+    auto sf_landed = [&](int st) { return drain_bar + 8u + 8u * st; };
     uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + OFF_TMEM_PTR);
     volatile uint32_t* abort_flag = tmem_ptr + 1;
 
@@ -206,14 +218,15 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
         prefetch_tmap(&tmap_sfb);
         prefetch_tmap(&tmap_d);
         for (int s = 0; s < STAGES; s++) {
-            mbar_init(full_bar(s), 1);
+            // the leader's producer (arrive.expect_tx, A/B bytes of both CTAs) and the 4 scale
+            // warps of each CTA (the stage's scale slot is in TMEM)
+            mbar_init(full_bar(s), 1 + 8);
             mbar_init(empty_bar(s), 1);
         }
         mbar_init(tmem_full, 1);
         mbar_init(tmem_empty, 8);                      // one elected lane of 4 epilogue warps x 2 CTAs
         mbar_init(drain_bar, 1);
         *abort_flag = 0u;
-        for (int k = 0; k < SF_SLOTS; k++) mbar_init(sf_full(k), 8);   // 4 scale warps x 2 CTAs
         for (int st = 0; st < STAGES; st++) mbar_init(sf_landed(st), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -288,18 +301,19 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
             bool ok = true;
             int iter = 0;
             int sf_slot = 0;
-            uint32_t sf_phase = 0;
             for (int tile = pair; tile < ntiles && ok; tile += npairs, iter++) {
                 if (iter > 0 &&
-                    !PROF_WAIT(2, mbar_wait(tmem_empty, (uint32_t)((iter - 1) & 1), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA))) {
+                    !PROF_WAIT(2, mbar_wait_spin(tmem_empty, (uint32_t)((iter - 1) & 1), WAIT_LIMIT_NS,
+                                                 DEV_TIMEOUT_GEMM_MMA))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t dcol = (iter & 1) ? ACC1_COL : 0;
                 for (int kb = 0; kb < nkb; kb++) {
-                    if (!PROF_WAIT(0, mbar_wait(full_bar(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA)) ||
-                        !PROF_WAIT(1, mbar_wait(sf_full(sf_slot), sf_phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA))) {
+                    // A/B of the stage have landed and its scales are in TMEM.  One wait per
+                    // stage: each wait in this thread costs tensor-pipe time.
+                    if (!PROF_WAIT(0, mbar_wait_spin(full_bar(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA))) {
                         ok = false;
                         break;
                     }
@@ -313,7 +327,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                                 scol + 12 * j + 4, (kb | j) != 0);
                     // releases the stage's shared memory (producer) and its scale slot (scale warps)
                     tc_commit2_pair(empty_bar(stage));
-                    if (++sf_slot == SF_SLOTS) { sf_slot = 0; sf_phase ^= 1u; }
+                    if (++sf_slot == SF_SLOTS) sf_slot = 0;
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
                 if (!ok) break;
@@ -337,8 +351,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
         // One slot holds one stage (4 K steps).  Slot reuse: global stage g writes the slot
         // that stage g - SF_SLOTS used; the MMA commit that releases that stage's shared memory
         // (empty_bar) also marks its scale slot free.
-        const uint32_t q = (uint32_t)(warp & 3);
+        const uint32_t q = (uint32_t)(warp & 3);          // TMEM lane quadrant of this warp
         const uint32_t lane_base = (q * 32u) << 16;
+        const int set = (warp - 6) >> 2;
         int stage = 0;
         uint32_t phase = 0;
         int sf_slot = 0;
@@ -346,6 +361,11 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
         long g = 0;
         for (int tile = pair; tile < ntiles && ok; tile += npairs) {
             for (int kb = 0; kb < nkb; kb++, g++) {
+                if ((int)(g % SFW_SETS) != set) {                // the other set's stage
+                    if (++sf_slot == SF_SLOTS) sf_slot = 0;
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                    continue;
+                }
                 // Every lane waits (each must observe the phase before reading the atoms); the
                 // outcome is made warp-uniform before the .sync.aligned TMEM stores.
                 bool w = true;
@@ -384,8 +404,8 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                 // before this arrival, so a relaxed arrival hands the slot over.  A release at
                 // cluster scope costs ~1300 cycles per arrival here (measured), more than a stage.
                 if (lane == 0) {
-                    if (leader) mbar_arrive_relaxed(sf_full(sf_slot));
-                    else mbar_arrive_remote_relaxed(mapa(sf_full(sf_slot), 0));
+                    if (leader) mbar_arrive_relaxed(full_bar(stage));
+                    else mbar_arrive_remote_relaxed(mapa(full_bar(stage), 0));
                 }
                 if (++sf_slot == SF_SLOTS) sf_slot = 0;
                 if (++stage == STAGES) { stage = 0; phase ^= 1u; }

@@ -188,6 +188,13 @@ __device__ __forceinline__ void st_v4(void* p, uint4 v) {
                  : "memory");
 }
 
+// 32-byte global store (sm_100: .v8 of 32-bit elements); p must be 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t* v) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]), "r"(v[1]),
+                 "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+
 // --------------------------------------------------------------- mbarrier ----
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
@@ -224,6 +231,40 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_
 #pragma unroll 1
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > limit_ns) {
+            record_error(err);
+            return false;
+        }
+    }
+}
+
+// Non-blocking probe of a phase (mbarrier.test_wait never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// mbar_wait for a thread that issues tcgen05.mma: polls with test_wait.  On B200 a try_wait in
+// the MMA-issuing thread costs ~240 cycles of tensor-pipe time per call even when the phase has
+// long completed, a test_wait ~110 (measured with 4 MMAs per wait).
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, uint64_t limit_ns,
+                                               unsigned int err) {
+#pragma unroll 1
+    for (int i = 0; i < 4096; i++)
+        if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+    while (true) {
+#pragma unroll 1
+        for (int i = 0; i < 64; i++)
+            if (mbar_test_wait(bar, parity)) return true;
         if (globaltimer_ns() - t0 > limit_ns) {
             record_error(err);
             return false;
