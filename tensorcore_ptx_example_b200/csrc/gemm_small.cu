@@ -7,25 +7,35 @@
 // the MMA computes D^T tiles [128 n][Mp m] (Mp = M rounded up to 16) with B as the M-side operand
 // and A as the N-side operand of tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X.
 // Split-K gives enough work units to stream B from every SM: unit (n-tile, s) covers K range
-// [s * Ks, (s + 1) * Ks) and writes its fp32 partial tile to a workspace.  A second kernel (one
-// thread per output, all S partial loads in flight) sums the partials in split order 0..S-1
-// (fp32, round to nearest) and applies alpha -> bf16.  (Summing in the CTA that finishes a
-// tile's last unit was measured slower: the sum then runs on 56 CTAs at the tail.)
+// [s * Ks, (s + 1) * Ks) and writes its fp32 partial tile to a workspace.  A second kernel (four
+// outputs per thread, all S partial loads in flight) sums the partials in split order 0..S-1
+// (fp32, round to nearest) and applies alpha -> bf16.  Both kernels are programmatic dependent
+// launches: the GEMM's set-up overlaps the previous kernel and the reduction is resident and
+// waiting when the GEMM finishes.  (Summing in the CTA that finishes a tile's last unit was
+// measured slower: the sum then runs on 56 CTAs at the tail.)
 //
-// Persistent CTAs (one per SM, 320 threads) walk the work units (n-tile, split), split fastest
-// so that the SMs stream neighbouring stretches of B:
-//   warp 0      TMA producer: per 256-K stage one box of B (128 rows x 128 B), one box of A
-//               (Mp rows x 128 B), both SWIZZLE_128B, and the stage's scale atoms of B and A
-//               (2 KB each, bulk copies), on the stage's "full" barrier;
-//   warp 1      MMA issuer: per stage four tcgen05.mma (M128 N=Mp K64), then one commit that
-//               releases the stage; after a unit's last stage a commit to its accumulator buffer;
+// Persistent CTAs walk the work units (n-tile, split), split fastest so that the SMs stream
+// neighbouring stretches of B.  For Mp <= 64 two CTAs share an SM (about 100 KB of shared memory
+// and 256 TMEM columns each: two independent pipelines per SM); the grid is the largest one that
+// divides the units evenly (cfg3 decode: 448 units on 224 CTAs).
+//   warp 0      TMA producer: per 256-K stage the scale atoms of B and A (2 KB each, bulk copies)
+//               on the stage's "sf_landed" barrier, then one box of B (128 rows x 128 B) and one
+//               box of A (Mp rows x 128 B), both SWIZZLE_128B, on its "full" barrier;
+//   warp 1      MMA issuer: per stage one wait on "full" (polled with test_wait), four
+//               tcgen05.mma (M128 N=Mp K64), then one commit that releases the stage; after a
+//               unit's last stage a commit to its accumulator buffer;
 //   warps 2-5   epilogue: tcgen05.ld of a finished unit's D^T tile, fp32 partial -> workspace;
 //   warps 6-9   scale warps: the stage's scale atoms shared memory -> registers -> TMEM slot of
-//               the same index (tcgen05.st, lane quadrant warp % 4).  A slot is rewritten only
-//               after its stage was refilled, which the producer does only after the MMAs that
-//               read the slot completed, so the slots need no barrier of their own.
-// TMEM (512 columns): two accumulator buffers at columns [0, 128) and [128, 256); scale slots
-// from column 256, 32 columns per stage: B scales (MMA M side) +0..15, A scales +16..31.
+//               the same index (tcgen05.st, lane quadrant warp % 4), then an arrival on the
+//               stage's "full" barrier, which therefore completes only when the scales are in
+//               TMEM too.  A slot is rewritten only after its stage was refilled, which the
+//               producer does only after the MMAs that read the slot completed.
+// TMEM: two accumulator buffers of Mp columns at [0, Mp) and [Mp, 2 Mp), then one 32-column scale
+// slot per stage (B scales +0..15, A scales +16..31); the allocation is the next power of two.
+//
+// Timeline at cfg3 (M16 N7168 K8192, 224 CTAs, measured with global timestamps): CTA starts spread
+// over 0.9 us, set-up 0.8 us, first stage lands 2 us later, the stream of B then runs at
+// ~6.6 TB/s for ~5 us, the last CTA exits at ~8.5 us and the reduction ends at ~11.5 us.
 #include "capi_internal.h"
 #include "nvfp4_common.cuh"
 #include "tma_host.h"
@@ -36,22 +46,41 @@ namespace gsmall {
 using gemm::desc_sw128;
 
 constexpr int THREADS = 320;
-constexpr int TMEM_COLS = 512;
-constexpr int ACC_COLS = 128;                         // per accumulator buffer (Mp <= 128)
-constexpr int SF_COL0 = 2 * ACC_COLS;
 constexpr int SF_SLOT_COLS = 32;
 constexpr int MAX_STAGES = 8;
-static_assert(SF_COL0 + SF_SLOT_COLS * MAX_STAGES <= TMEM_COLS, "scale slots fit in TMEM");
 constexpr int B_BOX = 128 * 128;                      // 128 rows x 128 B (256 K)
 constexpr int SF_STAGE = 2 * 4 * 512;                 // scale atoms of B and of A for 256 K
-constexpr int SMEM_BUDGET = 200 * 1024;
+// Shared-memory budget of one CTA: 200 KB with one CTA per SM; ~100 KB when two CTAs share an SM
+// (Mp <= 64, where the TMEM layout below fits in 256 columns), giving each SM two independent
+// load/MMA pipelines.
+#ifndef GSMALL_CTAS_PER_SM
+#define GSMALL_CTAS_PER_SM 2
+#endif
+constexpr int SMEM_BUDGET_1 = 200 * 1024;
+constexpr int SMEM_BUDGET_2 = 100 * 1024;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 
 __host__ __device__ constexpr int stage_bytes(int mp) { return B_BOX + mp * 128 + SF_STAGE; }
+__host__ __device__ constexpr int ctas_per_sm(int mp) { return (GSMALL_CTAS_PER_SM == 2 && mp <= 64) ? 2 : 1; }
 __host__ __device__ constexpr int num_stages(int mp) {
-    return SMEM_BUDGET / stage_bytes(mp) < MAX_STAGES ? SMEM_BUDGET / stage_bytes(mp) : MAX_STAGES;
+    return (ctas_per_sm(mp) == 2 ? SMEM_BUDGET_2 : SMEM_BUDGET_1) / stage_bytes(mp) < MAX_STAGES
+               ? (ctas_per_sm(mp) == 2 ? SMEM_BUDGET_2 : SMEM_BUDGET_1) / stage_bytes(mp)
+               : MAX_STAGES;
 }
-// [stages][full, empty, sf_full per stage][acc_full 2][acc_empty 2][drain][tmem slot]
+// TMEM: accumulator buffers [0, mp) and [mp, 2 mp) (fp32 D^T tile, one column per output
+// column), then one 32-column scale slot per stage; the allocation is the next power of two.
+__host__ __device__ constexpr int sf_col0(int mp) { return (2 * mp + 31) / 32 * 32; }
+__host__ __device__ constexpr int tmem_cols(int mp) {
+    return sf_col0(mp) + SF_SLOT_COLS * num_stages(mp) <= 32    ? 32
+           : sf_col0(mp) + SF_SLOT_COLS * num_stages(mp) <= 64  ? 64
+           : sf_col0(mp) + SF_SLOT_COLS * num_stages(mp) <= 128 ? 128
+           : sf_col0(mp) + SF_SLOT_COLS * num_stages(mp) <= 256 ? 256
+                                                                 : 512;
+}
+static_assert(sf_col0(128) + SF_SLOT_COLS * MAX_STAGES <= 512, "scale slots fit in TMEM");
+static_assert(ctas_per_sm(64) == 1 || (tmem_cols(64) <= 256 && tmem_cols(16) <= 256),
+              "two CTAs per SM share the 512 TMEM columns");
+// [stages][full, empty, sf_landed per stage][acc_full 2][acc_empty 2][drain][tmem slot]
 __host__ __device__ constexpr int smem_bytes(int mp) {
     return 1024 + num_stages(mp) * stage_bytes(mp) + (3 * MAX_STAGES + 5) * 8 + 16;
 }
@@ -98,7 +127,8 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
     const uint32_t bar0 = base + S * SB;
     auto full_bar = [&](int st) { return bar0 + 8u * st; };
     auto empty_bar = [&](int st) { return bar0 + 8u * (MAX_STAGES + st); };
-    auto sf_full = [&](int st) { return bar0 + 8u * (2 * MAX_STAGES + st); };
+    auto sf_landed = [&](int st) { return bar0 + 8u * (2 * MAX_STAGES + st); };
+    const int acc_cols = mp, sf0 = sf_col0(mp), tcols = tmem_cols(mp);
     const uint32_t acc_full = bar0 + 8u * (3 * MAX_STAGES), acc_empty = acc_full + 16, drain = acc_full + 32;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S * SB + (3 * MAX_STAGES + 5) * 8);
     uint32_t* abort_flag = tmem_slot + 1;       // the epilogue warps give up together
@@ -107,9 +137,9 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
         prefetch_tmap(&tmap_a);
         prefetch_tmap(&tmap_b);
         for (int st = 0; st < S; st++) {
-            mbar_init(full_bar(st), 1);
+            mbar_init(full_bar(st), 1 + 4);            // producer (B/A bytes) + the four scale warps
             mbar_init(empty_bar(st), 1);
-            mbar_init(sf_full(st), 4);                 // the four scale warps
+            mbar_init(sf_landed(st), 1);               // producer (scale bytes)
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(acc_full + 8 * b, 1);
@@ -122,13 +152,18 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(TMEM_COLS));
+                     "r"(tcols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
         tc_fence_before();
     }
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Programmatic dependent launch: the set-up above overlapped the previous kernel in the
+    // stream; its results are visible after this wait.  The split-K reduction may launch now
+    // (it waits for this grid in turn).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer ----
@@ -145,12 +180,14 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
                         break;
                     }
                     const int k = sp * ks + 256 * b;
-                    const uint32_t sbase = base + stage * SB, fb = full_bar(stage);
-                    mbar_arrive_expect_tx(fb, (uint32_t)SB);
+                    const uint32_t sbase = base + stage * SB, fb = full_bar(stage), lb = sf_landed(stage);
+                    // scales first (the scale warps move them on to TMEM), then B and A
+                    mbar_arrive_expect_tx(lb, (uint32_t)SF_STAGE);
+                    bulk_load(sbase + B_BOX + mp * 128, sfb + ((int64_t)nt * katoms + k / 64) * 512, 2048, lb);
+                    bulk_load(sbase + B_BOX + mp * 128 + 2048, sfa + (int64_t)(k / 64) * 512, 2048, lb);
+                    mbar_arrive_expect_tx(fb, (uint32_t)(B_BOX + mp * 128));
                     tma_load_2d(sbase, &tmap_b, k / 2, nt * 128, fb);
                     tma_load_2d(sbase + B_BOX, &tmap_a, k / 2, 0, fb);
-                    bulk_load(sbase + B_BOX + mp * 128, sfb + ((int64_t)nt * katoms + k / 64) * 512, 2048, fb);
-                    bulk_load(sbase + B_BOX + mp * 128 + 2048, sfa + (int64_t)(k / 64) * 512, 2048, fb);
                     fills++;
                     if (++stage == S) { stage = 0; phase ^= 1u; }
                 }
@@ -177,16 +214,16 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d = tmem + ACC_COLS * buf;
+                const uint32_t d = tmem + acc_cols * buf;
                 for (int b = 0; b < nbox; b++) {
-                    if (!mbar_wait(full_bar(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA) ||
-                        !mbar_wait(sf_full(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA)) {
+                    // B/A landed and the scale warps have put the stage's scales in TMEM
+                    if (!mbar_wait_spin(full_bar(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint32_t sbase = base + stage * SB;
-                    const uint32_t slot = tmem + SF_COL0 + SF_SLOT_COLS * stage;
+                    const uint32_t slot = tmem + sf0 + SF_SLOT_COLS * stage;
 #pragma unroll
                     for (int kk = 0; kk < 4; kk++)
                         tc_mma_rt(d, desc_sw128(sbase + 32 * kk), desc_sw128(sbase + B_BOX + 32 * kk), idesc,
@@ -209,7 +246,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
         for (int u = blockIdx.x; u < units; u += gridDim.x) {
             bool ok = true;
             for (int b = 0; b < nbox; b++) {
-                if (!__all_sync(0xFFFFFFFFu, mbar_wait(full_bar(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_SF))) {
+                if (!__all_sync(0xFFFFFFFFu, mbar_wait(sf_landed(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_SF))) {
                     ok = false;
                     break;
                 }
@@ -220,13 +257,13 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
                     vb[j] = *reinterpret_cast<const uint4*>(sf + 512 * j);
                     va[j] = *reinterpret_cast<const uint4*>(sf + 2048 + 512 * j);
                 }
-                const uint32_t slot = tmem + lane_base + SF_COL0 + SF_SLOT_COLS * stage;
+                const uint32_t slot = tmem + lane_base + sf0 + SF_SLOT_COLS * stage;
                 tc_st_x16(slot, vb);
                 tc_st_x16(slot + 16, va);
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(sf_full(stage));
+                if (lane == 0) mbar_arrive(full_bar(stage));
                 if (++stage == S) { stage = 0; phase ^= 1u; }
             }
             if (!ok) break;
@@ -248,7 +285,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
                 float* dst = ws + (int64_t)sp * M * N + n;
                 for (int c = 0; c < mp; c += 16) {
                     uint32_t r[16];
-                    tc_ld_x16(tmem + lane_base + ACC_COLS * buf + c, r);
+                    tc_ld_x16(tmem + lane_base + acc_cols * buf + c, r);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
                     for (int i = 0; i < 16; i++)
@@ -267,37 +304,72 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols));
 }
 
-// out[m][n] = bf16(alpha * (((ws[0] + ws[1]) + ws[2]) + ...)) (or the fp32 sum for kOutF32); one
-// thread per output, the partial loads of up to 16 splits issued before the ordered adds.
+// out[m][n] = bf16(alpha * (((ws[0] + ws[1]) + ws[2]) + ...)) (or the fp32 sum for kOutF32); four
+// consecutive outputs per thread (16-byte loads; M*N is a multiple of 128), the partial loads of
+// up to 16 splits issued before the ordered adds.
 template <bool kOutF32>
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, void* __restrict__ out,
                                                             int64_t mn, int splits, float alpha) {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < mn; i += (int64_t)gridDim.x * blockDim.x) {
-        float acc = 0.0f;
+    asm volatile("griddepcontrol.wait;" ::: "memory");      // the partials of the GEMM kernel
+    const int64_t mn4 = mn / 4;
+    const float4* w4 = reinterpret_cast<const float4*>(ws);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < mn4; i += (int64_t)gridDim.x * blockDim.x) {
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
         for (int t0 = 0; t0 < splits; t0 += 16) {
-            float v[16];
-#pragma unroll
-            for (int t = 0; t < 16; t++) v[t] = (t0 + t < splits) ? __ldcg(ws + (int64_t)(t0 + t) * mn + i) : 0.0f;
+            float4 v[16];
 #pragma unroll
             for (int t = 0; t < 16; t++)
-                if (t0 + t < splits) acc = __fadd_rn(acc, v[t]);
+                v[t] = (t0 + t < splits) ? __ldcg(w4 + (int64_t)(t0 + t) * mn4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int t = 0; t < 16; t++)
+                if (t0 + t < splits) {
+                    a0 = __fadd_rn(a0, v[t].x);
+                    a1 = __fadd_rn(a1, v[t].y);
+                    a2 = __fadd_rn(a2, v[t].z);
+                    a3 = __fadd_rn(a3, v[t].w);
+                }
         }
-        if constexpr (kOutF32)
-            reinterpret_cast<float*>(out)[i] = acc;
-        else
-            reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(__fmul_rn(acc, alpha));
+        if constexpr (kOutF32) {
+            reinterpret_cast<float4*>(out)[i] = make_float4(a0, a1, a2, a3);
+        } else {
+            const __nv_bfloat162 lo = __floats2bfloat162_rn(__fmul_rn(a0, alpha), __fmul_rn(a1, alpha));
+            const __nv_bfloat162 hi = __floats2bfloat162_rn(__fmul_rn(a2, alpha), __fmul_rn(a3, alpha));
+            uint2 o;
+            o.x = *reinterpret_cast<const uint32_t*>(&lo);
+            o.y = *reinterpret_cast<const uint32_t*>(&hi);
+            reinterpret_cast<uint2*>(out)[i] = o;
+        }
     }
 }
 
-// K per split: 512 when it divides K, else 256 (whole stages; enough units to spread over the
-// SMs evenly at decode shapes: N 7168, K 8192 gives 896 units).
+// K per split: the largest of 1024, 512, 256 that divides K (whole stages).  A function of K
+// only, so results do not depend on the device.  N 7168, K 8192 gives 448 units.  (Measured at
+// that shape: 512-K splits 21.5 us, 1024 19.5 us, 256 27.7 us -- fewer partials to write and
+// reduce.)
 inline int split_k(int64_t K) {
+#ifdef GSMALL_SPLIT
+    if (K % GSMALL_SPLIT == 0) return GSMALL_SPLIT;
+#endif
+    if (K % 1024 == 0) return 1024;
     if (K % 512 == 0) return 512;
     if (K % 256 == 0) return 256;
     return 0;
+}
+
+// Persistent grid for `units` equal work units: the largest grid <= sms that divides them evenly,
+// when that keeps at least 3/4 of the SMs busy (896 units on 148 SMs: 128 CTAs x 7 units, no
+// tail of a few CTAs with one unit more); otherwise one CTA per SM.
+inline int persistent_grid(int units, int sms) {
+    if (units <= sms) return units;
+#ifdef GSMALL_GRID_SMS
+    return sms;
+#endif
+    for (int g = sms; g * 4 >= sms * 3; g--)
+        if (units % g == 0) return g;
+    return sms;
 }
 
 // Workspace: the fp32 partials [splits][M][N].
@@ -337,16 +409,32 @@ nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void*
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     const int units = (int)(N / 128) * splits;
-    const int grid = units < sm_count() ? units : sm_count();
+    const int grid = persistent_grid(units, ctas_per_sm(mp) * sm_count());
     float* w = reinterpret_cast<float*>(ws);
-    gemm_small_kernel<<<grid, THREADS, smem, s>>>(ta, tb, reinterpret_cast<const uint8_t*>(sfa),
-                                                  reinterpret_cast<const uint8_t*>(sfb), w, (int)M, (int)N, (int)K, ks, mp);
+    // Both kernels are launched as programmatic dependents of the previous work in the stream.
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_small_kernel, ta, tb, reinterpret_cast<const uint8_t*>(sfa),
+                                       reinterpret_cast<const uint8_t*>(sfb), w, (int)M, (int)N, (int)K, ks, mp);
+    if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "gemm_small_kernel: %s", cudaGetErrorString(e));
     if ((st = check_launch("gemm_small_kernel"))) return st;
     const int64_t mn = M * N;
-    int64_t rg = (mn + 255) / 256;
+    int64_t rg = (mn / 4 + 255) / 256;
     const int64_t cap = (int64_t)sm_count() * 8;
     if (rg > cap) rg = cap;
-    splitk_reduce_kernel<kOutF32><<<(unsigned)rg, 256, 0, s>>>(w, D, mn, splits, alpha);
+    cfg.gridDim = dim3((unsigned)rg, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    e = cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<kOutF32>, (const float*)w, D, mn, splits, alpha);
+    if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "splitk_reduce_kernel: %s", cudaGetErrorString(e));
     return check_launch("splitk_reduce_kernel");
 }
 

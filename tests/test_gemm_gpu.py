@@ -169,6 +169,40 @@ def test_gemm_small_m_bitexact(nv, oracle, M, N, K):
         assert np.array_equal(ref.view(np.uint32), acc.view(np.uint32))
 
 
+def wide_range_operands(nv, M, N, K, seed, spread=4):
+    """N(0, 1) rows whose 16-element blocks are scaled by 2^e, e uniform in [-spread, spread]: the
+    partial sums then carry more bits than fp32 holds, so rounding depends on the split points."""
+    rng = np.random.default_rng(seed)
+
+    def mat(rows):
+        x = rng.standard_normal((rows, K)).astype(np.float32)
+        e = rng.integers(-spread, spread + 1, size=(rows, K // 16)).astype(np.float32)
+        x *= np.repeat(np.exp2(e), 16, axis=1)
+        p, s, gs = nv.quantize(torch.from_numpy(x).to(torch.bfloat16).cuda(), None)
+        return p, s, float(gs.item())
+
+    pa, sa, gsa = mat(M)
+    pb, sb, gsb = mat(N)
+    torch.cuda.synchronize()
+    return pa, sa, pb, sb, gsa, gsb
+
+
+@pytest.mark.parametrize("M,N,K", [(16, 256, 2048), (8, 7168, 8192)])
+def test_gemm_small_m_split_points_matter(nv, oracle, M, N, K):
+    """The split-K model is pinned where it is observable: with wide-range blocks the oracle's
+    result changes with the split size (checked here), and the kernel matches it at its own."""
+    pa, sa, pb, sb, gsa, gsb = wide_range_operands(nv, M, N, K, seed=M * 31 + K)
+    Df = nv.gemm_f32(pa, sa, pb, sb, M, N, K)
+    torch.cuda.synchronize()
+    assert nv.device_status() == 0
+    host = [t.cpu().numpy() for t in (pa, sa, pb, sb)]
+    ks = split_size(K)
+    acc = oracle.gemm_splitk_f32(*host, M, N, K, ks)
+    other = oracle.gemm_splitk_f32(*host, M, N, K, ks // 2)
+    assert np.count_nonzero(acc.view(np.uint32) != other.view(np.uint32)) > acc.size // 10
+    assert np.array_equal(Df.cpu().numpy().view(np.uint32), acc.view(np.uint32))
+
+
 def test_gemm_decode_cfg3_full_size(nv, oracle):
     """cfg3 decode shape M16 N7168 K8192, bit-exact everywhere against the split-K model, and the
     caller-workspace entry point gives the same bytes."""
