@@ -313,7 +313,10 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
 template <bool kOutF32>
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, void* __restrict__ out,
                                                             int64_t mn, int splits, float alpha) {
-    asm volatile("griddepcontrol.wait;" ::: "memory");      // the partials of the GEMM kernel
+    // The next kernel in the stream may launch now and overlap its set-up with this one; the
+    // partials of the GEMM kernel are visible after the wait.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int64_t mn4 = mn / 4;
     const float4* w4 = reinterpret_cast<const float4*>(ws);
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < mn4; i += (int64_t)gridDim.x * blockDim.x) {
