@@ -296,6 +296,33 @@ def decode_bench(nv, steps, warmup, flush):
             "launches_per_call": 2}
 
 
+def gemm_quantize_bench(nv, steps, flush):
+    """cfg3 GEMM whose epilogue writes NVFP4 (next layer's input) against GEMM (bf16 D) followed by
+    the quantizer; both produce the same bytes."""
+    import torch
+    pa, sa, pb, sb, alpha, d = gemm_setup(nv, 0)
+    nv.gemm(pa, sa, pb, sb, M_, N_, K_, alpha=alpha, out=d)
+    torch.cuda.synchronize()
+    gs = nv.global_scale_from_amax(float(d.float().abs().max()))
+    qp = torch.empty((M_, N_ // 2), dtype=torch.uint8, device="cuda")
+    qs = torch.empty(nv.sf_bytes(M_, N_), dtype=torch.uint8, device="cuda")
+    fused = lambda: nv.gemm_quantize(pa, sa, pb, sb, M_, N_, K_, alpha, gs, packed=qp, sf=qs)  # noqa: E731
+
+    def two_step():
+        nv.gemm(pa, sa, pb, sb, M_, N_, K_, alpha=alpha, out=d)
+        nv.quantize(d, gs, packed=qp, sf=qs)
+
+    for fn in (fused, two_step):
+        for _ in range(3):
+            fn()
+    ms_f = sum(timed_steps(fused, steps, flush)) / steps
+    ms_t = sum(timed_steps(two_step, steps, flush)) / steps
+    return {"workload": "cfg3 GEMM 8192^3 with NVFP4 output (given global scale)",
+            "us_fused": round(ms_f * 1e3, 1), "us_gemm_then_quantize": round(ms_t * 1e3, 1),
+            "tflops_fused": round(2.0 * M_ * N_ * K_ / (ms_f * 1e-3) / 1e12, 1), "launches_fused": 1,
+            "launches_two_step": 2}
+
+
 def cpu_baseline_gemm(target_s=8.0):
     """Reference CPU GEMM (cpu_gemm_ref_bs, random_cpu_ref/verify_random.h:154) on all host
     threads over a bounded M x N slice of the K=8192 problem; returns TFLOPS."""
@@ -397,6 +424,10 @@ def run_ours(args):
             extra["gemm_decode"] = decode_bench(nv, max(5, args.steps), 3, flush)
         except Exception as e:  # reported, not fatal
             extra["gemm_decode"] = {"error": str(e)}
+        try:
+            extra["gemm_quantize"] = gemm_quantize_bench(nv, min(max(5, args.steps), 20), flush)
+        except Exception as e:  # reported, not fatal
+            extra["gemm_quantize"] = {"error": str(e)}
     if world > 1:
         extra["allreduce"] = allreduce_bench(nv, world, rank, args, flush=flush)
 
@@ -625,6 +656,8 @@ def run_only(args):
         out = quantize_bench(nv, args.steps, args.warmup, flush)
     elif args.only == "gemm-decode":
         out = decode_bench(nv, args.steps, args.warmup, flush)
+    elif args.only == "gemm-quantize":
+        out = gemm_quantize_bench(nv, args.steps, flush)
     elif args.only == "ar-emulated":
         # the all-reduce data path of 8 ranks on this one GPU, phase by phase (no cross-GPU
         # waits): for profiling the phase kernels' memory traffic on a single device
@@ -665,7 +698,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--numel", type=int, default=4 << 20, help="elements per rank for --only ar-emulated")
-    ap.add_argument("--only", choices=["gemm", "gemm-decode", "quantize", "ar-sweep", "ar-emulated"], default=None,
+    ap.add_argument("--only", choices=["gemm", "gemm-decode", "gemm-quantize", "quantize", "ar-sweep", "ar-emulated"],
+                    default=None,
                     help="profiling mode: run one workload (warmup + steps launches) and print its "
                          "timings; not the benchmark line")
     args = ap.parse_args()

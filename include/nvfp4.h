@@ -142,6 +142,16 @@ NVFP4_API nvfp4_status_t nvfp4_gemm_bf16_ws(const void* A, const void* sfa, cons
 NVFP4_API nvfp4_status_t nvfp4_gemm_f32(const void* A, const void* sfa, const void* B, const void* sfb,
                               float* D, int64_t M, int64_t N, int64_t K, void* stream);
 
+/* GEMM with the quantizer fused into its epilogue, for back-to-back NVFP4 layers (no direct
+ * counterpart in the reference: it composes the GEMM above with nvfp4_quantize_bf16).
+ * Writes exactly the bytes of nvfp4_gemm_bf16 followed by nvfp4_quantize_bf16(D, gs_out):
+ * D_packed (M x N/2 bytes, E2M1 codes) and D_sf (nvfp4_sf_bytes(M, N), tcgen05 layout), without
+ * the bf16 D ever reaching memory.  gs_out is the global scale of D, given (finite, > 0).
+ * Requires M % 256 == 0, N % 256 == 0, K % 256 == 0, 32-byte aligned D_packed. */
+NVFP4_API nvfp4_status_t nvfp4_gemm_quantize(const void* A, const void* sfa, const void* B, const void* sfb,
+                                   float alpha, float gs_out, void* D_packed, void* D_sf, int64_t M,
+                                   int64_t N, int64_t K, void* stream);
+
 /* ----------------------------------------------------------- all-reduce ---- */
 /* NVFP4-compressed all-reduce of bf16 tensors across the GPUs of one node over NVLink /
  * NVSwitch peer memory, and the in-house bf16 peer-to-peer all-reduce it is measured

@@ -42,6 +42,7 @@ SIGNATURES = {
     "nvfp4_gemm_f32": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "nvfp4_gemm_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64]),
     "nvfp4_gemm_bf16_ws": (_I, [_P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
+    "nvfp4_gemm_quantize": (_I, [_P, _P, _P, _P, _F, _F, _P, _P, _I64, _I64, _I64, _P]),
     "nvfp4_diag_e2m1_encode": (_I, [_P, _P, _I64, _P]),
     "nvfp4_diag_e4m3_encode": (_I, [_P, _P, _I64, _P]),
     "nvfp4_diag_mma_peak": (_I, [_I, _I, _I, _P]),
@@ -183,6 +184,20 @@ def gemm(a_packed, sfa, b_packed, sfb, M: int, N: int, K: int, alpha: float = 1.
     check(lib().nvfp4_gemm_bf16(_ptr(a_packed), _ptr(sfa), _ptr(b_packed), _ptr(sfb), ctypes.c_float(alpha),
                                 _ptr(out), M, N, K, _stream(stream)))
     return out
+
+
+def gemm_quantize(a_packed, sfa, b_packed, sfb, M: int, N: int, K: int, alpha: float, global_scale: float,
+                  packed=None, sf=None, stream=None):
+    """NVFP4 of D = bf16(alpha * A @ B^T) with the given global scale, quantized in the GEMM's
+    epilogue: (packed [M, N/2] uint8, scales in the tcgen05 layout)."""
+    import torch
+    if packed is None:
+        packed = torch.empty((M, N // 2), dtype=torch.uint8, device=a_packed.device)
+    if sf is None:
+        sf = torch.empty(sf_bytes(M, N), dtype=torch.uint8, device=a_packed.device)
+    check(lib().nvfp4_gemm_quantize(_ptr(a_packed), _ptr(sfa), _ptr(b_packed), _ptr(sfb), ctypes.c_float(alpha),
+                                    ctypes.c_float(global_scale), _ptr(packed), _ptr(sf), M, N, K, _stream(stream)))
+    return packed, sf
 
 
 def gemm_f32(a_packed, sfa, b_packed, sfb, M: int, N: int, K: int, out=None, stream=None):

@@ -38,6 +38,8 @@
 //
 // Epilogue (warps 2..5 of both CTAs): tcgen05.ld 32x32b -> alpha * acc -> bf16 -> swizzled
 // shared-memory staging (2 x 16 KB) -> 2D TMA store, double buffered.
+#include <cstring>
+
 #include "capi_internal.h"
 #include "nvfp4_common.cuh"
 #include "tma_host.h"
@@ -179,11 +181,20 @@ __device__ unsigned long long g_gemm2_prof[296][16];
 #define PROF_WAIT(slot, expr) (expr)
 #endif
 
-template <bool kOutF32>
+// NVFP4 output of the fused epilogue: D is quantized with a given global scale into packed
+// [M][N/2] codes and block scales in the tcgen05 layout of an M x N matrix.
+struct QuantOut {
+    uint8_t* packed;
+    uint8_t* sf;
+    float gs_inv;
+};
+
+template <bool kOutF32, bool kQuantOut>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
              const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
-             const __grid_constant__ CUtensorMap tmap_d, int M, int N, int K, float alpha) {
+             const __grid_constant__ CUtensorMap tmap_d, QuantOut qout, int M, int N, int K, float alpha) {
+    static_assert(!(kOutF32 && kQuantOut), "the quantized output is made from the bf16 result");
     constexpr int CHUNK = kOutF32 ? 32 : 64;          // output columns per 128-byte staging row
     constexpr int NCHUNK = BN / CHUNK;
     constexpr int OVL = OVL_COLS / CHUNK;             // chunks inside the overlapping columns
@@ -216,7 +227,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
         prefetch_tmap(&tmap_b);
         prefetch_tmap(&tmap_sfa);
         prefetch_tmap(&tmap_sfb);
-        prefetch_tmap(&tmap_d);
+        if (!kQuantOut) prefetch_tmap(&tmap_d);
         for (int s = 0; s < STAGES; s++) {
             // the leader's producer (arrive.expect_tx, A/B bytes of both CTAs) and the 4 scale
             // warps of each CTA (the stage's scale slot is in TMEM)
@@ -446,6 +457,27 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                     __syncwarp();
                     if (lane == 0) mbar_arrive_remote(leader_empty);
                 }
+                if constexpr (kQuantOut) {
+                    // bf16(alpha * acc) exactly as the bf16 output, then four 16-element blocks
+                    // quantized with the quantizer's block function: 32 bytes of codes and one
+                    // 32-bit word of block scales per thread and chunk, stored directly.
+                    uint32_t w[32];
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        const __nv_bfloat162 p = __floats2bfloat162_rn(__fmul_rn(__uint_as_float(r[2 * i]), alpha),
+                                                                       __fmul_rn(__uint_as_float(r[2 * i + 1]), alpha));
+                        w[i] = *reinterpret_cast<const uint32_t*>(&p);
+                    }
+                    uint32_t q[8], sfw = 0;
+#pragma unroll
+                    for (int blk = 0; blk < 4; blk++)
+                        sfw |= q16_bf16(w + 8 * blk, qout.gs_inv, q[2 * blk], q[2 * blk + 1]) << (8 * blk);
+                    const int64_t m = m0 + row, col = (int64_t)tn * BN + c * CHUNK;
+                    st_global_v8(qout.packed + m * (N / 2) + col / 2, q);
+                    const int64_t off = ((m >> 7) * (N / 64) + (col >> 6)) * 512 + (m & 31) * 16 + ((m >> 5) & 3) * 4;
+                    *reinterpret_cast<uint32_t*>(qout.sf + off) = sfw;
+                    continue;
+                }
                 if (issuer) bulk_wait_read1();
                 epi_bar();
                 uint8_t* srow = smem + OFF_EPI + sbuf * EPI_BYTES + row * 128;
@@ -489,9 +521,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
 }
 
 // ------------------------------------------------------------------ host ----
-template <bool kOutF32>
+template <bool kOutF32, bool kQuantOut = false>
 nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void* sfb, float alpha, void* D, int64_t M,
-                      int64_t N, int64_t K, cudaStream_t s) {
+                      int64_t N, int64_t K, cudaStream_t s, QuantOut qout = QuantOut{nullptr, nullptr, 0.0f}) {
     CUtensorMap ta, tb, tsa, tsb, td;
     nvfp4_status_t st;
     if ((st = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, M, K / 2, 128, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
@@ -506,7 +538,8 @@ nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void*
     if ((st = make_tmap_2d(&tsb, sfb, CU_TENSOR_MAP_DATA_TYPE_UINT32, 128, (N / 128) * (K / 64), 512, 128, 4,
                            CU_TENSOR_MAP_SWIZZLE_NONE)))
         return st;
-    if (kOutF32) st = make_tmap_2d(&td, D, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M, N * 4, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (kQuantOut) memset(&td, 0, sizeof(td));       // unused: the epilogue stores NVFP4 directly
+    else if (kOutF32) st = make_tmap_2d(&td, D, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M, N * 4, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B);
     else st = make_tmap_2d(&td, D, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, N, M, N * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
 
@@ -516,14 +549,14 @@ nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void*
     cudaGetDevice(&dev);
     const bool cacheable = dev >= 0 && dev < 64;
     if (!cacheable || !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemm2_kernel<kOutF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(gemm2_kernel<kOutF32, kQuantOut>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "gemm2: smem attribute: %s", cudaGetErrorString(e));
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
         cfg.blockDim = dim3(NUM_THREADS, 1, 1);
         cfg.dynamicSmemBytes = SMEM_BYTES;
         int clusters = 0;
-        if (cudaOccupancyMaxActiveClusters(&clusters, gemm2_kernel<kOutF32>, &cfg) != cudaSuccess || clusters <= 0) {
+        if (cudaOccupancyMaxActiveClusters(&clusters, gemm2_kernel<kOutF32, kQuantOut>, &cfg) != cudaSuccess || clusters <= 0) {
             cudaGetLastError();
             clusters = sm_count() / 2;
         }
@@ -535,7 +568,7 @@ nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void*
     const int pairs_cap = cacheable ? max_pairs[dev] : sm_count() / 2;
     const int tiles = (int)((M / 256) * (N / BN));
     const int pairs = tiles < pairs_cap ? tiles : pairs_cap;
-    gemm2_kernel<kOutF32><<<2 * pairs, NUM_THREADS, SMEM_BYTES, s>>>(ta, tb, tsa, tsb, td, (int)M, (int)N, (int)K, alpha);
+    gemm2_kernel<kOutF32, kQuantOut><<<2 * pairs, NUM_THREADS, SMEM_BYTES, s>>>(ta, tb, tsa, tsb, td, qout, (int)M, (int)N, (int)K, alpha);
     return check_launch("gemm2_kernel");
 }
 

@@ -2,6 +2,8 @@
 //   M <= 128, M % 128 != 0 : small-M split-K kernel (gemm_small.cu; decode shapes), N % 128 == 0
 //   M % 256 == 0            : CTA-pair kernel (gemm_2sm.cu, tcgen05 cta_group::2, 256x256 pair tiles)
 //   M % 128 == 0            : single-CTA kernel (gemm.cu, 128x256 tiles)
+#include <cmath>
+#include <cstdint>
 #include <mutex>
 
 #include "capi_internal.h"
@@ -92,6 +94,24 @@ nvfp4_status_t nvfp4_gemm_bf16_ws(const void* A, const void* sfa, const void* B,
     clear_error();
     if (M > 0 && M < 128 && !workspace) return fail(NVFP4_ERR_INVALID_ARG, "gemm_ws: null workspace");
     return gemm::dispatch<false>(A, sfa, B, sfb, alpha, D, M, N, K, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+nvfp4_status_t nvfp4_gemm_quantize(const void* A, const void* sfa, const void* B, const void* sfb, float alpha,
+                                   float gs_out, void* D_packed, void* D_sf, int64_t M, int64_t N, int64_t K,
+                                   void* stream) {
+    clear_error();
+    if (!A || !sfa || !B || !sfb || !D_packed || !D_sf) return fail(NVFP4_ERR_INVALID_ARG, "gemm_quantize: null pointer");
+    if (M == 0 || N == 0) return NVFP4_OK;
+    if (M < 0 || N < 0 || K <= 0 || M % 256 || N % 256 || K % 256)
+        return fail(NVFP4_ERR_INVALID_ARG, "gemm_quantize: need M %% 256 == 0, N %% 256 == 0, K %% 256 == 0 (got %lld %lld %lld)",
+                    (long long)M, (long long)N, (long long)K);
+    if (!(gs_out > 0.0f) || !std::isfinite(gs_out))
+        return fail(NVFP4_ERR_INVALID_ARG, "gemm_quantize: global scale must be finite and > 0");
+    if (((uintptr_t)D_packed & 31) || ((uintptr_t)D_sf & 3) || !aligned16(A) || !aligned16(B) || !aligned16(sfa) ||
+        !aligned16(sfb))
+        return fail(NVFP4_ERR_INVALID_ARG, "gemm_quantize: D_packed must be 32-byte aligned, operands 16-byte aligned");
+    const gemm2::QuantOut q{reinterpret_cast<uint8_t*>(D_packed), reinterpret_cast<uint8_t*>(D_sf), 1.0f / gs_out};
+    return gemm2::launch<false, true>(A, sfa, B, sfb, alpha, nullptr, M, N, K, (cudaStream_t)stream, q);
 }
 
 nvfp4_status_t nvfp4_gemm_f32(const void* A, const void* sfa, const void* B, const void* sfb, float* D, int64_t M,

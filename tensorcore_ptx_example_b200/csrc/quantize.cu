@@ -26,7 +26,13 @@ namespace nvfp4 {
 
 constexpr int QTHREADS = 128;                 // dequantizer CTA
 constexpr int QR_THREADS = 256;               // quantizer CTA
-constexpr int QR_UNROLL = 2;                  // 16-element blocks (32 bytes) in flight per thread
+#ifndef QUANT_UNROLL
+#define QUANT_UNROLL 2
+#endif
+#ifndef QUANT_CTAS_PER_SM
+#define QUANT_CTAS_PER_SM 4
+#endif
+constexpr int QR_UNROLL = QUANT_UNROLL;       // 16-element blocks (32 bytes) in flight per thread
 
 template <bool kDevScale, bool kLoad32>
 __global__ void __launch_bounds__(QR_THREADS)
@@ -183,7 +189,7 @@ static nvfp4_status_t launch_quantize(const void* x, int64_t rows, int64_t cols,
     const int64_t nblocks = rows * cols / 16;
     if (nblocks == 0) return NVFP4_OK;
     const int64_t per_cta = (int64_t)QR_THREADS * QR_UNROLL;
-    const int64_t cap = (int64_t)sm_count() * 4;
+    const int64_t cap = (int64_t)sm_count() * QUANT_CTAS_PER_SM;
     int64_t grid = (nblocks + per_cta - 1) / per_cta;
     if (grid > cap) grid = cap;
     // 32-byte loads when the input allows them (16-byte alignment is the API's minimum)

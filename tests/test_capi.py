@@ -81,6 +81,17 @@ def test_argument_checks_reject_before_launch(nv):
     assert "workspace" in msg
     msg = _err(nv, L.nvfp4_gemm_f32(fake, fake, fake, fake, fake, 128, 256, 100, None))
     assert "K % 256" in msg
+    f1 = ctypes.c_float(1.0)
+    msg = _err(nv, L.nvfp4_gemm_quantize(fake, fake, fake, fake, f1, f1, fake, fake, 128, 256, 256, None))
+    assert "M % 256" in msg
+    msg = _err(nv, L.nvfp4_gemm_quantize(fake, fake, fake, fake, f1, ctypes.c_float(0.0), fake, fake, 256, 256, 256,
+                                         None))
+    assert "global scale" in msg
+    msg = _err(nv, L.nvfp4_gemm_quantize(fake, fake, fake, fake, f1, f1, None, fake, 256, 256, 256, None))
+    assert "null" in msg
+    msg = _err(nv, L.nvfp4_gemm_quantize(fake, fake, fake, fake, f1, f1, ctypes.c_void_p((1 << 20) + 16), fake, 256,
+                                         256, 256, None))
+    assert "32-byte" in msg
     msg = _err(nv, L.nvfp4_amax_bf16(fake, 7, fake, None))
     assert "numel" in msg
     msg = _err(nv, L.nvfp4_quantize_bf16_auto(fake, 128, 128, fake, fake, fake, None, None))

@@ -169,6 +169,43 @@ def test_gemm_small_m_bitexact(nv, oracle, M, N, K):
         assert np.array_equal(ref.view(np.uint32), acc.view(np.uint32))
 
 
+@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (512, 768, 1024), (256, 7168, 512)])
+def test_gemm_quantize_fused_matches_two_step(nv, oracle, M, N, K):
+    """The quantizer fused into the GEMM epilogue writes exactly the bytes of GEMM (bf16) followed
+    by the quantizer with the same global scale; on the smaller shapes also those of the oracle."""
+    pa, sa, pb, sb, gsa, gsb = quantized_operands(nv, oracle, M, N, K, seed=M + 3 * N + K)
+    alpha = float(np.float32(gsa) * np.float32(gsb))
+    D = nv.gemm(pa, sa, pb, sb, M, N, K, alpha=alpha)
+    torch.cuda.synchronize()
+    gs = nv.global_scale_from_amax(float(D.float().abs().max()))
+    qp, qs = nv.gemm_quantize(pa, sa, pb, sb, M, N, K, alpha, gs)
+    p2, s2, _ = nv.quantize(D, gs)
+    torch.cuda.synchronize()
+    assert nv.device_status() == 0
+    assert torch.equal(qp, p2) and torch.equal(qs, s2)
+    if M * N * K <= 512 * 768 * 1024:
+        acc = oracle.gemm_f32(pa.cpu().numpy(), sa.cpu().numpy(), pb.cpu().numpy(), sb.cpu().numpy(), M, N, K,
+                              model=MODEL)
+        d16 = oracle.gemm_epilogue_bf16(acc, alpha)
+        op, osf = oracle.quantize_bf16(d16, gs)
+        assert np.array_equal(qp.cpu().numpy().reshape(-1), op.reshape(-1))
+        assert np.array_equal(qs.cpu().numpy().reshape(-1), osf.reshape(-1))
+
+
+def test_gemm_quantize_fused_cfg3_full_size(nv, oracle):
+    M, N, K = workloads.CFG3_SHAPE
+    pa, sa, pb, sb, gsa, gsb = quantized_operands(nv, oracle, M, N, K, seed=29)
+    alpha = float(np.float32(gsa) * np.float32(gsb))
+    D = nv.gemm(pa, sa, pb, sb, M, N, K, alpha=alpha)
+    torch.cuda.synchronize()
+    gs = nv.global_scale_from_amax(float(D.float().abs().max()))
+    qp, qs = nv.gemm_quantize(pa, sa, pb, sb, M, N, K, alpha, gs)
+    p2, s2, _ = nv.quantize(D, gs)
+    torch.cuda.synchronize()
+    assert nv.device_status() == 0
+    assert torch.equal(qp, p2) and torch.equal(qs, s2)
+
+
 def wide_range_operands(nv, M, N, K, seed, spread=4):
     """N(0, 1) rows whose 16-element blocks are scaled by 2^e, e uniform in [-spread, spread]: the
     partial sums then carry more bits than fp32 holds, so rounding depends on the split points."""
