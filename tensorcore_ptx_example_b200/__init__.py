@@ -60,6 +60,8 @@ SIGNATURES = {
     "nvfp4_ar_allreduce": (_I, [_P, _P, _P, _I64, _F, _I, _P]),
     "nvfp4_ar_bf16_allreduce": (_I, [_P, _P, _P, _I64, _I, _P]),
     "nvfp4_ar_allreduce_emulated": (_I, [_P, _I, _P, _P, _I64, _F, _I, _I, _P]),
+    "nvfp4_gemm_allreduce": (_I, [_P, _P, _P, _P, _P, _F, _F, _P, _I64, _I64, _I64, _P]),
+    "nvfp4_gemm_allreduce_emulated": (_I, [_P, _I, _P, _P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _P]),
 }
 
 

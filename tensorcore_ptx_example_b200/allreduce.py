@@ -117,6 +117,20 @@ class AllReduce:
                                        _algo(algo), _stream(stream)))
         return out
 
+    def gemm_allreduce(self, a_packed, sfa, b_packed, sfb, M: int, N: int, K: int, alpha: float,
+                       global_scale: float, out=None, stream=None):
+        """Row-parallel NVFP4 GEMM fused with the two-shot all-reduce: every rank passes its K
+        shard (A_r [M, K], B_r [N, K] packed, scales in the tcgen05 layout) and gets
+        sum_r bf16(alpha_r A_r B_r^T) reduced through NVFP4, the bytes of gemm() followed by
+        allreduce(algo="twoshot").  global_scale: the same on every rank."""
+        import torch
+        if out is None:
+            out = torch.empty((M, N), dtype=torch.bfloat16, device=a_packed.device)
+        check(lib().nvfp4_gemm_allreduce(self.handle, _ptr(a_packed), _ptr(sfa), _ptr(b_packed), _ptr(sfb),
+                                         ctypes.c_float(alpha), ctypes.c_float(global_scale), _ptr(out), M, N, K,
+                                         _stream(stream)))
+        return out
+
     def bf16_allreduce(self, x, out=None, algo="auto", stream=None):
         """In-house bf16 peer-to-peer all-reduce (numel % (8 * world) == 0)."""
         import torch
@@ -198,3 +212,21 @@ def emulated_allreduce(inputs, global_scale: float = 1.0, algo="auto", bf16: boo
             torch.cuda.synchronize()
             for c in contexts:
                 c.close()
+
+
+def emulated_gemm_allreduce(operands, M: int, N: int, K: int, alphas, global_scale: float, contexts, stream=None):
+    """nvfp4_gemm_allreduce for len(operands) ranks on the current GPU: operands[r] =
+    (a_packed, sfa, b_packed, sfb) of rank r.  Returns the per-rank outputs."""
+    import torch
+    world = len(operands)
+    outs = [torch.empty((M, N), dtype=torch.bfloat16, device="cuda") for _ in range(world)]
+
+    def arr(i):
+        return (ctypes.c_void_p * world)(*[ctypes.c_void_p(op[i].data_ptr()) for op in operands])
+
+    hs = (ctypes.c_void_p * world)(*[c.handle for c in contexts])
+    al = (ctypes.c_float * world)(*[float(a) for a in alphas])
+    os_ = (ctypes.c_void_p * world)(*[ctypes.c_void_p(o.data_ptr()) for o in outs])
+    check(lib().nvfp4_gemm_allreduce_emulated(hs, world, arr(0), arr(1), arr(2), arr(3), al,
+                                              ctypes.c_float(global_scale), os_, M, N, K, _stream(stream)))
+    return outs

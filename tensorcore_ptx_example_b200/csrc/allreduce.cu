@@ -65,7 +65,8 @@ struct Params {
     uint32_t epoch;
     float gs;                        // global scale of the inputs (gs = amax / (6 * 448))
     uint64_t timeout_ns;
-    int phase;                       // -1: all phases with barriers; 0/1/2: that phase alone
+    int phase;                       // -1: all phases with barriers; -2: all but phase 0 (two-shot: the
+                                     // GEMM epilogue pushed the shards); 0/1/2: that phase alone
 };
 
 __device__ __forceinline__ uint32_t* flags_of(const Params& p, int r) {
@@ -239,7 +240,7 @@ __global__ void __launch_bounds__(AR_THREADS) ar_nvfp4_kernel(const Params p) {
 
     const int64_t shard = p.numel / n;
     const int64_t schunks = shard / 32;
-    if (fused || p.phase == 0) {
+    if (p.phase == -1 || p.phase == 0) {
         for (int64_t c = first; c < schunks; c += stride) {
             for (int k = 1; k <= n; k++) {
                 const int o = (me + k) % n;
@@ -670,6 +671,78 @@ nvfp4_status_t nvfp4_ar_bf16_allreduce(nvfp4_ar_t h, const void* in, void* out, 
     if (algo == NVFP4_AR_AUTO) algo = nvfp4_ar_choose_algo(h->world, numel);
     h->epoch++;
     return launch_bf16(h, make_params(h, in, out, numel, 0.0f, -1), algo == NVFP4_AR_TWOSHOT, (cudaStream_t)stream);
+}
+
+// GEMM whose epilogue quantizes and pushes D's shards into the owners' IN slots (phase 0 of the
+// two-shot), for the current epoch's parity region.
+static nvfp4_status_t launch_gemm_push(nvfp4_ar_t h, const void* A, const void* sfa, const void* B, const void* sfb,
+                                       float alpha, float gs, int64_t M, int64_t N, int64_t K, cudaStream_t s) {
+    gemm2::EpiOut q{};
+    const int64_t shard = M * N / h->world;
+    q.gs_inv = 1.0f / gs;
+    q.shard = shard;
+    q.sf_off = align16(shard / 2);
+    for (int o = 0; o < h->world; o++)
+        q.dst[o] = h->peer[o] + AR_FLAG_BYTES + (int64_t)(h->epoch & 1u) * h->region + (int64_t)h->rank * h->in_slot;
+    return gemm2::launch<gemm2::OUT_PUSH>(A, sfa, B, sfb, alpha, nullptr, M, N, K, s, q);
+}
+
+static nvfp4_status_t check_gemm_ar(nvfp4_ar_t h, const char* who, const void* A, const void* sfa, const void* B,
+                                    const void* sfb, const void* out, int64_t M, int64_t N, int64_t K, float gs) {
+    if (!A || !sfa || !B || !sfb) return fail(NVFP4_ERR_INVALID_ARG, "%s: null operand", who);
+    if (M <= 0 || N <= 0 || K <= 0 || M % 256 || N % 256 || K % 256)
+        return fail(NVFP4_ERR_INVALID_ARG, "%s: need M %% 256 == 0, N %% 256 == 0, K %% 256 == 0", who);
+    if (!aligned16(A) || !aligned16(B) || !aligned16(sfa) || !aligned16(sfb))
+        return fail(NVFP4_ERR_INVALID_ARG, "%s: operands must be 16-byte aligned", who);
+    nvfp4_status_t st = check_call(h, who, A, out, M * N, NVFP4_AR_TWOSHOT, 32);
+    if (st) return st;
+    if ((M * N / h->world) % 64 != 0)
+        return fail(NVFP4_ERR_INVALID_ARG, "%s: M*N/world must be a multiple of 64", who);
+    if (!(gs > 0.0f) || !isfinite(gs)) return fail(NVFP4_ERR_INVALID_ARG, "%s: global_scale must be finite and > 0", who);
+    return NVFP4_OK;
+}
+
+nvfp4_status_t nvfp4_gemm_allreduce(nvfp4_ar_t h, const void* A, const void* sfa, const void* B, const void* sfb,
+                                    float alpha, float global_scale, void* out, int64_t M, int64_t N, int64_t K,
+                                    void* stream) {
+    clear_error();
+    nvfp4_status_t st = check_gemm_ar(h, "gemm_allreduce", A, sfa, B, sfb, out, M, N, K, global_scale);
+    if (st) return st;
+    h->epoch++;
+    cudaStream_t s = (cudaStream_t)stream;
+    if ((st = launch_gemm_push(h, A, sfa, B, sfb, alpha, global_scale, M, N, K, s))) return st;
+    return launch_nvfp4(h, make_params(h, nullptr, out, M * N, global_scale, -2), true, s);
+}
+
+nvfp4_status_t nvfp4_gemm_allreduce_emulated(nvfp4_ar_t const* handles, int world, const void* const* A,
+                                             const void* const* sfa, const void* const* B, const void* const* sfb,
+                                             const float* alpha, float global_scale, void* const* outs, int64_t M,
+                                             int64_t N, int64_t K, void* stream) {
+    clear_error();
+    if (!handles || !A || !sfa || !B || !sfb || !alpha || !outs || world < 1 || world > AR_MAX_WORLD)
+        return fail(NVFP4_ERR_INVALID_ARG, "gemm_allreduce_emulated: bad arguments");
+    for (int r = 0; r < world; r++) {
+        nvfp4_status_t st = check_gemm_ar(handles[r], "gemm_allreduce_emulated", A[r], sfa[r], B[r], sfb[r], outs[r],
+                                          M, N, K, global_scale);
+        if (st) return st;
+        if (handles[r]->world != world || handles[r]->rank != r || handles[r]->device != handles[0]->device)
+            return fail(NVFP4_ERR_INVALID_ARG, "gemm_allreduce_emulated: contexts must be ranks 0..%d of one device",
+                        world - 1);
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    for (int r = 0; r < world; r++) handles[r]->epoch++;
+    // every rank's GEMM (pushes), then phase 1 of every rank, then phase 2: no kernel waits
+    for (int r = 0; r < world; r++) {
+        nvfp4_status_t st = launch_gemm_push(handles[r], A[r], sfa[r], B[r], sfb[r], alpha[r], global_scale, M, N, K, s);
+        if (st) return st;
+    }
+    for (int ph = 1; ph <= 2; ph++)
+        for (int r = 0; r < world; r++) {
+            nvfp4_status_t st = launch_nvfp4(handles[r], make_params(handles[r], nullptr, outs[r], M * N, global_scale, ph),
+                                             true, s);
+            if (st) return st;
+        }
+    return NVFP4_OK;
 }
 
 nvfp4_status_t nvfp4_ar_allreduce_emulated(nvfp4_ar_t const* handles, int world, const void* const* ins,

@@ -190,20 +190,30 @@ __device__ unsigned long long g_gemm2_prof[296][16];
 #define PROF_WAIT(slot, expr) (expr)
 #endif
 
-// NVFP4 output of the fused epilogue: D is quantized with a given global scale into packed
-// [M][N/2] codes and block scales in the tcgen05 layout of an M x N matrix.
-struct QuantOut {
-    uint8_t* packed;
+// Output of the epilogue:
+//   OUT_BF16 / OUT_F32  D through shared-memory staging and TMA stores;
+//   OUT_NVFP4           D = bf16(alpha * acc) quantized with a given global scale into packed
+//                       [M][N/2] codes and block scales in the tcgen05 layout of an M x N matrix;
+//   OUT_PUSH            the same quantization, written in the all-reduce payload layout into the
+//                       IN slot of the rank that owns the element's shard (two-shot reduce-scatter
+//                       step of a row-parallel GEMM; the slots may be peer memory).
+constexpr int OUT_BF16 = 0, OUT_F32 = 1, OUT_NVFP4 = 2, OUT_PUSH = 3;
+struct EpiOut {
+    uint8_t* packed;             // OUT_NVFP4
     uint8_t* sf;
-    float gs_inv;
+    float gs_inv;                // OUT_NVFP4, OUT_PUSH
+    uint8_t* dst[8];             // OUT_PUSH: payload base in the IN slot of owner o
+    int64_t shard;               // OUT_PUSH: elements per owner (a multiple of 64)
+    int64_t sf_off;              // OUT_PUSH: byte offset of the scales in a payload
 };
 
-template <bool kOutF32, bool kQuantOut>
+template <int kOut>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
              const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
-             const __grid_constant__ CUtensorMap tmap_d, QuantOut qout, int M, int N, int K, float alpha) {
-    static_assert(!(kOutF32 && kQuantOut), "the quantized output is made from the bf16 result");
+             const __grid_constant__ CUtensorMap tmap_d, const EpiOut qout, int M, int N, int K, float alpha) {
+    constexpr bool kOutF32 = kOut == OUT_F32;
+    constexpr bool kQuantOut = kOut == OUT_NVFP4 || kOut == OUT_PUSH;
     constexpr int CHUNK = kOutF32 ? 32 : 64;          // output columns per 128-byte staging row
     constexpr int NCHUNK = BN / CHUNK;
     constexpr int OVL = OVL_COLS / CHUNK;             // chunks inside the overlapping columns
@@ -509,9 +519,21 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                     for (int blk = 0; blk < 4; blk++)
                         sfw |= q16_bf16(w + 8 * blk, qout.gs_inv, q[2 * blk], q[2 * blk + 1]) << (8 * blk);
                     const int64_t m = m0 + row, col = (int64_t)tn * BN + c * CHUNK;
-                    st_global_v8(qout.packed + m * (N / 2) + col / 2, q);
-                    const int64_t off = ((m >> 7) * (N / 64) + (col >> 6)) * 512 + (m & 31) * 16 + ((m >> 5) & 3) * 4;
-                    *reinterpret_cast<uint32_t*>(qout.sf + off) = sfw;
+                    if constexpr (kOut == OUT_NVFP4) {
+                        st_global_v8(qout.packed + m * (N / 2) + col / 2, q);
+                        const int64_t off = ((m >> 7) * (N / 64) + (col >> 6)) * 512 + (m & 31) * 16 + ((m >> 5) & 3) * 4;
+                        *reinterpret_cast<uint32_t*>(qout.sf + off) = sfw;
+                    } else {
+                        // element e of the flattened D: owner e / shard, chunks of 32 elements
+                        // (16 bytes of codes, 2 scale bytes) at their index inside the shard
+                        const int64_t e = m * N + col;
+                        const int o = (int)(e / qout.shard);
+                        const int64_t ch = (e - (int64_t)o * qout.shard) / 32;
+                        uint8_t* d = qout.dst[o];
+                        st_v4(d + ch * 16, make_uint4(q[0], q[1], q[2], q[3]));
+                        st_v4(d + ch * 16 + 16, make_uint4(q[4], q[5], q[6], q[7]));
+                        *reinterpret_cast<uint32_t*>(d + qout.sf_off + ch * 2) = sfw;
+                    }
                     continue;
                 }
                 if (issuer) bulk_wait_read1();
@@ -546,6 +568,8 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
             }
         }
         if (issuer) bulk_wait_all();
+        // pushed payloads (peer memory) are complete before anything this rank does next
+        if constexpr (kOut == OUT_PUSH) __threadfence_system();
     }
 
     __syncwarp();
@@ -557,9 +581,11 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
 }
 
 // ------------------------------------------------------------------ host ----
-template <bool kOutF32, bool kQuantOut = false>
+template <int kOut>
 nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void* sfb, float alpha, void* D, int64_t M,
-                      int64_t N, int64_t K, cudaStream_t s, QuantOut qout = QuantOut{nullptr, nullptr, 0.0f}) {
+                      int64_t N, int64_t K, cudaStream_t s, const EpiOut& qout = EpiOut{}) {
+    constexpr bool kOutF32 = kOut == OUT_F32;
+    constexpr bool kQuantOut = kOut == OUT_NVFP4 || kOut == OUT_PUSH;
     CUtensorMap ta, tb, tsa, tsb, td;
     nvfp4_status_t st;
     if ((st = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, M, K / 2, 128, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
@@ -585,14 +611,14 @@ nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void*
     cudaGetDevice(&dev);
     const bool cacheable = dev >= 0 && dev < 64;
     if (!cacheable || !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemm2_kernel<kOutF32, kQuantOut>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(gemm2_kernel<kOut>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "gemm2: smem attribute: %s", cudaGetErrorString(e));
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
         cfg.blockDim = dim3(NUM_THREADS, 1, 1);
         cfg.dynamicSmemBytes = SMEM_BYTES;
         int clusters = 0;
-        if (cudaOccupancyMaxActiveClusters(&clusters, gemm2_kernel<kOutF32, kQuantOut>, &cfg) != cudaSuccess || clusters <= 0) {
+        if (cudaOccupancyMaxActiveClusters(&clusters, gemm2_kernel<kOut>, &cfg) != cudaSuccess || clusters <= 0) {
             cudaGetLastError();
             clusters = sm_count() / 2;
         }
@@ -604,7 +630,7 @@ nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void*
     const int pairs_cap = cacheable ? max_pairs[dev] : sm_count() / 2;
     const int tiles = (int)((M / 256) * (N / BN));
     const int pairs = tiles < pairs_cap ? tiles : pairs_cap;
-    gemm2_kernel<kOutF32, kQuantOut><<<2 * pairs, NUM_THREADS, SMEM_BYTES, s>>>(ta, tb, tsa, tsb, td, qout, (int)M, (int)N, (int)K, alpha);
+    gemm2_kernel<kOut><<<2 * pairs, NUM_THREADS, SMEM_BYTES, s>>>(ta, tb, tsa, tsb, td, qout, (int)M, (int)N, (int)K, alpha);
     return check_launch("gemm2_kernel");
 }
 

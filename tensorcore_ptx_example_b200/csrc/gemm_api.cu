@@ -67,7 +67,8 @@ static nvfp4_status_t dispatch(const void* A, const void* sfa, const void* B, co
         }
         return gsmall::launch<kOutF32>(A, sfa, B, sfb, alpha, D, M, N, K, ws, ws_bytes, s);
     }
-    if (M % 256 == 0) return gemm2::launch<kOutF32>(A, sfa, B, sfb, alpha, D, M, N, K, s);
+    if (M % 256 == 0)
+        return gemm2::launch<kOutF32 ? gemm2::OUT_F32 : gemm2::OUT_BF16>(A, sfa, B, sfb, alpha, D, M, N, K, s);
     return launch<kOutF32>(A, sfa, B, sfb, alpha, D, M, N, K, s);
 }
 
@@ -110,8 +111,11 @@ nvfp4_status_t nvfp4_gemm_quantize(const void* A, const void* sfa, const void* B
     if (((uintptr_t)D_packed & 31) || ((uintptr_t)D_sf & 3) || !aligned16(A) || !aligned16(B) || !aligned16(sfa) ||
         !aligned16(sfb))
         return fail(NVFP4_ERR_INVALID_ARG, "gemm_quantize: D_packed must be 32-byte aligned, operands 16-byte aligned");
-    const gemm2::QuantOut q{reinterpret_cast<uint8_t*>(D_packed), reinterpret_cast<uint8_t*>(D_sf), 1.0f / gs_out};
-    return gemm2::launch<false, true>(A, sfa, B, sfb, alpha, nullptr, M, N, K, (cudaStream_t)stream, q);
+    gemm2::EpiOut q{};
+    q.packed = reinterpret_cast<uint8_t*>(D_packed);
+    q.sf = reinterpret_cast<uint8_t*>(D_sf);
+    q.gs_inv = 1.0f / gs_out;
+    return gemm2::launch<gemm2::OUT_NVFP4>(A, sfa, B, sfb, alpha, nullptr, M, N, K, (cudaStream_t)stream, q);
 }
 
 nvfp4_status_t nvfp4_gemm_f32(const void* A, const void* sfa, const void* B, const void* sfb, float* D, int64_t M,

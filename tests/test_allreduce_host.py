@@ -84,6 +84,14 @@ def test_create_rejects_bad_arguments(nv):
     # calls on a null context are rejected before any CUDA work
     assert L.nvfp4_ar_allreduce(None, None, None, 64, ctypes.c_float(1.0), 0, None) == nv.NVFP4_ERR_INVALID_ARG
     assert L.nvfp4_ar_set_timeout(None, 10 ** 9) == nv.NVFP4_ERR_INVALID_ARG
+    fake = ctypes.c_void_p(1 << 20)
+    f1 = ctypes.c_float(1.0)
+    assert L.nvfp4_gemm_allreduce(None, fake, fake, fake, fake, f1, f1, fake, 256, 256, 256,
+                                  None) == nv.NVFP4_ERR_INVALID_ARG
+    assert L.nvfp4_gemm_allreduce(None, fake, fake, fake, fake, f1, f1, fake, 128, 256, 256,
+                                  None) == nv.NVFP4_ERR_INVALID_ARG
+    assert L.nvfp4_gemm_allreduce_emulated(None, 2, None, None, None, None, None, f1, None, 256, 256, 256,
+                                           None) == nv.NVFP4_ERR_INVALID_ARG
 
 
 # ------------------------------------------------------------ gloo ranks ----
