@@ -430,6 +430,7 @@ def run_ours(args):
             extra["gemm_quantize"] = {"error": str(e)}
     if world > 1:
         extra["allreduce"] = allreduce_bench(nv, world, rank, args, flush=flush)
+        extra["gemm_allreduce"] = gemm_allreduce_bench(nv, world, rank, args, flush=flush)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -550,6 +551,54 @@ def allreduce_bench(nv, world, rank, args, numel=None, steps=None, flush=None):
                                     "algbw_gbs": round(2.0 * numel / (e2e_ms * 1e-3) / 1e9, 1),
                                     "h2d_bytes_per_step": numel * 2, "d2h_bytes_per_step": numel * 2}
         res["gpu_launches_per_call"] = 1
+    finally:
+        torch.cuda.synchronize()
+        barrier(world)
+        ctx.close()
+    return res
+
+
+def gemm_allreduce_bench(nv, world, rank, args, flush=None):
+    """Row-parallel layer with the cfg4 output (M 4096 x N 7168 bf16) and K 8192 split over the
+    ranks: the NVFP4 GEMM fused with the two-shot all-reduce (one GEMM kernel whose epilogue
+    pushes the quantized tiles to their owners, then the all-reduce's reduce and all-gather)
+    against GEMM then all-reduce; device time per call, max over ranks."""
+    import torch
+
+    from tensorcore_ptx_example_b200 import allreduce as ar
+    from tensorcore_ptx_example_b200 import workloads
+    M, N = workloads.CFG4_SHAPE
+    K = 8192 // world
+    a = workloads.activations(M, K, seed=11 + 2 * rank)
+    b = workloads.gaussian(N, K, seed=12 + 2 * rank, std=0.02)
+    pa, sa, gsa = nv.quantize(a, None)
+    pb, sb, gsb = nv.quantize(b, None)
+    torch.cuda.synchronize()
+    del a, b
+    alpha = float(gsa.item()) * float(gsb.item())
+    d = nv.gemm(pa, sa, pb, sb, M, N, K, alpha=alpha)
+    torch.cuda.synchronize()
+    gs = ar.agree_global_scale(float(d.float().abs().max()))
+    ctx = ar.AllReduce.from_process_group(M * N)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    steps = max(5, min(args.steps, 20))
+    res = {"workload": f"row-parallel NVFP4 GEMM M{M} N{N} K{K} per rank (K 8192 total) + two-shot all-reduce",
+           "world": world}
+    try:
+        fused = lambda: ctx.gemm_allreduce(pa, sa, pb, sb, M, N, K, alpha, gs, out=out)  # noqa: E731
+
+        def unfused():
+            nv.gemm(pa, sa, pb, sb, M, N, K, alpha=alpha, out=d)
+            ctx.allreduce(d.view(-1), out.view(-1), global_scale=gs, algo="twoshot")
+
+        ms_f = _ar_time(fused, steps, 3, flush, world)
+        ms_u = _ar_time(unfused, steps, 3, flush, world)
+        o_f = ctx.gemm_allreduce(pa, sa, pb, sb, M, N, K, alpha, gs).clone()
+        unfused()
+        torch.cuda.synchronize()
+        res.update({"us_fused": round(ms_f * 1e3, 1), "us_gemm_then_allreduce": round(ms_u * 1e3, 1),
+                    "speedup": round(ms_u / ms_f, 3), "same_bytes": bool(torch.equal(o_f, out)),
+                    "launches_fused": 2, "launches_unfused": 2, "device_status": nv.device_status()})
     finally:
         torch.cuda.synchronize()
         barrier(world)

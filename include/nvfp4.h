@@ -224,7 +224,7 @@ NVFP4_API nvfp4_status_t nvfp4_ar_allreduce_emulated(nvfp4_ar_t const* handles, 
  * nvfp4_ar_allreduce.  `out` (bf16 M x N) is bit-identical to nvfp4_gemm_bf16 followed by
  * nvfp4_ar_allreduce(..., NVFP4_AR_TWOSHOT) with the same global_scale, on every rank.
  * Requires M % 256 == 0, N % 256 == 0, K % 256 == 0, M * N <= the context's max_numel,
- * M * N / world a multiple of 64.  global_scale bounds |D_r| for every rank (agree on it first). */
+ * M * N / world a multiple of 256.  global_scale bounds |D_r| for every rank (agree on it first). */
 NVFP4_API nvfp4_status_t nvfp4_gemm_allreduce(nvfp4_ar_t h, const void* A, const void* sfa, const void* B,
                                               const void* sfb, float alpha, float global_scale, void* out,
                                               int64_t M, int64_t N, int64_t K, void* stream);

@@ -696,8 +696,8 @@ static nvfp4_status_t check_gemm_ar(nvfp4_ar_t h, const char* who, const void* A
         return fail(NVFP4_ERR_INVALID_ARG, "%s: operands must be 16-byte aligned", who);
     nvfp4_status_t st = check_call(h, who, A, out, M * N, NVFP4_AR_TWOSHOT, 32);
     if (st) return st;
-    if ((M * N / h->world) % 64 != 0)
-        return fail(NVFP4_ERR_INVALID_ARG, "%s: M*N/world must be a multiple of 64", who);
+    if ((M * N / h->world) % 256 != 0)
+        return fail(NVFP4_ERR_INVALID_ARG, "%s: M*N/world must be a multiple of 256", who);
     if (!(gs > 0.0f) || !isfinite(gs)) return fail(NVFP4_ERR_INVALID_ARG, "%s: global_scale must be finite and > 0", who);
     return NVFP4_OK;
 }

@@ -203,7 +203,7 @@ struct EpiOut {
     uint8_t* sf;
     float gs_inv;                // OUT_NVFP4, OUT_PUSH
     uint8_t* dst[8];             // OUT_PUSH: payload base in the IN slot of owner o
-    int64_t shard;               // OUT_PUSH: elements per owner (a multiple of 64)
+    int64_t shard;               // OUT_PUSH: elements per owner (a multiple of 256)
     int64_t sf_off;              // OUT_PUSH: byte offset of the scales in a payload
 };
 
@@ -524,15 +524,39 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                         const int64_t off = ((m >> 7) * (N / 64) + (col >> 6)) * 512 + (m & 31) * 16 + ((m >> 5) & 3) * 4;
                         *reinterpret_cast<uint32_t*>(qout.sf + off) = sfw;
                     } else {
-                        // element e of the flattened D: owner e / shard, chunks of 32 elements
-                        // (16 bytes of codes, 2 scale bytes) at their index inside the shard
-                        const int64_t e = m * N + col;
-                        const int o = (int)(e / qout.shard);
-                        const int64_t ch = (e - (int64_t)o * qout.shard) / 32;
-                        uint8_t* d = qout.dst[o];
-                        st_v4(d + ch * 16, make_uint4(q[0], q[1], q[2], q[3]));
-                        st_v4(d + ch * 16 + 16, make_uint4(q[4], q[5], q[6], q[7]));
-                        *reinterpret_cast<uint32_t*>(d + qout.sf_off + ch * 2) = sfw;
+                        // Stage the tile row's codes (128 B, 16-byte units XOR-swizzled by row)
+                        // and scale words (16 B) in the staging buffers; after the last chunk the
+                        // four warps store whole 128-byte row segments into the owner's slot, so
+                        // that the pushes cross NVLink as full lines, not 16-byte pieces.
+                        (void)m;
+                        (void)col;
+                        uint8_t* stg = smem + OFF_EPI;
+                        uint8_t* stg_sf = smem + OFF_EPI + EPI_BYTES;
+                        *reinterpret_cast<uint4*>(stg + row * 128 + (((2 * c) ^ (row & 7)) << 4)) =
+                            make_uint4(q[0], q[1], q[2], q[3]);
+                        *reinterpret_cast<uint4*>(stg + row * 128 + (((2 * c + 1) ^ (row & 7)) << 4)) =
+                            make_uint4(q[4], q[5], q[6], q[7]);
+                        *reinterpret_cast<uint32_t*>(stg_sf + row * 16 + c * 4) = sfw;
+                        if (idx == NCHUNK - 1) {
+                            epi_bar();
+                            // element e of the flattened D: owner e / shard; a row segment of
+                            // 256 elements (128 B of codes, 16 B of scales) lies in one shard
+#pragma unroll
+                            for (int i = 0; i < 8; i++) {
+                                const int id = i * 128 + row, rr = id >> 3, u = id & 7;
+                                const int64_t e = (int64_t)(m0 + rr) * N + (int64_t)tn * BN;
+                                const int o = (int)(e / qout.shard);
+                                st_v4(qout.dst[o] + (e - (int64_t)o * qout.shard) / 2 + u * 16,
+                                      *reinterpret_cast<const uint4*>(stg + rr * 128 + ((u ^ (rr & 7)) << 4)));
+                            }
+                            {
+                                const int64_t e = (int64_t)(m0 + row) * N + (int64_t)tn * BN;
+                                const int o = (int)(e / qout.shard);
+                                st_v4(qout.dst[o] + qout.sf_off + (e - (int64_t)o * qout.shard) / 16,
+                                      *reinterpret_cast<const uint4*>(stg_sf + row * 16));
+                            }
+                            epi_bar();                    // staging free for the next tile
+                        }
                     }
                     continue;
                 }

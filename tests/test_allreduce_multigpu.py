@@ -86,6 +86,48 @@ def test_in_process_allreduce_bitexact(nv, oracle, algo):
 
 
 @needs2
+def test_in_process_gemm_allreduce_bitexact(nv, oracle):
+    """Row-parallel GEMM fused with the two-shot all-reduce across real GPUs: every rank's GEMM
+    epilogue pushes its quantized tiles into the owners' slots over NVLink."""
+    world = min(ngpus(), 8)
+    M, N, K = 256, 512, 512
+    ctxs, ops, alphas, ds = [], [], [], []
+    for r in range(world):
+        with torch.cuda.device(r):
+            a = workloads.activations(M, K, seed=300 + 2 * r)
+            b = workloads.gaussian(N, K, seed=301 + 2 * r, std=0.02)
+            pa, sa, gsa = nv.quantize(a, None)
+            pb, sb, gsb = nv.quantize(b, None)
+            al = float(np.float32(float(gsa.item())) * np.float32(float(gsb.item())))
+            ops.append((pa, sa, pb, sb))
+            alphas.append(al)
+            ds.append(nv.gemm(pa, sa, pb, sb, M, N, K, alpha=al))
+            ctxs.append(ar.AllReduce(world, r, M * N))
+    for r in range(world):
+        torch.cuda.synchronize(r)
+    gs = nv.global_scale_from_amax(max(float(d.float().abs().max()) for d in ds))
+    ar.join_in_process(ctxs)
+    try:
+        outs = [None] * world
+        for rep in range(2):
+            for r in range(world):
+                with torch.cuda.device(r):
+                    pa, sa, pb, sb = ops[r]
+                    outs[r] = ctxs[r].gemm_allreduce(pa, sa, pb, sb, M, N, K, alphas[r], gs)
+            for r in range(world):
+                torch.cuda.synchronize(r)
+            want = oracle.ar_twoshot([u16(d) for d in ds], gs)
+            for r in range(world):
+                with torch.cuda.device(r):
+                    assert nv.device_status() == 0
+                assert np.array_equal(u16(outs[r]), want), (rep, r)
+    finally:
+        for c in ctxs:
+            with torch.cuda.device(c.device):
+                c.close()
+
+
+@needs2
 def test_barrier_timeout_when_a_rank_never_arrives(nv):
     world, numel = 2, 32 * 2 * 512
     ctxs, xs, outs = [], [], []
