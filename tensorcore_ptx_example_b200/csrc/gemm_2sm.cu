@@ -8,9 +8,10 @@
 //   own CTA.  The pair MMA reads both B halves, so each SM
 //   moves 38 KB per 128x256x256 block instead of the 54 KB of a single-CTA 128x256 tile.  No
 //   load uses multicast.
-//   Warp roles (480 threads): warp 0 A/B TMA producer, warp 1 MMA issuer (leader CTA), warps 2-5
-//   epilogue, warps 6-13 scale warps in two sets of four (one per TMEM lane quadrant; set k takes
-//   the stages g with g % 2 == k), warp 14 scale TMA producer.  The scale warps move the scale atoms shared memory ->
+//   Warp roles (608 threads): warp 0 A/B TMA producer, warp 1 MMA issuer (leader CTA), warps 2-5
+//   and 15-18 epilogue in two sets of four (alternate 64-column chunks of a tile), warps 6-13
+//   scale warps in two sets of four (one per TMEM lane quadrant; set k takes the stages g with
+//   g % 2 == k), warp 14 scale TMA producer.  The scale warps move the scale atoms shared memory ->
 //   registers -> TMEM with tcgen05.st into a ring of TMEM slots and then arrive (in both CTAs)
 //   on the leader's "full" barrier of the stage, which therefore completes when A/B have landed
 //   AND the scales are in TMEM: the MMA thread makes one wait per stage.  It issues four
@@ -37,8 +38,9 @@
 // buffers.  The epilogue drains the overlapping columns of a tile first and then signals the
 // leader, so the next tile's MMAs start before the drain has finished.
 //
-// Epilogue (warps 2..5 of both CTAs): tcgen05.ld 32x32b -> alpha * acc -> bf16 -> swizzled
-// shared-memory staging (2 x 16 KB) -> 2D TMA store, double buffered.
+// Epilogue (two sets of four warps in both CTAs, alternate chunks, so the shared accumulator
+// columns drain in two chunk-times instead of three): tcgen05.ld 32x32b -> alpha * acc -> bf16
+// -> swizzled shared-memory staging (16 KB per set) -> 2D TMA store.
 #include <cstring>
 
 #include "capi_internal.h"
@@ -70,7 +72,8 @@ constexpr int EPI_BYTES = 128 * 128;                  // one staging buffer: 128
 // stages g with g % 2 == k, so each set has two stages of time for its loads and stores.
 constexpr int SFW_SETS = 2;
 constexpr int SFP_WARP = 6 + 4 * SFW_SETS;           // scale-atom producer
-constexpr int NUM_THREADS = 32 * (SFP_WARP + 1);      // TMA, MMA, 4 epilogue, 8 scale, scale TMA
+constexpr int EPI_WARP1 = SFP_WARP + 1;               // second set of epilogue warps
+constexpr int NUM_THREADS = 32 * (EPI_WARP1 + 4);     // + 4 warps of the second epilogue set
 constexpr int TMEM_COLS = 512;
 #ifndef GEMM2_ACC1_COL
 #define GEMM2_ACC1_COL 64
@@ -129,6 +132,10 @@ __device__ __forceinline__ void tma_load_pair(uint32_t dst, const void* tmap, in
 }
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void epi_bar_set(int set) {
+    if (set) asm volatile("bar.sync 2, 128;" ::: "memory");
+    else asm volatile("bar.sync 1, 128;" ::: "memory");
+}
 __device__ __forceinline__ void tc_mma2(uint32_t d, uint64_t a, uint64_t b, uint32_t sfa, uint32_t sfb,
                                         uint32_t accumulate) {
     asm volatile(
@@ -214,6 +221,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
              const __grid_constant__ CUtensorMap tmap_d, const EpiOut qout, int M, int N, int K, float alpha) {
     constexpr bool kOutF32 = kOut == OUT_F32;
     constexpr bool kQuantOut = kOut == OUT_NVFP4 || kOut == OUT_PUSH;
+    // two sets of four epilogue warps take alternate chunks (one set for OUT_PUSH, whose tile
+    // rows are staged across all chunks)
+    constexpr int ESETS = kOut == OUT_PUSH ? 1 : 2;
     constexpr int CHUNK = kOutF32 ? 32 : 64;          // output columns per 128-byte staging row
     constexpr int NCHUNK = BN / CHUNK;
     constexpr int OVL = OVL_COLS / CHUNK;             // chunks inside the overlapping columns
@@ -255,7 +265,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
             mbar_init(empty_bar(s), 1);
         }
         mbar_init(tmem_full, 1);
-        mbar_init(tmem_empty, 8);                      // one elected lane of 4 epilogue warps x 2 CTAs
+        mbar_init(tmem_empty, 8 * ESETS);              // one elected lane per epilogue warp, both CTAs
         mbar_init(drain_bar, 1);
         *abort_flag = 0u;
         for (int st = 0; st < SF_RING; st++) {
@@ -395,7 +405,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
             }
         }
         __syncwarp();
-    } else if (warp >= 6) {
+    } else if (warp >= 6 && warp < 6 + 4 * SFW_SETS) {
         // ------------------------------------------------------ scale warps (both CTAs) ----
         // Warp w writes TMEM lane quadrant w % 4.  Per K step, lane r of the quadrant receives
         // 16 bytes of each scale atom (row r % 32 of the atom: the four scale words of rows r,
@@ -469,13 +479,16 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
             }
         }
         __syncwarp();
-    } else {
+    } else if (warp < 6 || ESETS == 2) {
         // -------------------------------------------------------- epilogue ----
         const int quad = warp & 3;
         const int row = quad * 32 + lane;                     // row within this CTA's 128
         const uint32_t leader_empty = mapa(tmem_empty, 0);
-        const bool issuer = (warp == 2 && lane == 0);
-        int sbuf = 0;
+        const int eset = warp >= EPI_WARP1 ? 1 : 0;
+        const bool issuer = lane == 0 && (warp == 2 || warp == EPI_WARP1);
+        // the last chunk (in drain order) inside the shared columns that this set reads
+        const int last_shared = (OVL - 1 >= eset) ? OVL - 1 - ((OVL - 1 - eset) % ESETS) : -1;
+        int sbuf = ESETS == 2 ? eset : 0;
         int iter = 0;
         for (int tile = pair; tile < ntiles; tile += npairs, iter++) {
             const int tm = tile % num_m, tn = tile / num_m;
@@ -484,13 +497,18 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                                                               mbar_wait(tmem_full, (uint32_t)(iter & 1), WAIT_LIMIT_NS,
                                                                         DEV_TIMEOUT_GEMM_EPILOGUE)));
             if (!ok && lane == 0) *abort_flag = 1u;
-            epi_bar();
+            epi_bar_set(eset);
             if (*abort_flag) break;
             tc_fence_after();
             const uint32_t dcol = (iter & 1) ? ACC1_COL : 0;
             const int m0 = tm * 256 + (int)rank * BM;
+            if (last_shared < 0) {                             // no shared columns to drain
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_remote(leader_empty);
+            }
 #pragma unroll 1
-            for (int idx = 0; idx < NCHUNK; idx++) {
+            for (int idx = eset; idx < NCHUNK; idx += ESETS) {
                 // buffer 0 drains its last OVL chunks (the shared columns) first
                 const int c = (iter & 1) ? idx : (idx + NCHUNK - OVL) % NCHUNK;
                 uint32_t r[64];
@@ -498,7 +516,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                 tc_ld32(taddr, r);
                 if constexpr (!kOutF32) tc_ld32(taddr + 32, r + 32);
                 tc_wait_ld();
-                if (idx == OVL - 1) {                          // shared columns drained
+                if (idx == last_shared) {                      // shared columns drained
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive_remote(leader_empty);
@@ -560,8 +578,11 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                     }
                     continue;
                 }
-                if (issuer) bulk_wait_read1();
-                epi_bar();
+                if (issuer) {
+                    if (ESETS == 2) bulk_wait_read_n<0>();      // one staging buffer per set
+                    else bulk_wait_read1();
+                }
+                epi_bar_set(eset);
                 uint8_t* srow = smem + OFF_EPI + sbuf * EPI_BYTES + row * 128;
                 if constexpr (kOutF32) {
 #pragma unroll
@@ -583,12 +604,12 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                     }
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                epi_bar();
+                epi_bar_set(eset);
                 if (issuer) {
                     tma_store_2d(&tmap_d, base + OFF_EPI + sbuf * EPI_BYTES, tn * BN + c * CHUNK, m0);
                     bulk_commit();
                 }
-                sbuf ^= 1;
+                if (ESETS == 1) sbuf ^= 1;
             }
         }
         if (issuer) bulk_wait_all();
