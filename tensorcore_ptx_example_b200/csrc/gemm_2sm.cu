@@ -536,8 +536,8 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
 #pragma unroll
                     for (int blk = 0; blk < 4; blk++)
                         sfw |= q16_bf16(w + 8 * blk, qout.gs_inv, q[2 * blk], q[2 * blk + 1]) << (8 * blk);
-                    const int64_t m = m0 + row, col = (int64_t)tn * BN + c * CHUNK;
                     if constexpr (kOut == OUT_NVFP4) {
+                        const int64_t m = m0 + row, col = (int64_t)tn * BN + c * CHUNK;
                         st_global_v8(qout.packed + m * (N / 2) + col / 2, q);
                         const int64_t off = ((m >> 7) * (N / 64) + (col >> 6)) * 512 + (m & 31) * 16 + ((m >> 5) & 3) * 4;
                         *reinterpret_cast<uint32_t*>(qout.sf + off) = sfw;
@@ -546,8 +546,6 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                         // and scale words (16 B) in the staging buffers; after the last chunk the
                         // four warps store whole 128-byte row segments into the owner's slot, so
                         // that the pushes cross NVLink as full lines, not 16-byte pieces.
-                        (void)m;
-                        (void)col;
                         uint8_t* stg = smem + OFF_EPI;
                         uint8_t* stg_sf = smem + OFF_EPI + EPI_BYTES;
                         *reinterpret_cast<uint4*>(stg + row * 128 + (((2 * c) ^ (row & 7)) << 4)) =
