@@ -124,6 +124,17 @@ __device__ __forceinline__ uint32_t block_scale(float amax, float gs_inv, float&
     return code;
 }
 
+// (a * s, b * s), each rounded to nearest: one packed f32x2 multiply (sm_100).
+__device__ __forceinline__ void mul2_rn(float a, float b, float s, float& ya, float& yb) {
+    asm("{\n\t.reg .b64 x, y, z;\n\t"
+        "mov.b64 x, {%2, %3};\n\t"
+        "mov.b64 y, {%4, %4};\n\t"
+        "mul.rn.f32x2 z, x, y;\n\t"
+        "mov.b64 {%0, %1}, z;\n\t}"
+        : "=f"(ya), "=f"(yb)
+        : "f"(a), "f"(b), "f"(s));
+}
+
 // Quantize 16 floats: writes two 32-bit nibble words, returns the scale byte.
 __device__ __forceinline__ uint32_t q16(const float* v, float gs_inv, uint32_t& w0, uint32_t& w1) {
     float amax = 0.0f;
@@ -133,7 +144,7 @@ __device__ __forceinline__ uint32_t q16(const float* v, float gs_inv, uint32_t& 
     const uint32_t code = block_scale(amax, gs_inv, inv);
     float y[16];
 #pragma unroll
-    for (int i = 0; i < 16; i++) y[i] = __fmul_rn(v[i], inv);
+    for (int i = 0; i < 8; i++) mul2_rn(v[2 * i], v[2 * i + 1], inv, y[2 * i], y[2 * i + 1]);
     w0 = e2m1x8(y);
     w1 = e2m1x8(y + 8);
     if (inv == 0.0f) { w0 = 0u; w1 = 0u; }
@@ -152,10 +163,8 @@ __device__ __forceinline__ uint32_t q16_bf16(const uint32_t* w, float gs_inv, ui
     const uint32_t code = block_scale(amax, gs_inv, inv);
     float y[16];
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        y[2 * i] = __fmul_rn(__uint_as_float(w[i] << 16), inv);
-        y[2 * i + 1] = __fmul_rn(__uint_as_float(w[i] & 0xFFFF0000u), inv);
-    }
+    for (int i = 0; i < 8; i++)
+        mul2_rn(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u), inv, y[2 * i], y[2 * i + 1]);
     w0 = e2m1x8(y);
     w1 = e2m1x8(y + 8);
     if (inv == 0.0f) { w0 = 0u; w1 = 0u; }
