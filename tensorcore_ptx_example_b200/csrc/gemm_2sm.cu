@@ -247,7 +247,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
     uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + OFF_TMEM_PTR);
     volatile uint32_t* abort_flag = tmem_ptr + 1;
 
-    const int num_m = M / 256, num_n = N / BN, tiles = num_m * num_n;
+    // M % 256 == 128: the last pair's second CTA covers rows M .. M+127, which its TMA loads fill
+    // with zeros (A rows and their scale atoms lie past the tensor maps) and which it never stores
+    const int num_m = (M + 255) / 256, num_n = N / BN, tiles = num_m * num_n;
     const int nkb = K / BK;
     const int katoms = K / 64;
     const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
@@ -603,7 +605,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 epi_bar_set(eset);
-                if (issuer) {
+                if (issuer && m0 < M) {
                     tma_store_2d(&tmap_d, base + OFF_EPI + sbuf * EPI_BYTES, tn * BN + c * CHUNK, m0);
                     bulk_commit();
                 }
@@ -671,7 +673,7 @@ nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void*
         }
     }
     const int pairs_cap = cacheable ? max_pairs[dev] : sm_count() / 2;
-    const int tiles = (int)((M / 256) * (N / BN));
+    const int tiles = (int)(((M + 255) / 256) * (N / BN));
     const int pairs = tiles < pairs_cap ? tiles : pairs_cap;
     gemm2_kernel<kOut><<<2 * pairs, NUM_THREADS, SMEM_BYTES, s>>>(ta, tb, tsa, tsb, td, qout, (int)M, (int)N, (int)K, alpha);
     return check_launch("gemm2_kernel");

@@ -1,7 +1,7 @@
 // gemm_api.cu -- C ABI of the NVFP4 GEMM: shape checks and kernel choice.
-//   M <= 128, M % 128 != 0 : small-M split-K kernel (gemm_small.cu; decode shapes), N % 128 == 0
-//   M % 256 == 0            : CTA-pair kernel (gemm_2sm.cu, tcgen05 cta_group::2, 256x256 pair tiles)
-//   M % 128 == 0            : single-CTA kernel (gemm.cu, 128x256 tiles)
+//   0 < M < 128     : small-M split-K kernel (gemm_small.cu; decode shapes), N % 128 == 0
+//   M % 128 == 0    : CTA-pair kernel (gemm_2sm.cu, tcgen05 cta_group::2, 256x256 pair tiles; with
+//                     M % 256 == 128 the last pair's second CTA covers zero-filled rows)
 #include <cmath>
 #include <cstdint>
 #include <mutex>
@@ -67,9 +67,7 @@ static nvfp4_status_t dispatch(const void* A, const void* sfa, const void* B, co
         }
         return gsmall::launch<kOutF32>(A, sfa, B, sfb, alpha, D, M, N, K, ws, ws_bytes, s);
     }
-    if (M % 256 == 0)
-        return gemm2::launch<kOutF32 ? gemm2::OUT_F32 : gemm2::OUT_BF16>(A, sfa, B, sfb, alpha, D, M, N, K, s);
-    return launch<kOutF32>(A, sfa, B, sfb, alpha, D, M, N, K, s);
+    return gemm2::launch<kOutF32 ? gemm2::OUT_F32 : gemm2::OUT_BF16>(A, sfa, B, sfb, alpha, D, M, N, K, s);
 }
 
 }  // namespace gemm
