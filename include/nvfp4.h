@@ -218,13 +218,13 @@ NVFP4_API nvfp4_status_t nvfp4_ar_allreduce_emulated(nvfp4_ar_t const* handles, 
 /* Row-parallel GEMM fused with the NVFP4 two-shot all-reduce (no direct counterpart in the
  * reference; its oneshot_fused_kernel PUSH layout, nvfp4_allreduce.cuh:594-603, is the model).
  * Every rank r computes D_r = bf16(alpha * A_r B_r^T) for its K shard; the GEMM epilogue
- * quantizes each tile with global_scale and pushes it straight into the all-reduce slot of the
- * rank that owns the tile's elements (the reduce-scatter step), so the bf16 D_r never reaches
- * memory; the owners then sum in rank order, requantize and all-gather as in
+ * quantizes each tile with global_scale into the per-owner payloads of the two-shot (in this
+ * rank's all-reduce buffer), so the bf16 D_r never reaches memory; the all-reduce kernel then
+ * pushes the payloads to their owners, which sum in rank order, requantize and all-gather as in
  * nvfp4_ar_allreduce.  `out` (bf16 M x N) is bit-identical to nvfp4_gemm_bf16 followed by
  * nvfp4_ar_allreduce(..., NVFP4_AR_TWOSHOT) with the same global_scale, on every rank.
  * Requires M % 256 == 0, N % 256 == 0, K % 256 == 0, M * N <= the context's max_numel,
- * M * N / world a multiple of 256.  global_scale bounds |D_r| for every rank (agree on it first). */
+ * M * N / world a multiple of 64.  global_scale bounds |D_r| for every rank (agree on it first). */
 NVFP4_API nvfp4_status_t nvfp4_gemm_allreduce(nvfp4_ar_t h, const void* A, const void* sfa, const void* B,
                                               const void* sfb, float alpha, float global_scale, void* out,
                                               int64_t M, int64_t N, int64_t K, void* stream);

@@ -65,8 +65,11 @@ struct Params {
     uint32_t epoch;
     float gs;                        // global scale of the inputs (gs = amax / (6 * 448))
     uint64_t timeout_ns;
-    int phase;                       // -1: all phases with barriers; -2: all but phase 0 (two-shot: the
-                                     // GEMM epilogue pushed the shards); 0/1/2: that phase alone
+    int phase;                       // -1: all phases with barriers; 0/1/2: that phase alone;
+                                     // -3 / 3: two-shot with phase 0 pushing already quantized
+                                     // payloads from `payloads` (all phases / that phase alone)
+    const uint8_t* payloads;         // phase 0 from payloads: owner o's at payloads + o * payload_stride
+    int64_t payload_stride;
 };
 
 __device__ __forceinline__ uint32_t* flags_of(const Params& p, int r) {
@@ -240,6 +243,20 @@ __global__ void __launch_bounds__(AR_THREADS) ar_nvfp4_kernel(const Params p) {
 
     const int64_t shard = p.numel / n;
     const int64_t schunks = shard / 32;
+    if (p.phase == -3 || p.phase == 3) {
+        // the shards were quantized by the producer of the data (a GEMM epilogue): push them
+        for (int64_t c = first; c < schunks; c += stride) {
+            for (int k = 1; k <= n; k++) {
+                const int o = (me + k) % n;
+                uint4 pk;
+                uint32_t sc;
+                const uint8_t* src = p.payloads + (int64_t)o * p.payload_stride;
+                pk = ld_nc_v4(src + c * 16);
+                sc = *reinterpret_cast<const uint16_t*>(src + align16(shard / 2) + c * 2);
+                put_chunk(in_slot(p, o, me), shard, c, pk, sc);
+            }
+        }
+    }
     if (p.phase == -1 || p.phase == 0) {
         for (int64_t c = first; c < schunks; c += stride) {
             for (int k = 1; k <= n; k++) {
@@ -673,18 +690,31 @@ nvfp4_status_t nvfp4_ar_bf16_allreduce(nvfp4_ar_t h, const void* in, void* out, 
     return launch_bf16(h, make_params(h, in, out, numel, 0.0f, -1), algo == NVFP4_AR_TWOSHOT, (cudaStream_t)stream);
 }
 
-// GEMM whose epilogue quantizes and pushes D's shards into the owners' IN slots (phase 0 of the
-// two-shot), for the current epoch's parity region.
-static nvfp4_status_t launch_gemm_push(nvfp4_ar_t h, const void* A, const void* sfa, const void* B, const void* sfb,
-                                       float alpha, float gs, int64_t M, int64_t N, int64_t K, cudaStream_t s) {
+// The GEMM of a fused call quantizes D's shards into per-owner payloads in this rank's own
+// buffer, in the parity region the call does not use: peers write a rank's region of parity q
+// only in calls of parity q, and the next such call cannot start its pushes before this rank has
+// passed this call's second barrier, long after the payloads were pushed.
+static uint8_t* payload_scratch(nvfp4_ar_t h) {
+    return h->base + AR_FLAG_BYTES + (int64_t)((h->epoch & 1u) ^ 1u) * h->region;
+}
+
+static nvfp4_status_t launch_gemm_payload(nvfp4_ar_t h, const void* A, const void* sfa, const void* B, const void* sfb,
+                                          float alpha, float gs, int64_t M, int64_t N, int64_t K, cudaStream_t s) {
     gemm2::EpiOut q{};
     const int64_t shard = M * N / h->world;
     q.gs_inv = 1.0f / gs;
+    q.payload = payload_scratch(h);
+    q.payload_stride = payload_bytes(shard);
     q.shard = shard;
     q.sf_off = align16(shard / 2);
-    for (int o = 0; o < h->world; o++)
-        q.dst[o] = h->peer[o] + AR_FLAG_BYTES + (int64_t)(h->epoch & 1u) * h->region + (int64_t)h->rank * h->in_slot;
-    return gemm2::launch<gemm2::OUT_PUSH>(A, sfa, B, sfb, alpha, nullptr, M, N, K, s, q);
+    return gemm2::launch<gemm2::OUT_PAYLOAD>(A, sfa, B, sfb, alpha, nullptr, M, N, K, s, q);
+}
+
+static Params gemm_ar_params(nvfp4_ar_t h, void* out, int64_t numel, float gs, int phase) {
+    Params p = make_params(h, nullptr, out, numel, gs, phase);
+    p.payloads = payload_scratch(h);
+    p.payload_stride = payload_bytes(numel / h->world);
+    return p;
 }
 
 static nvfp4_status_t check_gemm_ar(nvfp4_ar_t h, const char* who, const void* A, const void* sfa, const void* B,
@@ -696,8 +726,8 @@ static nvfp4_status_t check_gemm_ar(nvfp4_ar_t h, const char* who, const void* A
         return fail(NVFP4_ERR_INVALID_ARG, "%s: operands must be 16-byte aligned", who);
     nvfp4_status_t st = check_call(h, who, A, out, M * N, NVFP4_AR_TWOSHOT, 32);
     if (st) return st;
-    if ((M * N / h->world) % 256 != 0)
-        return fail(NVFP4_ERR_INVALID_ARG, "%s: M*N/world must be a multiple of 256", who);
+    if ((M * N / h->world) % 64 != 0)
+        return fail(NVFP4_ERR_INVALID_ARG, "%s: M*N/world must be a multiple of 64", who);
     if (!(gs > 0.0f) || !isfinite(gs)) return fail(NVFP4_ERR_INVALID_ARG, "%s: global_scale must be finite and > 0", who);
     return NVFP4_OK;
 }
@@ -710,8 +740,8 @@ nvfp4_status_t nvfp4_gemm_allreduce(nvfp4_ar_t h, const void* A, const void* sfa
     if (st) return st;
     h->epoch++;
     cudaStream_t s = (cudaStream_t)stream;
-    if ((st = launch_gemm_push(h, A, sfa, B, sfb, alpha, global_scale, M, N, K, s))) return st;
-    return launch_nvfp4(h, make_params(h, nullptr, out, M * N, global_scale, -2), true, s);
+    if ((st = launch_gemm_payload(h, A, sfa, B, sfb, alpha, global_scale, M, N, K, s))) return st;
+    return launch_nvfp4(h, gemm_ar_params(h, out, M * N, global_scale, -3), true, s);
 }
 
 nvfp4_status_t nvfp4_gemm_allreduce_emulated(nvfp4_ar_t const* handles, int world, const void* const* A,
@@ -731,15 +761,18 @@ nvfp4_status_t nvfp4_gemm_allreduce_emulated(nvfp4_ar_t const* handles, int worl
     }
     cudaStream_t s = (cudaStream_t)stream;
     for (int r = 0; r < world; r++) handles[r]->epoch++;
-    // every rank's GEMM (pushes), then phase 1 of every rank, then phase 2: no kernel waits
+    // every rank's GEMM, then the push of the payloads, then phase 1, then phase 2 of every rank:
+    // no kernel waits
     for (int r = 0; r < world; r++) {
-        nvfp4_status_t st = launch_gemm_push(handles[r], A[r], sfa[r], B[r], sfb[r], alpha[r], global_scale, M, N, K, s);
+        nvfp4_status_t st =
+            launch_gemm_payload(handles[r], A[r], sfa[r], B[r], sfb[r], alpha[r], global_scale, M, N, K, s);
         if (st) return st;
     }
-    for (int ph = 1; ph <= 2; ph++)
+    const int phases[3] = {3, 1, 2};
+    for (int ph : phases)
         for (int r = 0; r < world; r++) {
-            nvfp4_status_t st = launch_nvfp4(handles[r], make_params(handles[r], nullptr, outs[r], M * N, global_scale, ph),
-                                             true, s);
+            nvfp4_status_t st =
+                launch_nvfp4(handles[r], gemm_ar_params(handles[r], outs[r], M * N, global_scale, ph), true, s);
             if (st) return st;
         }
     return NVFP4_OK;

@@ -201,17 +201,18 @@ __device__ unsigned long long g_gemm2_prof[296][16];
 //   OUT_BF16 / OUT_F32  D through shared-memory staging and TMA stores;
 //   OUT_NVFP4           D = bf16(alpha * acc) quantized with a given global scale into packed
 //                       [M][N/2] codes and block scales in the tcgen05 layout of an M x N matrix;
-//   OUT_PUSH            the same quantization, written in the all-reduce payload layout into the
-//                       IN slot of the rank that owns the element's shard (two-shot reduce-scatter
-//                       step of a row-parallel GEMM; the slots may be peer memory).
-constexpr int OUT_BF16 = 0, OUT_F32 = 1, OUT_NVFP4 = 2, OUT_PUSH = 3;
+//   OUT_PAYLOAD         the same quantization, written in the all-reduce payload layout, one
+//                       payload per owner of a shard of D (this rank's own memory), ready for the
+//                       two-shot all-reduce's push to the owners.
+constexpr int OUT_BF16 = 0, OUT_F32 = 1, OUT_NVFP4 = 2, OUT_PAYLOAD = 3;
 struct EpiOut {
     uint8_t* packed;             // OUT_NVFP4
     uint8_t* sf;
-    float gs_inv;                // OUT_NVFP4, OUT_PUSH
-    uint8_t* dst[8];             // OUT_PUSH: payload base in the IN slot of owner o
-    int64_t shard;               // OUT_PUSH: elements per owner (a multiple of 256)
-    int64_t sf_off;              // OUT_PUSH: byte offset of the scales in a payload
+    float gs_inv;                // OUT_NVFP4, OUT_PAYLOAD
+    uint8_t* payload;            // OUT_PAYLOAD: owner o's payload at payload + o * payload_stride
+    int64_t payload_stride;
+    int64_t shard;               // OUT_PAYLOAD: elements per owner (a multiple of 64)
+    int64_t sf_off;              // OUT_PAYLOAD: byte offset of the scales in a payload
 };
 
 template <int kOut>
@@ -220,10 +221,8 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
              const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
              const __grid_constant__ CUtensorMap tmap_d, const EpiOut qout, int M, int N, int K, float alpha) {
     constexpr bool kOutF32 = kOut == OUT_F32;
-    constexpr bool kQuantOut = kOut == OUT_NVFP4 || kOut == OUT_PUSH;
-    // two sets of four epilogue warps take alternate chunks (one set for OUT_PUSH, whose tile
-    // rows are staged across all chunks)
-    constexpr int ESETS = kOut == OUT_PUSH ? 1 : 2;
+    constexpr bool kQuantOut = kOut == OUT_NVFP4 || kOut == OUT_PAYLOAD;
+    constexpr int ESETS = 2;                              // epilogue warp sets (alternate chunks)
     constexpr int CHUNK = kOutF32 ? 32 : 64;          // output columns per 128-byte staging row
     constexpr int NCHUNK = BN / CHUNK;
     constexpr int OVL = OVL_COLS / CHUNK;             // chunks inside the overlapping columns
@@ -481,7 +480,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
             }
         }
         __syncwarp();
-    } else if (warp < 6 || ESETS == 2) {
+    } else {
         // -------------------------------------------------------- epilogue ----
         const int quad = warp & 3;
         const int row = quad * 32 + lane;                     // row within this CTA's 128
@@ -490,7 +489,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
         const bool issuer = lane == 0 && (warp == 2 || warp == EPI_WARP1);
         // the last chunk (in drain order) inside the shared columns that this set reads
         const int last_shared = (OVL - 1 >= eset) ? OVL - 1 - ((OVL - 1 - eset) % ESETS) : -1;
-        int sbuf = ESETS == 2 ? eset : 0;
+        const int sbuf = eset;                                // one staging buffer per set
         int iter = 0;
         for (int tile = pair; tile < ntiles; tile += npairs, iter++) {
             const int tm = tile % num_m, tn = tile / num_m;
@@ -544,44 +543,19 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                         const int64_t off = ((m >> 7) * (N / 64) + (col >> 6)) * 512 + (m & 31) * 16 + ((m >> 5) & 3) * 4;
                         *reinterpret_cast<uint32_t*>(qout.sf + off) = sfw;
                     } else {
-                        // Stage the tile row's codes (128 B, 16-byte units XOR-swizzled by row)
-                        // and scale words (16 B) in the staging buffers; after the last chunk the
-                        // four warps store whole 128-byte row segments into the owner's slot, so
-                        // that the pushes cross NVLink as full lines, not 16-byte pieces.
-                        uint8_t* stg = smem + OFF_EPI;
-                        uint8_t* stg_sf = smem + OFF_EPI + EPI_BYTES;
-                        *reinterpret_cast<uint4*>(stg + row * 128 + (((2 * c) ^ (row & 7)) << 4)) =
-                            make_uint4(q[0], q[1], q[2], q[3]);
-                        *reinterpret_cast<uint4*>(stg + row * 128 + (((2 * c + 1) ^ (row & 7)) << 4)) =
-                            make_uint4(q[4], q[5], q[6], q[7]);
-                        *reinterpret_cast<uint32_t*>(stg_sf + row * 16 + c * 4) = sfw;
-                        if (idx == NCHUNK - 1) {
-                            epi_bar();
-                            // element e of the flattened D: owner e / shard; a row segment of
-                            // 256 elements (128 B of codes, 16 B of scales) lies in one shard
-#pragma unroll
-                            for (int i = 0; i < 8; i++) {
-                                const int id = i * 128 + row, rr = id >> 3, u = id & 7;
-                                const int64_t e = (int64_t)(m0 + rr) * N + (int64_t)tn * BN;
-                                const int o = (int)(e / qout.shard);
-                                st_v4(qout.dst[o] + (e - (int64_t)o * qout.shard) / 2 + u * 16,
-                                      *reinterpret_cast<const uint4*>(stg + rr * 128 + ((u ^ (rr & 7)) << 4)));
-                            }
-                            {
-                                const int64_t e = (int64_t)(m0 + row) * N + (int64_t)tn * BN;
-                                const int o = (int)(e / qout.shard);
-                                st_v4(qout.dst[o] + qout.sf_off + (e - (int64_t)o * qout.shard) / 16,
-                                      *reinterpret_cast<const uint4*>(stg_sf + row * 16));
-                            }
-                            epi_bar();                    // staging free for the next tile
-                        }
+                        // element e of the flattened D: owner e / shard; chunks of 32 elements
+                        // (16 bytes of codes, 2 scale bytes) at their index inside the shard
+                        const int64_t e = (int64_t)(m0 + row) * N + (int64_t)tn * BN + c * CHUNK;
+                        const int o = (int)(e / qout.shard);
+                        const int64_t ch = (e - (int64_t)o * qout.shard) / 32;
+                        uint8_t* d = qout.payload + (int64_t)o * qout.payload_stride;
+                        st_v4(d + ch * 16, make_uint4(q[0], q[1], q[2], q[3]));
+                        st_v4(d + ch * 16 + 16, make_uint4(q[4], q[5], q[6], q[7]));
+                        *reinterpret_cast<uint32_t*>(d + qout.sf_off + ch * 2) = sfw;
                     }
                     continue;
                 }
-                if (issuer) {
-                    if (ESETS == 2) bulk_wait_read_n<0>();      // one staging buffer per set
-                    else bulk_wait_read1();
-                }
+                if (issuer) bulk_wait_read_n<0>();            // the set's previous store has read it
                 epi_bar_set(eset);
                 uint8_t* srow = smem + OFF_EPI + sbuf * EPI_BYTES + row * 128;
                 if constexpr (kOutF32) {
@@ -609,12 +583,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                     tma_store_2d(&tmap_d, base + OFF_EPI + sbuf * EPI_BYTES, tn * BN + c * CHUNK, m0);
                     bulk_commit();
                 }
-                if (ESETS == 1) sbuf ^= 1;
             }
         }
         if (issuer) bulk_wait_all();
-        // pushed payloads (peer memory) are complete before anything this rank does next
-        if constexpr (kOut == OUT_PUSH) __threadfence_system();
     }
 
     __syncwarp();
@@ -630,7 +601,7 @@ template <int kOut>
 nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void* sfb, float alpha, void* D, int64_t M,
                       int64_t N, int64_t K, cudaStream_t s, const EpiOut& qout = EpiOut{}) {
     constexpr bool kOutF32 = kOut == OUT_F32;
-    constexpr bool kQuantOut = kOut == OUT_NVFP4 || kOut == OUT_PUSH;
+    constexpr bool kQuantOut = kOut == OUT_NVFP4 || kOut == OUT_PAYLOAD;
     CUtensorMap ta, tb, tsa, tsb, td;
     nvfp4_status_t st;
     if ((st = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, M, K / 2, 128, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
