@@ -67,9 +67,9 @@ struct Params {
     uint64_t timeout_ns;
     int phase;                       // -1: all phases with barriers; 0/1/2: that phase alone;
                                      // -3 / 3: two-shot with phase 0 pushing already quantized
-                                     // payloads from `payloads` (all phases / that phase alone)
-    const uint8_t* payloads;         // phase 0 from payloads: owner o's at payloads + o * payload_stride
-    int64_t payload_stride;
+                                     // data (all phases / that phase alone)
+    const uint8_t* q_codes;          // phase 0 from quantized data: codes [numel / 2] and scales
+    const uint8_t* q_scales;         // [numel / 16] of the whole input, flat
 };
 
 __device__ __forceinline__ uint32_t* flags_of(const Params& p, int r) {
@@ -248,11 +248,9 @@ __global__ void __launch_bounds__(AR_THREADS) ar_nvfp4_kernel(const Params p) {
         for (int64_t c = first; c < schunks; c += stride) {
             for (int k = 1; k <= n; k++) {
                 const int o = (me + k) % n;
-                uint4 pk;
-                uint32_t sc;
-                const uint8_t* src = p.payloads + (int64_t)o * p.payload_stride;
-                pk = ld_nc_v4(src + c * 16);
-                sc = *reinterpret_cast<const uint16_t*>(src + align16(shard / 2) + c * 2);
+                const int64_t e32 = (int64_t)o * schunks + c;     // chunk of 32 elements of the input
+                const uint4 pk = ld_nc_v4(p.q_codes + e32 * 16);
+                const uint32_t sc = *reinterpret_cast<const uint16_t*>(p.q_scales + e32 * 2);
                 put_chunk(in_slot(p, o, me), shard, c, pk, sc);
             }
         }
@@ -690,30 +688,27 @@ nvfp4_status_t nvfp4_ar_bf16_allreduce(nvfp4_ar_t h, const void* in, void* out, 
     return launch_bf16(h, make_params(h, in, out, numel, 0.0f, -1), algo == NVFP4_AR_TWOSHOT, (cudaStream_t)stream);
 }
 
-// The GEMM of a fused call quantizes D's shards into per-owner payloads in this rank's own
-// buffer, in the parity region the call does not use: peers write a rank's region of parity q
-// only in calls of parity q, and the next such call cannot start its pushes before this rank has
-// passed this call's second barrier, long after the payloads were pushed.
-static uint8_t* payload_scratch(nvfp4_ar_t h) {
+// The GEMM of a fused call quantizes D (codes [M][N/2], flat scales) into this rank's own buffer,
+// in the parity region the call does not use: peers write a rank's region of parity q only in
+// calls of parity q, and the next such call cannot start its pushes before this rank has passed
+// this call's second barrier, long after the quantized data was pushed.
+static uint8_t* scratch_codes(nvfp4_ar_t h) {
     return h->base + AR_FLAG_BYTES + (int64_t)((h->epoch & 1u) ^ 1u) * h->region;
 }
+static uint8_t* scratch_scales(nvfp4_ar_t h, int64_t numel) { return scratch_codes(h) + align16(numel / 2); }
 
 static nvfp4_status_t launch_gemm_payload(nvfp4_ar_t h, const void* A, const void* sfa, const void* B, const void* sfb,
                                           float alpha, float gs, int64_t M, int64_t N, int64_t K, cudaStream_t s) {
     gemm2::EpiOut q{};
-    const int64_t shard = M * N / h->world;
     q.gs_inv = 1.0f / gs;
-    q.payload = payload_scratch(h);
-    q.payload_stride = payload_bytes(shard);
-    q.shard = shard;
-    q.sf_off = align16(shard / 2);
-    return gemm2::launch<gemm2::OUT_PAYLOAD>(A, sfa, B, sfb, alpha, nullptr, M, N, K, s, q);
+    q.sf = scratch_scales(h, M * N);
+    return gemm2::launch<gemm2::OUT_PAYLOAD>(A, sfa, B, sfb, alpha, scratch_codes(h), M, N, K, s, q);
 }
 
 static Params gemm_ar_params(nvfp4_ar_t h, void* out, int64_t numel, float gs, int phase) {
     Params p = make_params(h, nullptr, out, numel, gs, phase);
-    p.payloads = payload_scratch(h);
-    p.payload_stride = payload_bytes(numel / h->world);
+    p.q_codes = scratch_codes(h);
+    p.q_scales = scratch_scales(h, numel);
     return p;
 }
 

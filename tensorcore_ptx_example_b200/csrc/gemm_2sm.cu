@@ -201,18 +201,15 @@ __device__ unsigned long long g_gemm2_prof[296][16];
 //   OUT_BF16 / OUT_F32  D through shared-memory staging and TMA stores;
 //   OUT_NVFP4           D = bf16(alpha * acc) quantized with a given global scale into packed
 //                       [M][N/2] codes and block scales in the tcgen05 layout of an M x N matrix;
-//   OUT_PAYLOAD         the same quantization, written in the all-reduce payload layout, one
-//                       payload per owner of a shard of D (this rank's own memory), ready for the
-//                       two-shot all-reduce's push to the owners.
+//   OUT_PAYLOAD         the same quantization in the flat layout of the all-reduce payloads:
+//                       codes [M][N/2] through the staging buffers and TMA stores (tmap_d), one
+//                       scale byte per 16 elements at flat_sf[(m * N + n) / 16], for the two-shot
+//                       all-reduce to push to the owners of the shards.
 constexpr int OUT_BF16 = 0, OUT_F32 = 1, OUT_NVFP4 = 2, OUT_PAYLOAD = 3;
 struct EpiOut {
     uint8_t* packed;             // OUT_NVFP4
-    uint8_t* sf;
+    uint8_t* sf;                 // OUT_NVFP4: tcgen05 layout; OUT_PAYLOAD: flat
     float gs_inv;                // OUT_NVFP4, OUT_PAYLOAD
-    uint8_t* payload;            // OUT_PAYLOAD: owner o's payload at payload + o * payload_stride
-    int64_t payload_stride;
-    int64_t shard;               // OUT_PAYLOAD: elements per owner (a multiple of 64)
-    int64_t sf_off;              // OUT_PAYLOAD: byte offset of the scales in a payload
 };
 
 template <int kOut>
@@ -258,7 +255,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
         prefetch_tmap(&tmap_b);
         prefetch_tmap(&tmap_sfa);
         prefetch_tmap(&tmap_sfb);
-        if (!kQuantOut) prefetch_tmap(&tmap_d);
+        if (kOut != OUT_NVFP4) prefetch_tmap(&tmap_d);
         for (int s = 0; s < STAGES; s++) {
             // the leader's producer (arrive.expect_tx, A/B bytes of both CTAs) and the 4 scale
             // warps of each CTA (the stage's scale slot is in TMEM)
@@ -525,7 +522,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                 if constexpr (kQuantOut) {
                     // bf16(alpha * acc) exactly as the bf16 output, then four 16-element blocks
                     // quantized with the quantizer's block function: 32 bytes of codes and one
-                    // 32-bit word of block scales per thread and chunk, stored directly.
+                    // 32-bit word of block scales per thread and chunk.
                     uint32_t w[32];
 #pragma unroll
                     for (int i = 0; i < 32; i++) {
@@ -537,23 +534,29 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
 #pragma unroll
                     for (int blk = 0; blk < 4; blk++)
                         sfw |= q16_bf16(w + 8 * blk, qout.gs_inv, q[2 * blk], q[2 * blk + 1]) << (8 * blk);
+                    const int64_t m = m0 + row, col = (int64_t)tn * BN + c * CHUNK;
                     if constexpr (kOut == OUT_NVFP4) {
-                        const int64_t m = m0 + row, col = (int64_t)tn * BN + c * CHUNK;
                         st_global_v8(qout.packed + m * (N / 2) + col / 2, q);
                         const int64_t off = ((m >> 7) * (N / 64) + (col >> 6)) * 512 + (m & 31) * 16 + ((m >> 5) & 3) * 4;
                         *reinterpret_cast<uint32_t*>(qout.sf + off) = sfw;
+                        continue;
                     } else {
-                        // element e of the flattened D: owner e / shard; chunks of 32 elements
-                        // (16 bytes of codes, 2 scale bytes) at their index inside the shard
-                        const int64_t e = (int64_t)(m0 + row) * N + (int64_t)tn * BN + c * CHUNK;
-                        const int o = (int)(e / qout.shard);
-                        const int64_t ch = (e - (int64_t)o * qout.shard) / 32;
-                        uint8_t* d = qout.payload + (int64_t)o * qout.payload_stride;
-                        st_v4(d + ch * 16, make_uint4(q[0], q[1], q[2], q[3]));
-                        st_v4(d + ch * 16 + 16, make_uint4(q[4], q[5], q[6], q[7]));
-                        *reinterpret_cast<uint32_t*>(d + qout.sf_off + ch * 2) = sfw;
+                        // scales straight to the flat array; codes (32 B per row) through the
+                        // set's staging buffer and a TMA store of the 128 x 32 B box
+                        if (m < M) *reinterpret_cast<uint32_t*>(qout.sf + (m * N + col) / 16) = sfw;
+                        if (issuer) bulk_wait_read_n<0>();
+                        epi_bar_set(eset);
+                        uint8_t* srow = smem + OFF_EPI + sbuf * EPI_BYTES + row * 32;
+                        *reinterpret_cast<uint4*>(srow) = make_uint4(q[0], q[1], q[2], q[3]);
+                        *reinterpret_cast<uint4*>(srow + 16) = make_uint4(q[4], q[5], q[6], q[7]);
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        epi_bar_set(eset);
+                        if (issuer && m0 < M) {
+                            tma_store_2d(&tmap_d, base + OFF_EPI + sbuf * EPI_BYTES, (int)(col / 2), m0);
+                            bulk_commit();
+                        }
+                        continue;
                     }
-                    continue;
                 }
                 if (issuer) bulk_wait_read_n<0>();            // the set's previous store has read it
                 epi_bar_set(eset);
@@ -601,7 +604,6 @@ template <int kOut>
 nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void* sfb, float alpha, void* D, int64_t M,
                       int64_t N, int64_t K, cudaStream_t s, const EpiOut& qout = EpiOut{}) {
     constexpr bool kOutF32 = kOut == OUT_F32;
-    constexpr bool kQuantOut = kOut == OUT_NVFP4 || kOut == OUT_PAYLOAD;
     CUtensorMap ta, tb, tsa, tsb, td;
     nvfp4_status_t st;
     if ((st = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, M, K / 2, 128, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
@@ -616,7 +618,9 @@ nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void*
     if ((st = make_tmap_2d(&tsb, sfb, CU_TENSOR_MAP_DATA_TYPE_UINT32, 128, (N / 128) * (K / 64), 512, 128, 4,
                            CU_TENSOR_MAP_SWIZZLE_NONE)))
         return st;
-    if (kQuantOut) memset(&td, 0, sizeof(td));       // unused: the epilogue stores NVFP4 directly
+    if (kOut == OUT_NVFP4) memset(&td, 0, sizeof(td));        // unused: the epilogue stores directly
+    else if (kOut == OUT_PAYLOAD) st = make_tmap_2d(&td, D, CU_TENSOR_MAP_DATA_TYPE_UINT8, N / 2, M, N / 2, 32, 128,
+                                                    CU_TENSOR_MAP_SWIZZLE_NONE);
     else if (kOutF32) st = make_tmap_2d(&td, D, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M, N * 4, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B);
     else st = make_tmap_2d(&td, D, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, N, M, N * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
