@@ -526,8 +526,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                     uint32_t w[32];
 #pragma unroll
                     for (int i = 0; i < 32; i++) {
-                        const __nv_bfloat162 p = __floats2bfloat162_rn(__fmul_rn(__uint_as_float(r[2 * i]), alpha),
-                                                                       __fmul_rn(__uint_as_float(r[2 * i + 1]), alpha));
+                        float y0, y1;
+                        mul2_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]), alpha, y0, y1);
+                        const __nv_bfloat162 p = __floats2bfloat162_rn(y0, y1);
                         w[i] = *reinterpret_cast<const uint32_t*>(&p);
                     }
                     uint32_t q[8], sfw = 0;
@@ -573,8 +574,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
 #pragma unroll
                         for (int i = 0; i < 4; i++) {
                             const int e = 8 * j + 2 * i;
-                            const __nv_bfloat162 p = __floats2bfloat162_rn(__fmul_rn(__uint_as_float(r[e]), alpha),
-                                                                           __fmul_rn(__uint_as_float(r[e + 1]), alpha));
+                            float y0, y1;
+                            mul2_rn(__uint_as_float(r[e]), __uint_as_float(r[e + 1]), alpha, y0, y1);
+                            const __nv_bfloat162 p = __floats2bfloat162_rn(y0, y1);
                             o[i] = *reinterpret_cast<const uint32_t*>(&p);
                         }
                         *reinterpret_cast<uint4*>(srow + ((j ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
