@@ -29,7 +29,7 @@ def global_scale(nv, inputs):
     return nv.global_scale_from_amax(a)
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("world", [2, 3, 4, 6, 8])
 @pytest.mark.parametrize("algo", ["oneshot", "twoshot"])
 def test_nvfp4_allreduce_bitexact(nv, oracle, world, algo):
     numel = 32 * world * 37                       # several blocks, not a power of two

@@ -41,9 +41,9 @@ def partials(nv, ops, alphas, M, N, K):
     return [nv.gemm(pa, sa, pb, sb, M, N, K, alpha=al) for (pa, sa, pb, sb), al in zip(ops, alphas)]
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
 def test_gemm_allreduce_matches_unfused_and_oracle(nv, oracle, world):
-    M, N, K = 256, 512, 512
+    M, N, K = 256, 768 if world == 3 else 512, 512
     ops, alphas = rank_operands(nv, world, M, N, K, seed=40 * world)
     ds = partials(nv, ops, alphas, M, N, K)
     torch.cuda.synchronize()
