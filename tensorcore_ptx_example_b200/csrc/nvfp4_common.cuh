@@ -152,12 +152,14 @@ __device__ __forceinline__ uint32_t q16(const float* v, float gs_inv, uint32_t& 
 }
 
 // The same for 16 bf16 values packed two per word (element 2i in the low half of word i).
-// The amax is taken on the bit patterns: for finite bf16, |x| orders like (bits & 0x7FFF),
-// which two-lane 16-bit max instructions reduce four words at a time.
+// The amax: max.xorsign.abs.bf16x2 keeps per lane the larger magnitude of two bf16 pairs (its
+// sign is the xor of the signs, cleared afterwards), one instruction per word; for finite
+// values that is exactly max |x| of each half.
 __device__ __forceinline__ uint32_t q16_bf16(const uint32_t* w, float gs_inv, uint32_t& w0, uint32_t& w1) {
-    uint32_t m = 0;
+    uint32_t m = w[0];
 #pragma unroll
-    for (int i = 0; i < 8; i++) m = __vmaxu2(m, w[i] & 0x7FFF7FFFu);
+    for (int i = 1; i < 8; i++) asm("max.xorsign.abs.bf16x2 %0, %0, %1;" : "+r"(m) : "r"(w[i]));
+    m &= 0x7FFF7FFFu;
     const float amax = __uint_as_float(((m >> 16) > (m & 0xFFFFu) ? (m >> 16) : (m & 0xFFFFu)) << 16);
     float inv;
     const uint32_t code = block_scale(amax, gs_inv, inv);
