@@ -137,21 +137,13 @@ __device__ __forceinline__ void quant32(const __nv_bfloat16* x, float gs_inv, ui
     uint4 raw[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) raw[i] = ld_nc_v4(reinterpret_cast<const uint8_t*>(x) + 16 * i);
-    uint32_t w[8];
+    uint32_t w[4];
     scales = 0;
 #pragma unroll
     for (int b = 0; b < 2; b++) {
-        float v[16];
-#pragma unroll
-        for (int i = 0; i < 2; i++) {
-            const uint32_t q[4] = {raw[2 * b + i].x, raw[2 * b + i].y, raw[2 * b + i].z, raw[2 * b + i].w};
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                v[8 * i + 2 * k] = __uint_as_float(q[k] << 16);
-                v[8 * i + 2 * k + 1] = __uint_as_float(q[k] & 0xFFFF0000u);
-            }
-        }
-        scales |= q16(v, gs_inv, w[2 * b], w[2 * b + 1]) << (8 * b);
+        const uint32_t q[8] = {raw[2 * b].x,     raw[2 * b].y,     raw[2 * b].z,     raw[2 * b].w,
+                               raw[2 * b + 1].x, raw[2 * b + 1].y, raw[2 * b + 1].z, raw[2 * b + 1].w};
+        scales |= q16_bf16(q, gs_inv, w[2 * b], w[2 * b + 1]) << (8 * b);
     }
     packed = make_uint4(w[0], w[1], w[2], w[3]);
 }
