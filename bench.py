@@ -276,6 +276,15 @@ def decode_bench(nv, steps, warmup, flush):
     e1.record(s)
     torch.cuda.synchronize()
     ms_stream = e0.elapsed_time(e1) / calls
+    # the same stream with the weights marked constant (B streams before each dependency wait)
+    torch.cuda._sleep(HIDE_HOST_CYCLES * 4)
+    e0.record(s)
+    for i in range(calls):
+        pbi, sbi = bs[i % weight_sets]
+        nv.gemm(pa, sa, pbi, sbi, M, N, K, alpha=alpha, out=d, weights_const=True)
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms_stream_wc = e0.elapsed_time(e1) / calls
     del bs
     # algorithmic bytes: B and its scales, A and its scales, D
     byts = N * K // 2 + N * K // 16 + M * K // 2 + nv.sf_bytes(M, K) + M * N * 2
@@ -292,7 +301,9 @@ def decode_bench(nv, steps, warmup, flush):
             "stream": {"us_per_call": round(ms_stream * 1e3, 2), "calls": calls, "weight_sets": weight_sets,
                        "roofline": {"bound": "hbm", "achieved": round(gbs_stream, 1), "peak": hbm, "unit": "GB/s",
                                     "frac": round(gbs_stream / hbm, 4)},
-                       "timing": "back-to-back calls over 8 different B (264 MB > L2), one event pair"},
+                       "timing": "back-to-back calls over 8 different B (264 MB > L2), one event pair",
+                       "us_per_call_weights_const": round(ms_stream_wc * 1e3, 2),
+                       "frac_weights_const": round(byts / (ms_stream_wc * 1e-3) / 1e9 / hbm, 4)},
             "launches_per_call": 2}
 
 

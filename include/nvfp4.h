@@ -138,6 +138,15 @@ NVFP4_API size_t nvfp4_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 NVFP4_API nvfp4_status_t nvfp4_gemm_bf16_ws(const void* A, const void* sfa, const void* B, const void* sfb,
                                   float alpha, void* D, int64_t M, int64_t N, int64_t K, void* workspace,
                                   size_t workspace_bytes, void* stream);
+/* nvfp4_gemm_bf16 with flags (an extension of this library).  NVFP4_GEMM_WEIGHTS_CONST: B and
+ * sfb are not written by work queued before this call on `stream` (model weights).  The decode
+ * kernel (0 < M < 128) then starts streaming B before it waits for the preceding kernel
+ * (programmatic dependent launch), overlapping that kernel's tail; A and sfa are still read only
+ * after the wait.  The tiled kernels ignore the flag.  Results are identical with or without it. */
+#define NVFP4_GEMM_WEIGHTS_CONST 1
+NVFP4_API nvfp4_status_t nvfp4_gemm_bf16_flags(const void* A, const void* sfa, const void* B, const void* sfb,
+                                     float alpha, void* D, int64_t M, int64_t N, int64_t K, int flags,
+                                     void* stream);
 /* Same kernel, raw fp32 accumulators (no alpha) into D (fp32 row-major M x N). */
 NVFP4_API nvfp4_status_t nvfp4_gemm_f32(const void* A, const void* sfa, const void* B, const void* sfb,
                               float* D, int64_t M, int64_t N, int64_t K, void* stream);

@@ -43,6 +43,7 @@ SIGNATURES = {
     "nvfp4_gemm_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64]),
     "nvfp4_gemm_bf16_ws": (_I, [_P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
     "nvfp4_gemm_quantize": (_I, [_P, _P, _P, _P, _F, _F, _P, _P, _I64, _I64, _I64, _P]),
+    "nvfp4_gemm_bf16_flags": (_I, [_P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _I, _P]),
     "nvfp4_diag_e2m1_encode": (_I, [_P, _P, _I64, _P]),
     "nvfp4_diag_e4m3_encode": (_I, [_P, _P, _I64, _P]),
     "nvfp4_diag_mma_peak": (_I, [_I, _I, _I, _P]),
@@ -178,13 +179,23 @@ def dequantize(packed, sf, rows: int, cols: int, global_scale: float, out=None, 
 
 
 # -------------------------------------------------------------------- GEMM ----
-def gemm(a_packed, sfa, b_packed, sfb, M: int, N: int, K: int, alpha: float = 1.0, out=None, stream=None):
-    """D = bf16(alpha * A @ B^T) for NVFP4 A [M, K] and B [N, K]."""
+NVFP4_GEMM_WEIGHTS_CONST = 1
+
+
+def gemm(a_packed, sfa, b_packed, sfb, M: int, N: int, K: int, alpha: float = 1.0, out=None, stream=None,
+         weights_const: bool = False):
+    """D = bf16(alpha * A @ B^T) for NVFP4 A [M, K] and B [N, K].  weights_const: B and its
+    scales are not written by earlier work on the stream (lets the decode kernel stream B
+    before its dependency wait)."""
     import torch
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=a_packed.device)
-    check(lib().nvfp4_gemm_bf16(_ptr(a_packed), _ptr(sfa), _ptr(b_packed), _ptr(sfb), ctypes.c_float(alpha),
-                                _ptr(out), M, N, K, _stream(stream)))
+    if weights_const:
+        check(lib().nvfp4_gemm_bf16_flags(_ptr(a_packed), _ptr(sfa), _ptr(b_packed), _ptr(sfb), ctypes.c_float(alpha),
+                                          _ptr(out), M, N, K, NVFP4_GEMM_WEIGHTS_CONST, _stream(stream)))
+    else:
+        check(lib().nvfp4_gemm_bf16(_ptr(a_packed), _ptr(sfa), _ptr(b_packed), _ptr(sfb), ctypes.c_float(alpha),
+                                    _ptr(out), M, N, K, _stream(stream)))
     return out
 
 

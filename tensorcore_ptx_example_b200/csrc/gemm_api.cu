@@ -55,7 +55,8 @@ static nvfp4_status_t internal_workspace(size_t need, void** out) {
 
 template <bool kOutF32>
 static nvfp4_status_t dispatch(const void* A, const void* sfa, const void* B, const void* sfb, float alpha, void* D,
-                               int64_t M, int64_t N, int64_t K, void* ws, size_t ws_bytes, cudaStream_t s) {
+                               int64_t M, int64_t N, int64_t K, void* ws, size_t ws_bytes, cudaStream_t s,
+                               int flags = 0) {
     nvfp4_status_t st = check_args(A, sfa, B, sfb, D, M, N, K);
     if (st != NVFP4_OK) return st;
     if (small_m(M)) {
@@ -65,7 +66,8 @@ static nvfp4_status_t dispatch(const void* A, const void* sfa, const void* B, co
         } else if (!aligned16(ws)) {
             return fail(NVFP4_ERR_INVALID_ARG, "gemm: workspace must be 16-byte aligned");
         }
-        return gsmall::launch<kOutF32>(A, sfa, B, sfb, alpha, D, M, N, K, ws, ws_bytes, s);
+        return gsmall::launch<kOutF32>(A, sfa, B, sfb, alpha, D, M, N, K, ws, ws_bytes, s,
+                                       (flags & NVFP4_GEMM_WEIGHTS_CONST) != 0);
     }
     return gemm2::launch<kOutF32 ? gemm2::OUT_F32 : gemm2::OUT_BF16>(A, sfa, B, sfb, alpha, D, M, N, K, s);
 }
@@ -81,6 +83,13 @@ nvfp4_status_t nvfp4_gemm_bf16(const void* A, const void* sfa, const void* B, co
                                int64_t M, int64_t N, int64_t K, void* stream) {
     clear_error();
     return gemm::dispatch<false>(A, sfa, B, sfb, alpha, D, M, N, K, nullptr, 0, (cudaStream_t)stream);
+}
+
+nvfp4_status_t nvfp4_gemm_bf16_flags(const void* A, const void* sfa, const void* B, const void* sfb, float alpha,
+                                     void* D, int64_t M, int64_t N, int64_t K, int flags, void* stream) {
+    clear_error();
+    if (flags & ~NVFP4_GEMM_WEIGHTS_CONST) return fail(NVFP4_ERR_INVALID_ARG, "gemm_flags: unknown flag bits");
+    return gemm::dispatch<false>(A, sfa, B, sfb, alpha, D, M, N, K, nullptr, 0, (cudaStream_t)stream, flags);
 }
 
 size_t nvfp4_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {

@@ -115,7 +115,7 @@ __device__ __forceinline__ void tc_mma_rt(uint32_t d, uint64_t a, uint64_t b, ui
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                   const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, float* __restrict__ ws, int M,
-                  int N, int K, int ks, int mp) {
+                  int N, int K, int ks, int mp, int b_const) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -161,8 +161,10 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
     const uint32_t tmem = *tmem_slot;
     // Programmatic dependent launch: the set-up above overlapped the previous kernel in the
     // stream; its results are visible after this wait.  The split-K reduction may launch now
-    // (it waits for this grid in turn).
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // (it waits for this grid in turn).  With b_const (B and its scales are not written by
+    // earlier work in the stream, e.g. weights) the producer first issues the B loads of its
+    // first stages and waits afterwards.
+    if (!(b_const && warp == 0)) asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (warp == 0) {
@@ -172,22 +174,45 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
             uint32_t phase = 0;
             bool ok = true;
             long fills = 0;
+            // b_const: B and its scales of the first S stages (the ring's first use needs no
+            // wait), issued before the dependency wait; their A halves follow it
+            int pre = 0;
+            if (b_const) {
+                for (int u = blockIdx.x; u < units && pre < S; u += gridDim.x) {
+                    const int sp = u % splits, nt = u / splits;
+                    for (int b = 0; b < nbox && pre < S; b++, pre++) {
+                        const int k = sp * ks + 256 * b;
+                        const uint32_t sbase = base + pre * SB, fb = full_bar(pre), lb = sf_landed(pre);
+                        mbar_arrive_expect_tx(lb, (uint32_t)SF_STAGE);
+                        bulk_load(sbase + B_BOX + mp * 128, sfb + ((int64_t)nt * katoms + k / 64) * 512, 2048, lb);
+                        mbar_arrive_expect_tx(fb, (uint32_t)(B_BOX + mp * 128));
+                        tma_load_2d(sbase, &tmap_b, k / 2, nt * 128, fb);
+                    }
+                }
+                asm volatile("griddepcontrol.wait;" ::: "memory");
+            }
             for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
                 const int sp = u % splits, nt = u / splits;
                 for (int b = 0; b < nbox; b++) {
-                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_PRODUCER)) {
-                        ok = false;
-                        break;
-                    }
                     const int k = sp * ks + 256 * b;
                     const uint32_t sbase = base + stage * SB, fb = full_bar(stage), lb = sf_landed(stage);
-                    // scales first (the scale warps move them on to TMEM), then B and A
-                    mbar_arrive_expect_tx(lb, (uint32_t)SF_STAGE);
-                    bulk_load(sbase + B_BOX + mp * 128, sfb + ((int64_t)nt * katoms + k / 64) * 512, 2048, lb);
-                    bulk_load(sbase + B_BOX + mp * 128 + 2048, sfa + (int64_t)(k / 64) * 512, 2048, lb);
-                    mbar_arrive_expect_tx(fb, (uint32_t)(B_BOX + mp * 128));
-                    tma_load_2d(sbase, &tmap_b, k / 2, nt * 128, fb);
-                    tma_load_2d(sbase + B_BOX, &tmap_a, k / 2, 0, fb);
+                    if (fills < pre) {
+                        // B already on its way: the A halves of the stage
+                        bulk_load(sbase + B_BOX + mp * 128 + 2048, sfa + (int64_t)(k / 64) * 512, 2048, lb);
+                        tma_load_2d(sbase + B_BOX, &tmap_a, k / 2, 0, fb);
+                    } else {
+                        if (!mbar_wait(empty_bar(stage), phase ^ 1u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_PRODUCER)) {
+                            ok = false;
+                            break;
+                        }
+                        // scales first (the scale warps move them on to TMEM), then B and A
+                        mbar_arrive_expect_tx(lb, (uint32_t)SF_STAGE);
+                        bulk_load(sbase + B_BOX + mp * 128, sfb + ((int64_t)nt * katoms + k / 64) * 512, 2048, lb);
+                        bulk_load(sbase + B_BOX + mp * 128 + 2048, sfa + (int64_t)(k / 64) * 512, 2048, lb);
+                        mbar_arrive_expect_tx(fb, (uint32_t)(B_BOX + mp * 128));
+                        tma_load_2d(sbase, &tmap_b, k / 2, nt * 128, fb);
+                        tma_load_2d(sbase + B_BOX, &tmap_a, k / 2, 0, fb);
+                    }
                     fills++;
                     if (++stage == S) { stage = 0; phase ^= 1u; }
                 }
@@ -383,7 +408,7 @@ inline size_t workspace_bytes(int64_t M, int64_t N, int64_t K) {
 
 template <bool kOutF32>
 nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void* sfb, float alpha, void* D,
-                      int64_t M, int64_t N, int64_t K, void* ws, size_t ws_bytes, cudaStream_t s) {
+                      int64_t M, int64_t N, int64_t K, void* ws, size_t ws_bytes, cudaStream_t s, bool b_const = false) {
     const int ks = split_k(K);
     if (ks == 0) return fail(NVFP4_ERR_INVALID_ARG, "gemm (small M): K %% 256 != 0");
     if (N % 128 != 0) return fail(NVFP4_ERR_INVALID_ARG, "gemm (small M): N %% 128 != 0");
@@ -426,7 +451,8 @@ nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void*
     cfg.attrs = pdl;
     cfg.numAttrs = 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_small_kernel, ta, tb, reinterpret_cast<const uint8_t*>(sfa),
-                                       reinterpret_cast<const uint8_t*>(sfb), w, (int)M, (int)N, (int)K, ks, mp);
+                                       reinterpret_cast<const uint8_t*>(sfb), w, (int)M, (int)N, (int)K, ks, mp,
+                                       b_const ? 1 : 0);
     if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "gemm_small_kernel: %s", cudaGetErrorString(e));
     if ((st = check_launch("gemm_small_kernel"))) return st;
     const int64_t mn = M * N;

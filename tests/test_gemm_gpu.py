@@ -240,6 +240,25 @@ def test_gemm_small_m_split_points_matter(nv, oracle, M, N, K):
     assert np.array_equal(Df.cpu().numpy().view(np.uint32), acc.view(np.uint32))
 
 
+def test_gemm_decode_weights_const(nv, oracle):
+    """NVFP4_GEMM_WEIGHTS_CONST lets the decode kernel load B before its dependency wait; A is
+    still read after it.  Calls right after the kernels that produce A (the quantizer) and with
+    different weights each time give the bytes of the plain calls."""
+    M, N, K = 16, 1024, 4096
+    bs = [quantized_operands(nv, oracle, M, N, K, seed=60 + i)[2:4] for i in range(3)]
+    plain, flagged = [], []
+    for i in range(3):
+        a = workloads.activations(M, K, seed=70 + i)
+        pa, sa, gsa = nv.quantize(a, None)                 # A produced just before the GEMM
+        plain.append(nv.gemm(pa, sa, bs[i][0], bs[i][1], M, N, K, alpha=0.5))
+        pa2, sa2, _ = nv.quantize(a, None)
+        flagged.append(nv.gemm(pa2, sa2, bs[i][0], bs[i][1], M, N, K, alpha=0.5, weights_const=True))
+    torch.cuda.synchronize()
+    assert nv.device_status() == 0
+    for p, f in zip(plain, flagged):
+        assert torch.equal(p, f)
+
+
 def test_gemm_decode_cfg3_full_size(nv, oracle):
     """cfg3 decode shape M16 N7168 K8192, bit-exact everywhere against the split-K model, and the
     caller-workspace entry point gives the same bytes."""
