@@ -82,6 +82,8 @@ def test_argument_checks_reject_before_launch(nv):
     msg = _err(nv, L.nvfp4_gemm_f32(fake, fake, fake, fake, fake, 128, 256, 100, None))
     assert "K % 256" in msg
     f1 = ctypes.c_float(1.0)
+    msg = _err(nv, L.nvfp4_gemm_bf16_flags(fake, fake, fake, fake, f1, fake, 16, 256, 256, 6, None))
+    assert "flag" in msg
     msg = _err(nv, L.nvfp4_gemm_quantize(fake, fake, fake, fake, f1, f1, fake, fake, 128, 256, 256, None))
     assert "M % 256" in msg
     msg = _err(nv, L.nvfp4_gemm_quantize(fake, fake, fake, fake, f1, ctypes.c_float(0.0), fake, fake, 256, 256, 256,
