@@ -373,18 +373,24 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
     }
 }
 
-// K per split: the largest of 1024, 512, 256 that divides K (whole stages).  A function of K
-// only, so results do not depend on the device.  N 7168, K 8192 gives 448 units.  (Measured at
-// that shape: 512-K splits 21.5 us, 1024 19.5 us, 256 27.7 us -- fewer partials to write and
-// reduce.)
-inline int split_k(int64_t K) {
+// K per split: the largest of 2048, 1024, 512, 256 that divides K and still gives at least
+// SPLIT_UNITS_TARGET work units (N/128 tiles x K/split), else the smallest that divides K.  A
+// function of N and K only (the target is a constant, not the device's SM count), so results do
+// not depend on the device.  cfg3 decode (N 7168, K 8192): 2048 -> 224 units.  (Measured there,
+// back-to-back calls: 512-K splits 13.9 us, 1024 12.1 us, 2048 11.6 us -- fewer partials.)
+constexpr int64_t SPLIT_UNITS_TARGET = 148;
+inline int split_k(int64_t N, int64_t K) {
 #ifdef GSMALL_SPLIT
     if (K % GSMALL_SPLIT == 0) return GSMALL_SPLIT;
 #endif
-    if (K % 1024 == 0) return 1024;
-    if (K % 512 == 0) return 512;
-    if (K % 256 == 0) return 256;
-    return 0;
+    const int64_t tiles = N / 128;
+    int best = 0;
+    for (int ks : {2048, 1024, 512, 256}) {
+        if (K % ks) continue;
+        best = ks;
+        if (tiles * (K / ks) >= SPLIT_UNITS_TARGET) return ks;
+    }
+    return best;
 }
 
 // Persistent grid for `units` equal work units: the largest grid <= sms that divides them evenly,
@@ -402,14 +408,14 @@ inline int persistent_grid(int units, int sms) {
 
 // Workspace: the fp32 partials [splits][M][N].
 inline size_t workspace_bytes(int64_t M, int64_t N, int64_t K) {
-    const int ks = split_k(K);
+    const int ks = split_k(N, K);
     return ks ? (size_t)(K / ks) * (size_t)M * (size_t)N * sizeof(float) : 0;
 }
 
 template <bool kOutF32>
 nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void* sfb, float alpha, void* D,
                       int64_t M, int64_t N, int64_t K, void* ws, size_t ws_bytes, cudaStream_t s, bool b_const = false) {
-    const int ks = split_k(K);
+    const int ks = split_k(N, K);
     if (ks == 0) return fail(NVFP4_ERR_INVALID_ARG, "gemm (small M): K %% 256 != 0");
     if (N % 128 != 0) return fail(NVFP4_ERR_INVALID_ARG, "gemm (small M): N %% 128 != 0");
     if (ws_bytes < workspace_bytes(M, N, K))

@@ -138,12 +138,19 @@ def dequant_f32(oracle, packed, sf, rows, cols, gs):
     return e2m1[codes] * bs.repeat_interleave(16, dim=1)
 
 
-def split_size(K):
-    """K per split of the small-M kernel: the largest of 1024 / 512 / 256 dividing K."""
-    for ks in (1024, 512, 256):
-        if K % ks == 0:
+def split_size(N, K):
+    """K per split of the small-M kernel: the largest of 2048 / 1024 / 512 / 256 dividing K that
+    still gives at least 148 work units (N/128 tiles x K/split), else the smallest dividing K."""
+    best = None
+    for ks in (2048, 1024, 512, 256):
+        if K % ks:
+            continue
+        best = ks
+        if (N // 128) * (K // ks) >= 148:
             return ks
-    raise ValueError(K)
+    if best is None:
+        raise ValueError(K)
+    return best
 
 
 @pytest.mark.parametrize("M,N,K", [(16, 256, 256), (16, 384, 2048), (1, 128, 512), (48, 256, 768),
@@ -157,7 +164,7 @@ def test_gemm_small_m_bitexact(nv, oracle, M, N, K):
     torch.cuda.synchronize()
     assert nv.device_status() == 0
     acc = oracle.gemm_splitk_f32(pa.cpu().numpy(), sa.cpu().numpy(), pb.cpu().numpy(), sb.cpu().numpy(),
-                                 M, N, K, split_size(K))
+                                 M, N, K, split_size(N, K))
     assert np.array_equal(Df.cpu().numpy().view(np.uint32), acc.view(np.uint32))
     want = oracle.gemm_epilogue_bf16(acc, alpha)
     got = D.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
@@ -233,7 +240,7 @@ def test_gemm_small_m_split_points_matter(nv, oracle, M, N, K):
     torch.cuda.synchronize()
     assert nv.device_status() == 0
     host = [t.cpu().numpy() for t in (pa, sa, pb, sb)]
-    ks = split_size(K)
+    ks = split_size(N, K)
     acc = oracle.gemm_splitk_f32(*host, M, N, K, ks)
     other = oracle.gemm_splitk_f32(*host, M, N, K, ks // 2)
     assert np.count_nonzero(acc.view(np.uint32) != other.view(np.uint32)) > acc.size // 10
@@ -273,7 +280,7 @@ def test_gemm_decode_cfg3_full_size(nv, oracle):
     torch.cuda.synchronize()
     assert nv.device_status() == 0
     acc = oracle.gemm_splitk_f32(pa.cpu().numpy(), sa.cpu().numpy(), pb.cpu().numpy(), sb.cpu().numpy(),
-                                 M, N, K, split_size(K))
+                                 M, N, K, split_size(N, K))
     want = oracle.gemm_epilogue_bf16(acc, alpha)
     got = D.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
     assert np.count_nonzero(got != want) == 0
