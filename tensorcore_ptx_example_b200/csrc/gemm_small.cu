@@ -17,7 +17,7 @@
 // Persistent CTAs walk the work units (n-tile, split), split fastest so that the SMs stream
 // neighbouring stretches of B.  For Mp <= 64 two CTAs share an SM (about 100 KB of shared memory
 // and 256 TMEM columns each: two independent pipelines per SM); the grid is the largest one that
-// divides the units evenly (cfg3 decode: 448 units on 224 CTAs).
+// divides the units evenly (cfg3 decode: 224 units on 224 CTAs).
 //   warp 0      TMA producer: per 256-K stage the scale atoms of B and A (2 KB each, bulk copies)
 //               on the stage's "sf_landed" barrier, then one box of B (128 rows x 128 B) and one
 //               box of A (Mp rows x 128 B), both SWIZZLE_128B, on its "full" barrier;
@@ -393,14 +393,12 @@ inline int split_k(int64_t N, int64_t K) {
     return best;
 }
 
-// Persistent grid for `units` equal work units: the largest grid <= sms that divides them evenly,
-// when that keeps at least 3/4 of the SMs busy (896 units on 148 SMs: 128 CTAs x 7 units, no
-// tail of a few CTAs with one unit more); otherwise one CTA per SM.
+// Persistent grid for `units` equal work units over `slots` resident CTAs: all units at once
+// when they fit; else the largest grid <= slots that divides them evenly, when that keeps at least
+// 3/4 of the slots busy (e.g. 896 units on 148 slots: 128 CTAs x 7 units, no tail of a few CTAs
+// with one unit more); otherwise one CTA per slot.
 inline int persistent_grid(int units, int sms) {
     if (units <= sms) return units;
-#ifdef GSMALL_GRID_SMS
-    return sms;
-#endif
     for (int g = sms; g * 4 >= sms * 3; g--)
         if (units % g == 0) return g;
     return sms;
