@@ -50,9 +50,3 @@ def nv():
     nv.lib()
     return nv
 
-
-@pytest.fixture(scope="session")
-def out_dir():
-    d = os.path.join(ROOT, "gpurun_out")
-    os.makedirs(d, exist_ok=True)
-    return d
