@@ -538,6 +538,30 @@ def _ar_time(fn, steps, warmup, flush, world):
     return max_over_ranks(sum(ts) / len(ts), world)
 
 
+def _ar_time_b2b(fn, calls, warmup, world):
+    """Per-call device time (ms) of `calls` back-to-back all-reduces (the reference harness's
+    method, bench_ar.cu:965-972: events around a loop of calls), max over ranks.  The GPU spins
+    first while the host queues every call, so no host launch gap falls inside the region.  One
+    untimed call after the spin lines the ranks up (spins of equal cycle counts end at different
+    times on GPUs at different clocks); the calls' own barriers keep them in step after that."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(HIDE_HOST_CYCLES * max(1, calls // 4))
+    fn()
+    e0.record(s)
+    for _ in range(calls):
+        fn()
+    e1.record(s)
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(e0.elapsed_time(e1) / calls, world)
+
+
 def _ar_entry(name, numel, world, ms, payload_bytes_per_elt):
     """bf16-equivalent algbw / busbw (nccl-tests convention) and wire rate of one algorithm."""
     t = ms * 1e-3
@@ -654,8 +678,9 @@ def gemm_allreduce_bench(nv, world, rank, args, flush=None):
 
 
 def allreduce_sweep(args):
-    """cfg5: 16 KB .. 256 MB of bf16 per rank (doubling), NVFP4 one-shot / two-shot and bf16
-    one-shot / two-shot, max over ranks of the mean device time per call."""
+    """cfg5: 16 KB .. 256 MB of bf16 per rank (doubling), NVFP4 low-latency one-shot (up to
+    1 MB) / one-shot / two-shot and bf16 one-shot / two-shot, max over ranks of the mean device
+    time per call over back-to-back calls."""
     import torch
 
     import tensorcore_ptx_example_b200 as nv
@@ -673,14 +698,18 @@ def allreduce_sweep(args):
         for b in sizes:
             n = b // 2
             x, o = xfull[:n], ofull[:n]
-            steps = 20 if b <= (16 << 20) else 8
+            calls = 50 if b <= (16 << 20) else 10
             row = {"bytes": b, "numel": n}
-            for name, fn, bpe in [
-                    ("nvfp4_oneshot", lambda: ctx.allreduce(x, o, global_scale=gs, algo="oneshot"), 0.5625),
-                    ("nvfp4_twoshot", lambda: ctx.allreduce(x, o, global_scale=gs, algo="twoshot"), 0.5625),
-                    ("bf16_oneshot", lambda: ctx.bf16_allreduce(x, o, algo="oneshot"), 2.0),
-                    ("bf16_twoshot", lambda: ctx.bf16_allreduce(x, o, algo="twoshot"), 2.0)]:
-                ms = _ar_time(fn, steps, 3, None, world)
+            algos = [
+                ("nvfp4_lowlat", lambda: ctx.allreduce(x, o, global_scale=gs, algo="lowlat"), 1.25),
+                ("nvfp4_oneshot", lambda: ctx.allreduce(x, o, global_scale=gs, algo="oneshot"), 0.5625),
+                ("nvfp4_twoshot", lambda: ctx.allreduce(x, o, global_scale=gs, algo="twoshot"), 0.5625),
+                ("bf16_oneshot", lambda: ctx.bf16_allreduce(x, o, algo="oneshot"), 2.0),
+                ("bf16_twoshot", lambda: ctx.bf16_allreduce(x, o, algo="twoshot"), 2.0)]
+            if b > ar.LOWLAT_CAP_BYTES:
+                algos = algos[1:]
+            for name, fn, bpe in algos:
+                ms = _ar_time_b2b(fn, calls, 3, world)
                 e = _ar_entry(name, n, world, ms, bpe)
                 row[name] = {"us": e["us"], "algbw_gbs": e["algbw_gbs"], "busbw_gbs": e["busbw_gbs"]}
             rows.append(row)

@@ -182,10 +182,19 @@ typedef struct nvfp4_ar* nvfp4_ar_t;
 #define NVFP4_AR_AUTO 0
 #define NVFP4_AR_ONESHOT 1
 #define NVFP4_AR_TWOSHOT 2
-/* NVFP4_AR_AUTO picks one-shot up to this many bf16 bytes, two-shot above. */
+/* One-shot whose barrier is replaced by flags carried in the data (8-byte words: 4 bytes of
+ * payload + the call's epoch, NCCL's LL protocol): one fewer NVLink round trip, 2.2x the bytes
+ * on the wire.  Same results as NVFP4_AR_ONESHOT.  NVFP4 only; at most
+ * NVFP4_AR_LOWLAT_CAP_BYTES of bf16 per call. */
+#define NVFP4_AR_LOWLAT 3
+#define NVFP4_AR_LOWLAT_CAP_BYTES (1 << 20)
+/* NVFP4_AR_AUTO picks the low-latency one-shot up to NVFP4_AR_LOWLAT_MAX_BYTES of bf16,
+ * one-shot up to NVFP4_AR_ONESHOT_MAX_BYTES, two-shot above. */
+#define NVFP4_AR_LOWLAT_MAX_BYTES (1 << 20)
 #define NVFP4_AR_ONESHOT_MAX_BYTES (4 << 20)
 
-/* Device bytes a context allocates (flags + two parities of comm buffers). */
+/* Device bytes a context allocates (flags + two parities of comm buffers + two parities of the
+ * low-latency area). */
 NVFP4_API int64_t nvfp4_ar_buffer_bytes(int world, int64_t max_numel);
 /* world 1..8, rank in [0, world); max_numel: largest numel any call will use. */
 NVFP4_API nvfp4_status_t nvfp4_ar_create(int world, int rank, int64_t max_numel, nvfp4_ar_t* out);
@@ -203,8 +212,8 @@ NVFP4_API nvfp4_status_t nvfp4_ar_set_peers(nvfp4_ar_t h, void* const* bases);
 /* Time limit of each cross-GPU wait (default 5 s); a wait that runs out records a device status
  * (nvfp4_device_status) and the kernel returns. */
 NVFP4_API nvfp4_status_t nvfp4_ar_set_timeout(nvfp4_ar_t h, uint64_t timeout_ns);
-/* Recovery after a timed-out call: clears this rank's barrier words and restarts its epoch
- * count.  Synchronises the device.  Every rank must call it, with no all-reduce of any rank in
+/* Recovery after a timed-out call: clears this rank's barrier and low-latency words and
+ * restarts its epoch count.  Synchronises the device.  Every rank must call it, with no all-reduce of any rank in
  * flight (synchronise all ranks first, e.g. with a host barrier), before the next call. */
 NVFP4_API nvfp4_status_t nvfp4_ar_reset(nvfp4_ar_t h);
 /* The algorithm NVFP4_AR_AUTO resolves to. */

@@ -22,8 +22,10 @@ import ctypes
 
 from . import _ptr, _stream, check, lib
 
-AUTO, ONESHOT, TWOSHOT = 0, 1, 2
-_ALGOS = {"auto": AUTO, "oneshot": ONESHOT, "twoshot": TWOSHOT, AUTO: AUTO, ONESHOT: ONESHOT, TWOSHOT: TWOSHOT}
+AUTO, ONESHOT, TWOSHOT, LOWLAT = 0, 1, 2, 3
+LOWLAT_CAP_BYTES = 1 << 20          # NVFP4_AR_LOWLAT_CAP_BYTES: largest low-latency call (bf16 bytes)
+_ALGOS = {"auto": AUTO, "oneshot": ONESHOT, "twoshot": TWOSHOT, "lowlat": LOWLAT,
+          AUTO: AUTO, ONESHOT: ONESHOT, TWOSHOT: TWOSHOT, LOWLAT: LOWLAT}
 
 
 def buffer_bytes(world: int, max_numel: int) -> int:
@@ -37,7 +39,7 @@ def choose_algo(world: int, numel: int) -> int:
 
 def _algo(a) -> int:
     if a not in _ALGOS:
-        raise ValueError(f"algo must be one of auto/oneshot/twoshot, got {a!r}")
+        raise ValueError(f"algo must be one of auto/oneshot/twoshot/lowlat, got {a!r}")
     return _ALGOS[a]
 
 
@@ -106,7 +108,9 @@ class AllReduce:
     # ------------------------------------------------------------- calls ----
     def allreduce(self, x, out=None, global_scale: float = None, algo="auto", stream=None):
         """NVFP4 all-reduce of a contiguous bf16 CUDA tensor (numel % (32 * world) == 0).
-        global_scale: gs = amax / (6 * 448), the same on every rank (see agree_global_scale)."""
+        global_scale: gs = amax / (6 * 448), the same on every rank (see agree_global_scale).
+        algo: "oneshot", "twoshot", "lowlat" (one-shot with flags carried in the data, no
+        barrier; same results as "oneshot"; at most LOWLAT_CAP_BYTES of bf16) or "auto"."""
         import torch
         if global_scale is None:
             raise ValueError("global_scale is required (the same on every rank)")

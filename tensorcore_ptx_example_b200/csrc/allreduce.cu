@@ -4,6 +4,7 @@
 // One context per rank (one GPU each).  A context owns one device allocation, exported to the
 // other ranks (CUDA IPC between processes, or plain peer pointers inside one process):
 //   [flags: u32 [AR_MAX_BLOCKS][AR_MAX_WORLD]] [parity 0 region] [parity 1 region]
+//   [low-latency area: parity 0, parity 1, each [world][ll_slot]]
 //   region = IN [world][in_slot] + GATHER [world][gather_slot]
 // Calls alternate parities, so back-to-back calls never write the region a slower rank may
 // still be reading.  Every call carries an epoch; barrier flags only grow (2 per call), so they
@@ -25,6 +26,17 @@
 //   Sums are fp32 fma(code, scale * gs, acc) in rank order 0..n-1 (the reference sums in a
 //   rank-rotated order, :515-518); only the order of the pushes is rotated (rank me+1 first) so
 //   that the ranks do not all target the same peer at once.
+//
+// Low-latency one-shot (small messages): the barrier is replaced by flags carried in the data,
+// the LL protocol of NCCL.  Every 8-byte word a rank pushes holds 4 bytes of payload and a
+// non-zero tag (the call's epoch); 64-bit stores and loads are single-copy atomic, so a reader
+// that sees the tag in a word also sees that word's payload, and no fence or barrier is needed.
+// A chunk of 32 elements is 5 words (16 code bytes, 2 scale bytes + 2 bytes of padding), stored
+// word-major ([5][chunks] u64) so a warp's stores cover 256 contiguous bytes.  The reader zeroes
+// each word after reading it, so between calls the area is all zero: the next write to a word
+// comes from a call of the same parity, which no peer starts before this rank has finished the
+// current call (it needs this rank's data of the call in between).  A non-zero tag therefore
+// always belongs to the current call, and the 32-bit epoch may wrap.
 //
 // Synchronisation: block b of every rank handles the same chunks in every phase, so a phase
 // only needs block b of every rank to have finished the previous phase: after its pushes block
@@ -70,6 +82,8 @@ struct Params {
                                      // data (all phases / that phase alone)
     const uint8_t* q_codes;          // phase 0 from quantized data: codes [numel / 2] and scales
     const uint8_t* q_scales;         // [numel / 16] of the whole input, flat
+    int64_t ll_off;                  // byte offset of the low-latency area in every rank's buffer
+    int64_t ll_slot;                 // bytes of one low-latency slot
 };
 
 __device__ __forceinline__ uint32_t* flags_of(const Params& p, int r) {
@@ -85,6 +99,19 @@ __device__ __forceinline__ uint8_t* gather_slot(const Params& p, int r, int o) {
     return region_of(p, r) + (int64_t)p.world * p.in_slot + (int64_t)o * p.gather_slot;
 }
 
+// Low-latency slot of source rank s in rank r's buffer, for this call's parity.
+__device__ __forceinline__ uint64_t* ll_slot_of(const Params& p, int r, int s) {
+    return reinterpret_cast<uint64_t*>(p.comm[r] + p.ll_off +
+                                       ((int64_t)(p.epoch & 1u) * p.world + s) * p.ll_slot);
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* ptr, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* ptr) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
+    return v;
+}
 __device__ __forceinline__ void st_release_sys(uint32_t* ptr, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }
@@ -298,6 +325,86 @@ __global__ void __launch_bounds__(AR_THREADS) ar_nvfp4_kernel(const Params p) {
     }
 }
 
+// ---------------------------------------------------------------- low-latency one-shot ----
+constexpr int AR_LL_THREADS = 128;
+constexpr int AR_LL_WORDS = 5;                 // u64 words per 32-element chunk
+
+// Chunk c of a slot of `chunks` chunks, every word tagged with `epoch`.
+__device__ __forceinline__ void ll_put(uint64_t* slot, int64_t chunks, int64_t c, uint4 pk, uint32_t sc,
+                                       uint32_t epoch) {
+    const uint64_t tag = (uint64_t)epoch << 32;
+    const uint32_t w[AR_LL_WORDS] = {pk.x, pk.y, pk.z, pk.w, sc};
+#pragma unroll
+    for (int i = 0; i < AR_LL_WORDS; i++) st_relaxed_sys_u64(slot + i * chunks + c, tag | w[i]);
+}
+// Waits (bounded) until every word of chunk c carries `epoch`, then zeroes the words; false if
+// the wait ran out.
+__device__ __forceinline__ bool ll_get(uint64_t* slot, int64_t chunks, int64_t c, uint32_t epoch,
+                                       uint64_t timeout_ns, uint4& pk, uint32_t& sc) {
+    uint64_t v[AR_LL_WORDS];
+    int spins = 0;
+    uint64_t t0 = 0;
+    for (;;) {
+        bool ready = true;
+#pragma unroll
+        for (int i = 0; i < AR_LL_WORDS; i++) {
+            v[i] = ld_relaxed_sys_u64(slot + i * chunks + c);
+            ready &= (uint32_t)(v[i] >> 32) == epoch;
+        }
+        if (ready) break;
+        if (++spins == 64) t0 = globaltimer_ns();
+        if (spins > 64 && (spins & 63) == 0 && globaltimer_ns() - t0 > timeout_ns) return false;
+    }
+#pragma unroll
+    for (int i = 0; i < AR_LL_WORDS; i++) slot[i * chunks + c] = 0;
+    pk = make_uint4((uint32_t)v[0], (uint32_t)v[1], (uint32_t)v[2], (uint32_t)v[3]);
+    sc = (uint32_t)v[4] & 0xFFFFu;
+    return true;
+}
+
+// One-shot with the data-carried flags: A: quantize each chunk and push it to every peer;
+// B: sum the ranks' chunks in rank order 0..n-1 as each arrives (this rank's own chunk is
+// quantized again: the same bits as the pushed one).  Results equal ar_nvfp4_kernel<false>.
+// phase -1: A and B; 0: A alone; 1: B alone (single-GPU emulation).
+__global__ void __launch_bounds__(AR_LL_THREADS) ar_nvfp4_ll_kernel(const Params p) {
+    const int n = p.world, me = p.rank;
+    const float gs_inv = __fdiv_rn(1.0f, p.gs);
+    const int64_t chunks = p.numel / 32;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t tag = p.epoch | (uint32_t)(p.epoch == 0u);   // never 0 (the cleared value)
+    if (p.phase == -1 || p.phase == 0) {
+        for (int64_t c = first; c < chunks; c += stride) {
+            uint4 pk;
+            uint32_t sc;
+            quant32(p.in + c * 32, gs_inv, pk, sc);
+            for (int k = 1; k < n; k++) {                     // rank me+1 first
+                const int r = (me + k) % n;
+                ll_put(ll_slot_of(p, r, me), chunks, c, pk, sc, tag);
+            }
+        }
+    }
+    if (p.phase == -1 || p.phase == 1) {
+        for (int64_t c = first; c < chunks; c += stride) {
+            float acc[32];
+#pragma unroll
+            for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+            for (int s = 0; s < n; s++) {                      // fixed sum order 0 .. n-1
+                uint4 pk;
+                uint32_t sc;
+                if (s == me) {
+                    quant32(p.in + c * 32, gs_inv, pk, sc);
+                } else if (!ll_get(ll_slot_of(p, me, s), chunks, c, tag, p.timeout_ns, pk, sc)) {
+                    record_error(DEV_TIMEOUT_AR_BARRIER);
+                    return;
+                }
+                dq32_acc(pk, sc, p.gs, acc);
+            }
+            store_bf16x32(p.out + c * 32, acc);
+        }
+    }
+}
+
 // ---------------------------------------------------------------- bf16 kernels ----
 // Chunk = 8 bf16 (16 bytes).  Sum in fp32, rank order 0 .. n-1, round to bf16 once.
 __device__ __forceinline__ void acc_bf16x8(uint4 v, float* acc) {
@@ -384,6 +491,7 @@ struct nvfp4_ar {
     int world = 0, rank = 0, device = -1;
     int64_t max_numel = 0;
     int64_t in_slot = 0, gather_slot = 0, region = 0;
+    int64_t ll_numel = 0, ll_slot = 0, ll_off = 0;   // low-latency area: capacity, slot bytes, offset
     size_t bytes = 0;
     uint8_t* base = nullptr;
     uint8_t* peer[AR_MAX_WORLD] = {};
@@ -391,7 +499,7 @@ struct nvfp4_ar {
     bool ready = false;
     uint32_t epoch = 0;
     uint64_t timeout_ns = AR_DEFAULT_TIMEOUT_NS;
-    int max_grid = 0;
+    int max_grid = 0, ll_max_grid = 0;
 };
 
 namespace {
@@ -407,6 +515,13 @@ void slot_sizes(int world, int64_t max_numel, int64_t& in_slot, int64_t& gather_
     gather_slot = a > b ? a : b;
 }
 
+// Low-latency area: elements one call may use, and bytes of one slot (5 u64 words per 32 elements).
+void ll_sizes(int64_t max_numel, int64_t& ll_numel, int64_t& ll_slot) {
+    ll_numel = max_numel < NVFP4_AR_LOWLAT_CAP_BYTES / 2 ? max_numel : NVFP4_AR_LOWLAT_CAP_BYTES / 2;
+    ll_numel -= ll_numel % 32;
+    ll_slot = ll_numel / 32 * AR_LL_WORDS * 8;
+}
+
 nvfp4_status_t check_ctx(nvfp4_ar_t h, const char* who) {
     if (!h) return fail(NVFP4_ERR_INVALID_ARG, "%s: null context", who);
     int dev = -1;
@@ -416,9 +531,9 @@ nvfp4_status_t check_ctx(nvfp4_ar_t h, const char* who) {
     return NVFP4_OK;
 }
 
-int resident_grid(const void* fn) {
+int resident_grid(const void* fn, int threads = AR_THREADS) {
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, AR_THREADS, 0) != cudaSuccess || per_sm < 1) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0) != cudaSuccess || per_sm < 1) {
         cudaGetLastError();
         per_sm = 1;
     }
@@ -442,8 +557,13 @@ nvfp4_status_t check_call(nvfp4_ar_t h, const char* who, const void* in, const v
     if (numel < 0 || numel > h->max_numel)
         return fail(NVFP4_ERR_INVALID_ARG, "%s: numel %lld outside [0, max_numel=%lld]", who, (long long)numel,
                     (long long)h->max_numel);
-    if (algo != NVFP4_AR_AUTO && algo != NVFP4_AR_ONESHOT && algo != NVFP4_AR_TWOSHOT)
-        return fail(NVFP4_ERR_INVALID_ARG, "%s: algo must be NVFP4_AR_AUTO, _ONESHOT or _TWOSHOT", who);
+    if (algo != NVFP4_AR_AUTO && algo != NVFP4_AR_ONESHOT && algo != NVFP4_AR_TWOSHOT && algo != NVFP4_AR_LOWLAT)
+        return fail(NVFP4_ERR_INVALID_ARG, "%s: algo must be NVFP4_AR_AUTO, _ONESHOT, _TWOSHOT or _LOWLAT", who);
+    if (algo == NVFP4_AR_LOWLAT && elems_per_chunk != 32)
+        return fail(NVFP4_ERR_INVALID_ARG, "%s: NVFP4_AR_LOWLAT is an NVFP4 algorithm", who);
+    if (algo == NVFP4_AR_LOWLAT && numel > h->ll_numel)
+        return fail(NVFP4_ERR_INVALID_ARG, "%s: NVFP4_AR_LOWLAT takes at most %lld elements in this context", who,
+                    (long long)h->ll_numel);
     if (numel == 0) return NVFP4_OK;
     if (!in || !out) return fail(NVFP4_ERR_INVALID_ARG, "%s: null buffer", who);
     if (!aligned16(in) || !aligned16(out)) return fail(NVFP4_ERR_INVALID_ARG, "%s: buffers must be 16-byte aligned", who);
@@ -462,7 +582,10 @@ int64_t nvfp4_ar_buffer_bytes(int world, int64_t max_numel) {
     if (world < 1 || world > AR_MAX_WORLD || max_numel < 0) return -1;
     int64_t in_slot, gather_slot;
     slot_sizes(world, max_numel, in_slot, gather_slot);
-    return (int64_t)AR_FLAG_BYTES + 2 * ((int64_t)world * in_slot + (int64_t)world * gather_slot);
+    int64_t ll_numel, ll_slot;
+    ll_sizes(max_numel, ll_numel, ll_slot);
+    return (int64_t)AR_FLAG_BYTES + 2 * ((int64_t)world * in_slot + (int64_t)world * gather_slot) +
+           2 * (int64_t)world * ll_slot;
 }
 
 nvfp4_status_t nvfp4_ar_create(int world, int rank, int64_t max_numel, nvfp4_ar_t* out) {
@@ -479,7 +602,9 @@ nvfp4_status_t nvfp4_ar_create(int world, int rank, int64_t max_numel, nvfp4_ar_
     cudaGetDevice(&h->device);
     slot_sizes(world, max_numel, h->in_slot, h->gather_slot);
     h->region = (int64_t)world * h->in_slot + (int64_t)world * h->gather_slot;
-    h->bytes = AR_FLAG_BYTES + 2 * (size_t)h->region;
+    ll_sizes(max_numel, h->ll_numel, h->ll_slot);
+    h->ll_off = (int64_t)AR_FLAG_BYTES + 2 * h->region;
+    h->bytes = (size_t)h->ll_off + 2 * (size_t)world * (size_t)h->ll_slot;
     cudaError_t e = cudaMalloc(&h->base, h->bytes);
     if (e == cudaSuccess) e = cudaMemset(h->base, 0, h->bytes);
     if (e != cudaSuccess) {
@@ -495,6 +620,7 @@ nvfp4_status_t nvfp4_ar_create(int world, int rank, int64_t max_numel, nvfp4_ar_
     if (g3 < g) g = g3;
     if (g4 < g) g = g4;
     h->max_grid = g;
+    h->ll_max_grid = resident_grid((const void*)ar_nvfp4_ll_kernel, AR_LL_THREADS);
     h->peer[rank] = h->base;
     if (world == 1) h->ready = true;
     *out = h;
@@ -611,6 +737,8 @@ nvfp4_status_t nvfp4_ar_reset(nvfp4_ar_t h) {
     if (st) return st;
     cudaError_t e = cudaDeviceSynchronize();
     if (e == cudaSuccess) e = cudaMemset(h->base, 0, AR_FLAG_BYTES);
+    // a timed-out call may have left low-latency words set: clear them too
+    if (e == cudaSuccess) e = cudaMemset(h->base + h->ll_off, 0, h->bytes - (size_t)h->ll_off);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "ar_reset: %s", cudaGetErrorString(e));
     h->epoch = 0;
@@ -619,8 +747,11 @@ nvfp4_status_t nvfp4_ar_reset(nvfp4_ar_t h) {
 
 int nvfp4_ar_choose_algo(int world, int64_t numel) {
     if (world <= 1) return NVFP4_AR_ONESHOT;
-    // one-shot pushes the whole payload to every peer but needs one barrier: better while the
-    // call is latency-bound (measured crossover on 8 x B200 around 1-4 MB of bf16)
+    // the low-latency one-shot needs no barrier but sends 2.2x the payload (faster than one-shot
+    // up to its 1 MB cap on 2 and 8 x B200); one-shot pushes the whole payload to every peer but
+    // needs one barrier: better than two-shot while the call is latency-bound (measured
+    // crossover on 8 x B200 between 4 and 8 MB of bf16)
+    if (numel * 2 <= NVFP4_AR_LOWLAT_MAX_BYTES) return NVFP4_AR_LOWLAT;
     return numel * 2 <= NVFP4_AR_ONESHOT_MAX_BYTES ? NVFP4_AR_ONESHOT : NVFP4_AR_TWOSHOT;
 }
 
@@ -639,9 +770,17 @@ static Params make_params(nvfp4_ar_t h, const void* in, void* out, int64_t numel
     p.gs = gs;
     p.timeout_ns = h->timeout_ns;
     p.phase = phase;
+    p.ll_off = h->ll_off;
+    p.ll_slot = h->ll_slot;
     return p;
 }
 
+static nvfp4_status_t launch_nvfp4_ll(nvfp4_ar_t h, const Params& p, cudaStream_t s) {
+    int64_t g = (p.numel / 32 + AR_LL_THREADS - 1) / AR_LL_THREADS;
+    if (g > h->ll_max_grid) g = h->ll_max_grid;   // every block resident: blocks wait on peers
+    ar_nvfp4_ll_kernel<<<(int)(g < 1 ? 1 : g), AR_LL_THREADS, 0, s>>>(p);
+    return check_launch("ar_nvfp4_ll_kernel");
+}
 static nvfp4_status_t launch_nvfp4(nvfp4_ar_t h, const Params& p, bool twoshot, cudaStream_t s) {
     const int64_t work = twoshot ? p.numel / p.world / 32 : p.numel / 32;
     const int grid = grid_for(h, work);
@@ -665,9 +804,11 @@ nvfp4_status_t nvfp4_ar_allreduce(nvfp4_ar_t h, const void* in, void* out, int64
     if (!(global_scale > 0.0f) || !isfinite(global_scale))
         return fail(NVFP4_ERR_INVALID_ARG, "ar_allreduce: global_scale must be finite and > 0");
     if (algo == NVFP4_AR_AUTO) algo = nvfp4_ar_choose_algo(h->world, numel);
+    if (algo == NVFP4_AR_LOWLAT && numel > h->ll_numel) algo = NVFP4_AR_ONESHOT;
     h->epoch++;
-    return launch_nvfp4(h, make_params(h, in, out, numel, global_scale, -1), algo == NVFP4_AR_TWOSHOT,
-                        (cudaStream_t)stream);
+    const Params p = make_params(h, in, out, numel, global_scale, -1);
+    if (algo == NVFP4_AR_LOWLAT) return launch_nvfp4_ll(h, p, (cudaStream_t)stream);
+    return launch_nvfp4(h, p, algo == NVFP4_AR_TWOSHOT, (cudaStream_t)stream);
 }
 
 nvfp4_status_t nvfp4_ar_bf16_allreduce(nvfp4_ar_t h, const void* in, void* out, int64_t numel, int algo,
@@ -676,6 +817,7 @@ nvfp4_status_t nvfp4_ar_bf16_allreduce(nvfp4_ar_t h, const void* in, void* out, 
     nvfp4_status_t st = check_call(h, "ar_bf16_allreduce", in, out, numel, algo, 8);
     if (st || numel == 0) return st;
     if (algo == NVFP4_AR_AUTO) algo = nvfp4_ar_choose_algo(h->world, numel);
+    if (algo == NVFP4_AR_LOWLAT) algo = NVFP4_AR_ONESHOT;
     h->epoch++;
     return launch_bf16(h, make_params(h, in, out, numel, 0.0f, -1), algo == NVFP4_AR_TWOSHOT, (cudaStream_t)stream);
 }
@@ -782,8 +924,18 @@ nvfp4_status_t nvfp4_ar_allreduce_emulated(nvfp4_ar_t const* handles, int world,
     if (!bf16_payload && (!(global_scale > 0.0f) || !isfinite(global_scale)))
         return fail(NVFP4_ERR_INVALID_ARG, "ar_allreduce_emulated: global_scale must be finite and > 0");
     if (algo == NVFP4_AR_AUTO) algo = nvfp4_ar_choose_algo(world, numel);
+    if (algo == NVFP4_AR_LOWLAT && (bf16_payload || numel > handles[0]->ll_numel)) algo = NVFP4_AR_ONESHOT;
     const bool two = algo == NVFP4_AR_TWOSHOT;
     for (int r = 0; r < world; r++) handles[r]->epoch++;
+    if (algo == NVFP4_AR_LOWLAT) {
+        for (int ph = 0; ph < 2; ph++)
+            for (int r = 0; r < world; r++) {
+                nvfp4_status_t st = launch_nvfp4_ll(handles[r], make_params(handles[r], ins[r], outs[r], numel,
+                                                                            global_scale, ph), (cudaStream_t)stream);
+                if (st) return st;
+            }
+        return NVFP4_OK;
+    }
     // Phase by phase, rank by rank: the launches are ordered on one stream, so no kernel ever
     // waits for another one.
     const int phases = two ? 3 : 2;

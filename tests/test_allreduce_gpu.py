@@ -30,7 +30,7 @@ def global_scale(nv, inputs):
 
 
 @pytest.mark.parametrize("world", [2, 3, 4, 6, 8])
-@pytest.mark.parametrize("algo", ["oneshot", "twoshot"])
+@pytest.mark.parametrize("algo", ["oneshot", "twoshot", "lowlat"])
 def test_nvfp4_allreduce_bitexact(nv, oracle, world, algo):
     numel = 32 * world * 37                       # several blocks, not a power of two
     ins = rank_inputs(world, numel, seed0=100 * world)
@@ -38,7 +38,7 @@ def test_nvfp4_allreduce_bitexact(nv, oracle, world, algo):
     outs = ar.emulated_allreduce(ins, gs, algo)
     torch.cuda.synchronize()
     assert nv.device_status() == 0
-    want = (oracle.ar_oneshot if algo == "oneshot" else oracle.ar_twoshot)([u16(x) for x in ins], gs)
+    want = (oracle.ar_twoshot if algo == "twoshot" else oracle.ar_oneshot)([u16(x) for x in ins], gs)
     for r in range(world):                        # every rank holds the same result
         got = u16(outs[r])
         assert np.array_equal(got, want), f"rank {r}: {np.count_nonzero(got != want)} mismatches"
@@ -64,7 +64,9 @@ def test_repeated_calls_alternate_buffers(nv, oracle):
     ar.join_in_process(ctxs)
     try:
         for i, (algo, bf16) in enumerate([("oneshot", False), ("twoshot", False), ("twoshot", True),
-                                          ("oneshot", True), ("twoshot", False), ("oneshot", False)]):
+                                          ("lowlat", False), ("lowlat", False), ("lowlat", False),
+                                          ("oneshot", True), ("twoshot", False), ("oneshot", False),
+                                          ("lowlat", False)]):
             ins = rank_inputs(world, numel, seed0=1000 + 10 * i, std=1.0 + i)
             gs = global_scale(nv, ins)
             outs = ar.emulated_allreduce(ins, gs, algo, bf16=bf16, contexts=ctxs)
@@ -73,9 +75,55 @@ def test_repeated_calls_alternate_buffers(nv, oracle):
             if bf16:
                 want = oracle.ar_bf16(x16)
             else:
-                want = (oracle.ar_oneshot if algo == "oneshot" else oracle.ar_twoshot)(x16, gs)
+                want = (oracle.ar_twoshot if algo == "twoshot" else oracle.ar_oneshot)(x16, gs)
             for r in range(world):
                 assert np.array_equal(u16(outs[r]), want), (i, algo, bf16, r)
+    finally:
+        for c in ctxs:
+            c.close()
+
+
+def test_lowlat_sizes_change_between_calls(nv, oracle):
+    """The low-latency area is laid out per call (word-major over this call's chunks) and zeroed
+    by its readers: calls of changing sizes on the same contexts stay exact."""
+    world = 4
+    ctxs = [ar.AllReduce(world, r, 32 * world * 96) for r in range(world)]
+    ar.join_in_process(ctxs)
+    try:
+        for i, m in enumerate([96, 5, 96, 1, 40, 40, 96]):
+            ins = rank_inputs(world, 32 * world * m, seed0=3000 + i, std=0.5 + i)
+            gs = global_scale(nv, ins)
+            outs = ar.emulated_allreduce(ins, gs, "lowlat", contexts=ctxs)
+            torch.cuda.synchronize()
+            assert nv.device_status() == 0
+            want = oracle.ar_oneshot([u16(x) for x in ins], gs)
+            for r in range(world):
+                assert np.array_equal(u16(outs[r]), want), (i, m, r)
+    finally:
+        for c in ctxs:
+            c.close()
+
+
+def test_lowlat_limits(nv):
+    """NVFP4 only and at most LOWLAT_CAP_BYTES of bf16; "auto" picks it for small messages."""
+    world = 2
+    cap = ar.LOWLAT_CAP_BYTES // 2
+    numel = 2 * cap
+    ctxs = [ar.AllReduce(world, r, numel) for r in range(world)]
+    ar.join_in_process(ctxs)
+    try:
+        big = [torch.zeros(numel, dtype=torch.bfloat16, device="cuda") for _ in range(world)]
+        with pytest.raises(nv.NVFP4Error) as e:
+            ar.emulated_allreduce(big, 1.0, "lowlat", contexts=ctxs)
+        assert e.value.code == nv.NVFP4_ERR_INVALID_ARG
+        with pytest.raises(nv.NVFP4Error) as e:
+            ctxs[0].bf16_allreduce(big[0][:64], algo="lowlat")
+        assert e.value.code == nv.NVFP4_ERR_INVALID_ARG
+        ok = [x[:cap] for x in big]
+        outs = ar.emulated_allreduce(ok, 1.0, "lowlat", contexts=ctxs)
+        torch.cuda.synchronize()
+        assert nv.device_status() == 0 and all(int(torch.count_nonzero(o)) == 0 for o in outs)
+        assert ar.choose_algo(world, 1024) == ar.LOWLAT
     finally:
         for c in ctxs:
             c.close()

@@ -54,7 +54,7 @@ def run_in_process(ctxs, xs, outs, fn):
 
 
 @needs2
-@pytest.mark.parametrize("algo", ["oneshot", "twoshot"])
+@pytest.mark.parametrize("algo", ["oneshot", "twoshot", "lowlat"])
 def test_in_process_allreduce_bitexact(nv, oracle, algo):
     world = min(ngpus(), 8)
     numel = 32 * world * 1000
@@ -70,12 +70,13 @@ def test_in_process_allreduce_bitexact(nv, oracle, algo):
     try:
         for rep in range(3):                      # repeated calls: parities and epochs
             run_in_process(ctxs, xs, outs, lambda c, x, o: c.allreduce(x, o, global_scale=gs, algo=algo))
-            want = (oracle.ar_oneshot if algo == "oneshot" else oracle.ar_twoshot)([u16(x) for x in host], gs)
+            want = (oracle.ar_twoshot if algo == "twoshot" else oracle.ar_oneshot)([u16(x) for x in host], gs)
             for r in range(world):
                 with torch.cuda.device(r):
                     assert nv.device_status() == 0
                 assert np.array_equal(u16(outs[r]), want), (rep, r)
-        run_in_process(ctxs, xs, outs, lambda c, x, o: c.bf16_allreduce(x, o, algo=algo))
+        run_in_process(ctxs, xs, outs, lambda c, x, o: c.bf16_allreduce(x, o, algo=algo if algo != "lowlat"
+                                                                        else "oneshot"))
         want = oracle.ar_bf16([u16(x) for x in host])
         for r in range(world):
             assert np.array_equal(u16(outs[r]), want)
@@ -128,7 +129,8 @@ def test_in_process_gemm_allreduce_bitexact(nv, oracle):
 
 
 @needs2
-def test_barrier_timeout_when_a_rank_never_arrives(nv):
+@pytest.mark.parametrize("algo", ["twoshot", "lowlat"])
+def test_barrier_timeout_when_a_rank_never_arrives(nv, algo):
     world, numel = 2, 32 * 2 * 512
     ctxs, xs, outs = [], [], []
     for r in range(world):
@@ -141,7 +143,7 @@ def test_barrier_timeout_when_a_rank_never_arrives(nv):
     try:
         with torch.cuda.device(0):
             nv.device_status()                    # clear
-            ctxs[0].allreduce(xs[0], outs[0], global_scale=1.0 / 2688.0, algo="twoshot")   # rank 1 never calls
+            ctxs[0].allreduce(xs[0], outs[0], global_scale=1.0 / 2688.0, algo=algo)   # rank 1 never calls
             torch.cuda.synchronize(0)
             assert nv.device_status() == DEV_TIMEOUT_AR_BARRIER
         # the device is still usable; after a reset of every rank the contexts work again
@@ -149,7 +151,7 @@ def test_barrier_timeout_when_a_rank_never_arrives(nv):
             with torch.cuda.device(c.device):
                 c.reset()
         run_in_process(ctxs, xs, outs, lambda c, x, o: c.allreduce(x, o, global_scale=1.0 / 2688.0,
-                                                                     algo="twoshot"))
+                                                                     algo=algo))
         for r in range(world):
             with torch.cuda.device(r):
                 assert nv.device_status() == 0
@@ -183,7 +185,7 @@ def _ipc_worker(rank, world, port, numel, results):
         ctx = ar.AllReduce.from_process_group(numel)
         x = host[rank].cuda()
         outs = {}
-        for algo in ("oneshot", "twoshot"):
+        for algo in ("oneshot", "twoshot", "lowlat"):
             o = ctx.allreduce(x, global_scale=gs, algo=algo)
             torch.cuda.synchronize()
             outs[algo] = u16(o)
@@ -210,6 +212,7 @@ def test_multi_process_ipc_allreduce_bitexact(oracle):
     gs = oracle_gs(host)
     x16 = [u16(x) for x in host]
     want = {"oneshot": oracle.ar_oneshot(x16, gs), "twoshot": oracle.ar_twoshot(x16, gs)}
+    want["lowlat"] = want["oneshot"]
     for r in range(world):
         outs, status = res[r]
         assert status == 0
