@@ -701,7 +701,7 @@ def allreduce_sweep(args):
             calls = 50 if b <= (16 << 20) else 10
             row = {"bytes": b, "numel": n}
             algos = [
-                ("nvfp4_lowlat", lambda: ctx.allreduce(x, o, global_scale=gs, algo="lowlat"), 1.25),
+                ("nvfp4_lowlat", lambda: ctx.allreduce(x, o, global_scale=gs, algo="lowlat"), 0.75),
                 ("nvfp4_oneshot", lambda: ctx.allreduce(x, o, global_scale=gs, algo="oneshot"), 0.5625),
                 ("nvfp4_twoshot", lambda: ctx.allreduce(x, o, global_scale=gs, algo="twoshot"), 0.5625),
                 ("bf16_oneshot", lambda: ctx.bf16_allreduce(x, o, algo="oneshot"), 2.0),

@@ -182,8 +182,8 @@ typedef struct nvfp4_ar* nvfp4_ar_t;
 #define NVFP4_AR_AUTO 0
 #define NVFP4_AR_ONESHOT 1
 #define NVFP4_AR_TWOSHOT 2
-/* One-shot whose barrier is replaced by flags carried in the data (8-byte words: 4 bytes of
- * payload + the call's epoch, NCCL's LL protocol): one fewer NVLink round trip, 2.2x the bytes
+/* One-shot whose barrier is replaced by flags carried in the data (8-byte words: 7 bytes of
+ * payload + a tag byte, as in NCCL's LL protocol): one fewer NVLink round trip, 1.33x the bytes
  * on the wire.  Same results as NVFP4_AR_ONESHOT.  NVFP4 only; at most
  * NVFP4_AR_LOWLAT_CAP_BYTES of bf16 per call. */
 #define NVFP4_AR_LOWLAT 3

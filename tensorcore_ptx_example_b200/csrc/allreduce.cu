@@ -28,15 +28,15 @@
 //   that the ranks do not all target the same peer at once.
 //
 // Low-latency one-shot (small messages): the barrier is replaced by flags carried in the data,
-// the LL protocol of NCCL.  Every 8-byte word a rank pushes holds 4 bytes of payload and a
-// non-zero tag (the call's epoch); 64-bit stores and loads are single-copy atomic, so a reader
-// that sees the tag in a word also sees that word's payload, and no fence or barrier is needed.
-// A chunk of 32 elements is 5 words (16 code bytes, 2 scale bytes + 2 bytes of padding), stored
-// word-major ([5][chunks] u64) so a warp's stores cover 256 contiguous bytes.  The reader zeroes
-// each word after reading it, so between calls the area is all zero: the next write to a word
-// comes from a call of the same parity, which no peer starts before this rank has finished the
-// current call (it needs this rank's data of the call in between).  A non-zero tag therefore
-// always belongs to the current call, and the 32-bit epoch may wrap.
+// as in NCCL's LL protocol.  Every 8-byte word a rank pushes holds 7 bytes of payload and a
+// non-zero tag byte; 64-bit stores and loads are single-copy atomic, so a reader that sees the
+// tag in a word also sees that word's payload, and no fence or barrier is needed.  A chunk of 32
+// elements (16 code bytes + 2 scale bytes) is 3 words, stored word-major ([3][chunks] u64) so a
+// warp's stores cover 256 contiguous bytes.  The reader zeroes each word after reading it, so
+// between calls the area is all zero: the next write to a word comes from a call of the same
+// parity, which no peer starts before this rank has finished the current call (it needs this
+// rank's data of the call in between).  A word with a tag therefore always belongs to the
+// current call.
 //
 // Synchronisation: block b of every rank handles the same chunks in every phase, so a phase
 // only needs block b of every rank to have finished the previous phase: after its pushes block
@@ -327,20 +327,24 @@ __global__ void __launch_bounds__(AR_THREADS) ar_nvfp4_kernel(const Params p) {
 
 // ---------------------------------------------------------------- low-latency one-shot ----
 constexpr int AR_LL_THREADS = 128;
-constexpr int AR_LL_WORDS = 5;                 // u64 words per 32-element chunk
+constexpr int AR_LL_WORDS = 3;                 // u64 words per 32-element chunk
+constexpr uint64_t AR_LL_TAG = 1ull << 56;     // top byte of a written word: never zero
+constexpr uint64_t AR_LL_M56 = AR_LL_TAG - 1;  // its 7 payload bytes
 
-// Chunk c of a slot of `chunks` chunks, every word tagged with `epoch`.
-__device__ __forceinline__ void ll_put(uint64_t* slot, int64_t chunks, int64_t c, uint4 pk, uint32_t sc,
-                                       uint32_t epoch) {
-    const uint64_t tag = (uint64_t)epoch << 32;
-    const uint32_t w[AR_LL_WORDS] = {pk.x, pk.y, pk.z, pk.w, sc};
+// Chunk c of a slot of `chunks` chunks: the 144 payload bits (codes lo = bytes 0-7, hi = bytes
+// 8-15, then the two scale bytes) as 56 + 56 + 32 bits, each word tagged.
+__device__ __forceinline__ void ll_put(uint64_t* slot, int64_t chunks, int64_t c, uint4 pk, uint32_t sc) {
+    const uint64_t lo = (uint64_t)pk.x | ((uint64_t)pk.y << 32), hi = (uint64_t)pk.z | ((uint64_t)pk.w << 32);
+    const uint64_t w[AR_LL_WORDS] = {(lo & AR_LL_M56) | AR_LL_TAG,
+                                     (((lo >> 56) | (hi << 8)) & AR_LL_M56) | AR_LL_TAG,
+                                     (hi >> 48) | ((uint64_t)(sc & 0xFFFFu) << 16) | AR_LL_TAG};
 #pragma unroll
-    for (int i = 0; i < AR_LL_WORDS; i++) st_relaxed_sys_u64(slot + i * chunks + c, tag | w[i]);
+    for (int i = 0; i < AR_LL_WORDS; i++) st_relaxed_sys_u64(slot + i * chunks + c, w[i]);
 }
-// Waits (bounded) until every word of chunk c carries `epoch`, then zeroes the words; false if
-// the wait ran out.
-__device__ __forceinline__ bool ll_get(uint64_t* slot, int64_t chunks, int64_t c, uint32_t epoch,
-                                       uint64_t timeout_ns, uint4& pk, uint32_t& sc) {
+// Waits (bounded) until every word of chunk c is tagged, then zeroes the words; false if the
+// wait ran out.
+__device__ __forceinline__ bool ll_get(uint64_t* slot, int64_t chunks, int64_t c, uint64_t timeout_ns, uint4& pk,
+                                       uint32_t& sc) {
     uint64_t v[AR_LL_WORDS];
     int spins = 0;
     uint64_t t0 = 0;
@@ -349,7 +353,7 @@ __device__ __forceinline__ bool ll_get(uint64_t* slot, int64_t chunks, int64_t c
 #pragma unroll
         for (int i = 0; i < AR_LL_WORDS; i++) {
             v[i] = ld_relaxed_sys_u64(slot + i * chunks + c);
-            ready &= (uint32_t)(v[i] >> 32) == epoch;
+            ready &= v[i] >= AR_LL_TAG;
         }
         if (ready) break;
         if (++spins == 64) t0 = globaltimer_ns();
@@ -357,8 +361,10 @@ __device__ __forceinline__ bool ll_get(uint64_t* slot, int64_t chunks, int64_t c
     }
 #pragma unroll
     for (int i = 0; i < AR_LL_WORDS; i++) slot[i * chunks + c] = 0;
-    pk = make_uint4((uint32_t)v[0], (uint32_t)v[1], (uint32_t)v[2], (uint32_t)v[3]);
-    sc = (uint32_t)v[4] & 0xFFFFu;
+    const uint64_t lo = (v[0] & AR_LL_M56) | (v[1] << 56);
+    const uint64_t hi = ((v[1] & AR_LL_M56) >> 8) | (v[2] << 48);
+    pk = make_uint4((uint32_t)lo, (uint32_t)(lo >> 32), (uint32_t)hi, (uint32_t)(hi >> 32));
+    sc = (uint32_t)(v[2] >> 16) & 0xFFFFu;
     return true;
 }
 
@@ -372,7 +378,6 @@ __global__ void __launch_bounds__(AR_LL_THREADS) ar_nvfp4_ll_kernel(const Params
     const int64_t chunks = p.numel / 32;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const uint32_t tag = p.epoch | (uint32_t)(p.epoch == 0u);   // never 0 (the cleared value)
     if (p.phase == -1 || p.phase == 0) {
         for (int64_t c = first; c < chunks; c += stride) {
             uint4 pk;
@@ -380,7 +385,7 @@ __global__ void __launch_bounds__(AR_LL_THREADS) ar_nvfp4_ll_kernel(const Params
             quant32(p.in + c * 32, gs_inv, pk, sc);
             for (int k = 1; k < n; k++) {                     // rank me+1 first
                 const int r = (me + k) % n;
-                ll_put(ll_slot_of(p, r, me), chunks, c, pk, sc, tag);
+                ll_put(ll_slot_of(p, r, me), chunks, c, pk, sc);
             }
         }
     }
@@ -394,7 +399,7 @@ __global__ void __launch_bounds__(AR_LL_THREADS) ar_nvfp4_ll_kernel(const Params
                 uint32_t sc;
                 if (s == me) {
                     quant32(p.in + c * 32, gs_inv, pk, sc);
-                } else if (!ll_get(ll_slot_of(p, me, s), chunks, c, tag, p.timeout_ns, pk, sc)) {
+                } else if (!ll_get(ll_slot_of(p, me, s), chunks, c, p.timeout_ns, pk, sc)) {
                     record_error(DEV_TIMEOUT_AR_BARRIER);
                     return;
                 }
@@ -515,7 +520,7 @@ void slot_sizes(int world, int64_t max_numel, int64_t& in_slot, int64_t& gather_
     gather_slot = a > b ? a : b;
 }
 
-// Low-latency area: elements one call may use, and bytes of one slot (5 u64 words per 32 elements).
+// Low-latency area: elements one call may use, and bytes of one slot (3 u64 words per 32 elements).
 void ll_sizes(int64_t max_numel, int64_t& ll_numel, int64_t& ll_slot) {
     ll_numel = max_numel < NVFP4_AR_LOWLAT_CAP_BYTES / 2 ? max_numel : NVFP4_AR_LOWLAT_CAP_BYTES / 2;
     ll_numel -= ll_numel % 32;
@@ -747,7 +752,7 @@ nvfp4_status_t nvfp4_ar_reset(nvfp4_ar_t h) {
 
 int nvfp4_ar_choose_algo(int world, int64_t numel) {
     if (world <= 1) return NVFP4_AR_ONESHOT;
-    // the low-latency one-shot needs no barrier but sends 2.2x the payload (faster than one-shot
+    // the low-latency one-shot needs no barrier but sends 1.33x the payload (faster than one-shot
     // up to its 1 MB cap on 2 and 8 x B200); one-shot pushes the whole payload to every peer but
     // needs one barrier: better than two-shot while the call is latency-bound (measured
     // crossover on 8 x B200 between 4 and 8 MB of bf16)

@@ -64,11 +64,11 @@ def test_oracle_allreduce_order_and_determinism(oracle):
 def test_buffer_bytes_and_algo_choice(nv):
     L = nv.lib()
     # flags (1024 blocks x 8 ranks x 4 B) + 2 parities x (world IN slots + world GATHER slots)
-    # + 2 parities x world low-latency slots (5 u64 words per 32 elements, up to 512 K elements)
+    # + 2 parities x world low-latency slots (3 u64 words per 32 elements, up to 512 K elements)
     numel, world = 1 << 20, 8
     in_slot = max(numel // 2 + numel // 16, numel * 2)
     gather = max((numel // world) // 2 + (numel // world) // 16, (numel // world) * 2)
-    ll_slot = min(numel, 1 << 19) // 32 * 40
+    ll_slot = min(numel, 1 << 19) // 32 * 24
     assert L.nvfp4_ar_buffer_bytes(world, numel) == (1024 * 8 * 4 + 2 * (world * in_slot + world * gather)
                                                      + 2 * world * ll_slot)
     assert L.nvfp4_ar_buffer_bytes(0, numel) == -1 and L.nvfp4_ar_buffer_bytes(9, numel) == -1
