@@ -380,6 +380,77 @@ def cpu_baseline_gemm(target_s=8.0):
             "seconds": round(dt, 3)}
 
 
+def _bf16_sample(rng, shape):
+    """N(0, 1) bf16 bit patterns (float32 draws truncated to their top 16 bits); at most 4 M
+    distinct draws, repeated to fill the shape."""
+    import numpy as np
+    n = int(np.prod(shape))
+    base = (rng.standard_normal(min(n, 1 << 22), dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    return np.resize(base, shape)
+
+
+def _sized_sample(run, unit, limit, target_s):
+    """Units (a multiple of `unit`, at most `limit`) that `run` handles in about target_s seconds,
+    from a calibration run of one unit; returns (units, seconds of the sized run)."""
+    rate = unit / max(run(unit), 1e-6)
+    n = min(limit, max(unit, int(target_s * rate) // unit * unit))
+    return n, run(n)
+
+
+def cpu_baseline_quantize(target_s=2.0):
+    """The oracle's quantizer (its restatement of q16 / quantize_kernel,
+    blackwell/allreduce_sm100_sm120/nvfp4_allreduce.cuh:272-302,427-454; the reference has no CPU
+    quantizer) on all host threads over a bounded row slice of cfg2, given the global scale;
+    GB/s at 2.5625 B/elt."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import py_oracle
+    from tensorcore_ptx_example_b200 import workloads
+    threads = py_oracle.nthreads_default()
+    rows_total, cols = workloads.CFG2_SHAPE
+    full = _bf16_sample(np.random.default_rng(2), (rows_total, cols))
+    gs, _ = py_oracle.global_scale(py_oracle.amax_bf16(full))
+
+    def run(rows, nthreads=threads):
+        x = full[:rows]
+        t0 = time.perf_counter()
+        py_oracle.quantize_bf16(x, gs, nthreads=nthreads)
+        return time.perf_counter() - t0
+
+    rows, dt = _sized_sample(run, 128, rows_total, target_s)
+    rows1, dt1 = _sized_sample(lambda r: run(r, 1), 128, rows_total, target_s / 2)
+    return {"value": round(rows * cols * 2.5625 / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{rows}x{cols} rows of cfg2 (N(0,1)), oracle orc_quantize_bf16", "seconds": round(dt, 3),
+            "single_thread_gbs": round(rows1 * cols * 2.5625 / dt1 / 1e9, 3), "single_thread_rows": rows1}
+
+
+def cpu_baseline_allreduce(target_s=2.0, world=8):
+    """The oracle's fixed-order NVFP4 two-shot (quantize, dequant-sum in rank order 0..n-1,
+    requantize, dequantize: the data flow of twoshot_fused_kernel, nvfp4_allreduce.cuh:498-567)
+    for 8 ranks on all host threads, over a bounded slice of cfg4 per rank; bf16-equivalent
+    algbw 2 * numel / t in GB/s, the unit of the GPU all-reduce lines."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import py_oracle
+    from tensorcore_ptx_example_b200 import workloads
+    threads = py_oracle.nthreads_default()
+    rows, cols = workloads.CFG4_SHAPE
+    rng = np.random.default_rng(4)
+    full = [_bf16_sample(rng, rows * cols) for _ in range(world)]
+    gs, _ = py_oracle.global_scale(max(py_oracle.amax_bf16(x) for x in full))
+
+    def run(numel):
+        ins = [x[:numel] for x in full]
+        t0 = time.perf_counter()
+        py_oracle.ar_twoshot(ins, gs, nthreads=threads)
+        return time.perf_counter() - t0
+
+    numel, dt = _sized_sample(run, 32 * world * 256, rows * cols, target_s)
+    return {"value": round(2.0 * numel / dt / 1e9, 3), "unit": "GB/s (bf16-equivalent algbw)", "cores": threads,
+            "kind": "port", "sample": f"{numel} elements per rank x {world} ranks of cfg4 (N(0,1)), oracle "
+                                      f"orc_ar_twoshot", "seconds": round(dt, 3)}
+
+
 def run_ours(args):
     import torch
     import tensorcore_ptx_example_b200 as nv
@@ -481,6 +552,16 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_gemm()
+        for key, fn in (("quantize", cpu_baseline_quantize), ("allreduce_cpu_baseline", cpu_baseline_allreduce)):
+            try:
+                res = fn()
+            except Exception as e:  # reported, not fatal
+                res = {"error": str(e)}
+            if key == "quantize":
+                if isinstance(extra.get("quantize"), dict):
+                    extra["quantize"]["cpu_baseline"] = res
+            else:
+                extra[key] = res
 
     traffic = read_profile_traffic("gemm_cfg3")
     line = {

@@ -89,7 +89,8 @@ def test_in_process_allreduce_bitexact(nv, oracle, algo):
 @needs2
 def test_in_process_gemm_allreduce_bitexact(nv, oracle):
     """Row-parallel GEMM fused with the two-shot all-reduce across real GPUs: every rank's GEMM
-    epilogue pushes its quantized tiles into the owners' slots over NVLink."""
+    epilogue quantizes its tiles into its own all-reduce buffer, and the all-reduce kernel pushes
+    them to the owners of the shards over NVLink."""
     world = min(ngpus(), 8)
     M, N, K = 256, 512, 512
     ctxs, ops, alphas, ds = [], [], [], []
