@@ -3,19 +3,29 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Headline (metric "NVFP4 GEMM TFLOPS"): the cfg3 block-scaled GEMM M=N=K=8192 on each GPU,
-operands quantized on the device from seeded synthetic bf16 (A ~ N(0,1) with 0.1 % x50
-outliers, B ~ N(0, 0.02)).  One step = one GEMM launch; L2 is flushed (256 MB write) between
-timed steps; steps are timed with CUDA events on the launching stream and the max over ranks
-is taken.  With N > 1 every rank runs its own GEMM (replicas, weak scaling) and the line also
-carries the cfg4 NVFP4 all-reduce (bf16-equivalent bus bandwidth) when the all-reduce module
-is built.  Extra keys: the cfg2 quantizer (GB/s), the roofline of the GEMM kernel, the CPU
-baseline, the end-to-end number through the C ABI with host buffers, and SM clocks sampled
-during the timed region.
+The metric is BASELINE's: "NVFP4 GEMM TFLOPS (1 GPU); NVFP4 all-reduce bf16-equiv GB/s at 2/4/8 B200".
 
---impl reference times the reference's own CPU implementation of the GEMM
-(cpu_gemm_ref_bs from random_cpu_ref/verify_random.h, compiled into oracle/_ref) on a bounded
-sample with all host threads, on rank 0 only.
+N = 1: the cfg3 block-scaled GEMM M=N=K=8192 (operands quantized on the device from seeded
+synthetic bf16: A ~ N(0,1) with 0.1 % x50 outliers, B ~ N(0, 0.02)).  One step = one GEMM launch;
+L2 is flushed between timed steps; CUDA events on the launching stream.  Extra keys: the roofline
+against the FP4 MMA issue rate measured live on the same GPU, the cfg2 quantizer (with the
+reference's own quantize kernel timed beside it), the decode GEMM, the GEMM with the quantizing
+epilogue, the CPU baselines, an end-to-end number through the C ABI with host buffers, and SM
+clocks sampled during the timed region.
+
+N > 1 (one process per GPU under torchrun): the cfg4 NVFP4 all-reduce (4096 x 7168 bf16 per
+rank, N(0,1), seed = rank; algorithm NVFP4_AR_AUTO).  One step = one all-reduce call; L2 flushed
+between steps; the time is the max over ranks.  `value` is the bf16-equivalent algorithm
+bandwidth 2 * numel / t (nccl-tests convention; busbw = algbw * 2 (n-1) / n).  The line also
+carries bit-exact parity against the CPU oracle on sampled windows of every algorithm's output,
+each algorithm's time and wire rate, compact cfg5 rows (best NVFP4 against best bf16), the
+reference's own fused kernels timed on the same GPUs, the fused row-parallel GEMM + all-reduce,
+GEMM replicas, and the end-to-end all-reduce with host buffers.
+
+--impl reference times the reference's CPU path on rank 0 (other ranks exit): at N = 1 its
+cpu_gemm_ref_bs (random_cpu_ref/verify_random.h, compiled into oracle/_ref) on a bounded slice of
+the GEMM; at N > 1 the oracle's fixed-order NVFP4 two-shot for N ranks over a bounded slice of
+cfg4 (the reference has no CPU all-reduce of its own).
 """
 from __future__ import annotations
 
@@ -34,6 +44,7 @@ M_ = N_ = K_ = 8192
 FLUSH_BYTES = 256 << 20          # > 126 MB L2
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FP4_NOMINAL_TFLOPS = 9000.0       # B200 dense FP4 (NVIDIA spec, without sparsity)
+METRIC = "NVFP4 GEMM TFLOPS (1 GPU); NVFP4 all-reduce bf16-equiv GB/s at 2/4/8 B200"
 HBM_FALLBACK_GBS = 6650.0
 BF16_FALLBACK_TFLOPS = 1590.0
 
@@ -217,6 +228,10 @@ def quantize_bench(nv, steps, warmup, flush):
     gsd = torch.empty(1, dtype=torch.float32, device="cuda")
     ts_auto = timed_steps(lambda: nv.lib().nvfp4_quantize_bf16_auto(
         nv._ptr(x), rows, cols, nv._ptr(packed), nv._ptr(sf), nv._ptr(gsd), nv._ptr(ws), nv._stream()), steps, flush)
+    try:
+        ref = reference_quantize_kernel(x, gs, steps, flush)
+    except Exception as e:  # reported, not fatal
+        ref = {"error": str(e)}
     n = rows * cols
     ms = sum(ts) / len(ts)
     byts = n * 2.5625
@@ -232,7 +247,9 @@ def quantize_bench(nv, steps, warmup, flush):
                      "frac": round(gbs / hbm, 4), "peak_source": f"{peak_kind} HBM copy",
                      "traffic": read_profile_traffic("quantize_cfg2")},
         "amax_us": round(sum(ts_amax) / len(ts_amax) * 1e3, 2),
+        "amax_gbs": round(n * 2 / (sum(ts_amax) / len(ts_amax) * 1e-3) / 1e9, 1),
         "auto_scale_total_us": round(sum(ts_auto) / len(ts_auto) * 1e3, 2),
+        "reference_kernel": ref,
     }
 
 
@@ -424,37 +441,95 @@ def cpu_baseline_quantize(target_s=2.0):
             "single_thread_gbs": round(rows1 * cols * 2.5625 / dt1 / 1e9, 3), "single_thread_rows": rows1}
 
 
-def cpu_baseline_allreduce(target_s=2.0, world=8):
+class CpuAllReduceSample:
     """The oracle's fixed-order NVFP4 two-shot (quantize, dequant-sum in rank order 0..n-1,
     requantize, dequantize: the data flow of twoshot_fused_kernel, nvfp4_allreduce.cuh:498-567)
-    for 8 ranks on all host threads, over a bounded slice of cfg4 per rank; bf16-equivalent
-    algbw 2 * numel / t in GB/s, the unit of the GPU all-reduce lines."""
-    import numpy as np
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import py_oracle
-    from tensorcore_ptx_example_b200 import workloads
-    threads = py_oracle.nthreads_default()
-    rows, cols = workloads.CFG4_SHAPE
-    rng = np.random.default_rng(4)
-    full = [_bf16_sample(rng, rows * cols) for _ in range(world)]
-    gs, _ = py_oracle.global_scale(max(py_oracle.amax_bf16(x) for x in full))
+    for `world` ranks on all host threads, over a bounded slice of cfg4 per rank; bf16-equivalent
+    algbw 2 * numel / t in GB/s, the unit of the GPU all-reduce lines.  Inputs are drawn once."""
 
-    def run(numel):
-        ins = [x[:numel] for x in full]
+    def __init__(self, world=8):
+        import numpy as np
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import py_oracle
+        from tensorcore_ptx_example_b200 import workloads
+        self.po = py_oracle
+        self.world = world
+        self.threads = py_oracle.nthreads_default()
+        rows, cols = workloads.CFG4_SHAPE
+        self.limit = rows * cols
+        rng = np.random.default_rng(4)
+        self.full = [_bf16_sample(rng, rows * cols) for _ in range(world)]
+        self.gs, _ = py_oracle.global_scale(max(py_oracle.amax_bf16(x) for x in self.full))
+
+    def run(self, numel):
+        ins = [x[:numel] for x in self.full]
         t0 = time.perf_counter()
-        py_oracle.ar_twoshot(ins, gs, nthreads=threads)
+        self.po.ar_twoshot(ins, self.gs, nthreads=self.threads)
         return time.perf_counter() - t0
 
-    numel, dt = _sized_sample(run, 32 * world * 256, rows * cols, target_s)
-    return {"value": round(2.0 * numel / dt / 1e9, 3), "unit": "GB/s (bf16-equivalent algbw)", "cores": threads,
-            "kind": "port", "sample": f"{numel} elements per rank x {world} ranks of cfg4 (N(0,1)), oracle "
-                                      f"orc_ar_twoshot", "seconds": round(dt, 3)}
+    def measure(self, target_s=2.0):
+        numel, dt = _sized_sample(self.run, 32 * self.world * 256, self.limit, target_s)
+        return {"value": round(2.0 * numel / dt / 1e9, 3), "unit": "GB/s (bf16-equivalent algbw)",
+                "cores": self.threads, "kind": "port",
+                "sample": f"{numel} elements per rank x {self.world} ranks of cfg4 (N(0,1)), oracle orc_ar_twoshot",
+                "seconds": round(dt, 3)}
 
 
-def run_ours(args):
+def cpu_baseline_allreduce(target_s=2.0, world=8):
+    return CpuAllReduceSample(world).measure(target_s)
+
+
+def reference_quantize_kernel(x, gs, steps, flush):
+    """Same-box baseline: the reference's own quantize_kernel (nvfp4_allreduce.cuh:427-454; linear
+    scale layout, rcp.approx reciprocals, 4-byte loads), compiled from the reference header into
+    oracle/_ref/libref_ar.so, timed on the same GPU and input as ours, with SFScaleVal = 1 / gs."""
+    import ctypes
+
+    import numpy as np
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import py_oracle
+    if not py_oracle.ref_ar_available():
+        return {"unavailable": "oracle/_ref/libref_ar.so not built (needs the reference tree at build time)"}
+    L = py_oracle.ref_ar_lib()
+    numel = x.numel()
+    out = torch.empty(int(L.ref_layout_total_bytes(numel)), dtype=torch.uint8, device="cuda")
+    sf_val = float(np.float32(1.0) / np.float32(gs))
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    xp, op = ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(out.data_ptr())
+
+    def fn():
+        rc = L.ref_quantize(xp, op, numel, sf_val, st)
+        if rc:
+            raise RuntimeError(f"ref_quantize: cuda error {rc}")
+    for _ in range(3):
+        fn()
+    ts = timed_steps(fn, steps, flush)
+    ms = sum(ts) / len(ts)
+    return {"kernel": "nvfp4_ar::quantize_kernel (reference, oracle/_ref/libref_ar.so)", "us": round(ms * 1e3, 2),
+            "gbs": round(numel * 2.5625 / (ms * 1e-3) / 1e9, 1),
+            "note": "same input and L2 flush; linear scale layout instead of the tcgen05 one"}
+
+
+def fp4_peak_measure(local):
+    """The FP4 block-scaled MMA issue rate of this GPU, measured live (diagnostics library:
+    every SM pair issues M256 N256 K64 MMAs from resident shared memory on pseudo-random E2M1
+    operands), with its own clock samples: the tensor roofline of the GEMM."""
+    from tensorcore_ptx_example_b200 import diag
+    sampler = ClockSampler(local)
+    sampler.start()
+    tf = diag.mma_peak(cta_group=2, iters=32768, repeats=5, random_operands=True)
+    clocks = sampler.stop()
+    assert diag.device_status() == 0
+    return {"tflops": round(tf, 1), "clocks": clocks,
+            "probe": "nvfp4_diag_mma_peak cta_group 2, 32768 MMAs per SM pair, random operands, best of 5"}
+
+
+def run_gemm_line(args):
     import torch
     import tensorcore_ptx_example_b200 as nv
-    world, rank, local = dist_setup(args)
+    world, rank, local = 1, 0, int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
     peaks, peak_kind = load_peaks()
     flush = L2Flush()
 
@@ -464,19 +539,16 @@ def run_ours(args):
         fn()
     torch.cuda.synchronize()
     assert nv.device_status() == 0
-    barrier(world)
-    torch.cuda.synchronize()
     sampler = ClockSampler(local)
     sampler.start()
     ts = timed_steps(fn, args.steps, flush)
     clocks = sampler.stop()
-    barrier(world)
-    total_ms = max_over_ranks(sum(ts), world)
+    total_ms = sum(ts)
     flops = 2.0 * M_ * N_ * K_
-    value = flops * args.steps * world / (total_ms * 1e-3) / 1e12
+    value = flops * args.steps / (total_ms * 1e-3) / 1e12
     mean_ms = sum(ts) / len(ts)
     achieved = flops / (mean_ms * 1e-3) / 1e12
-    fp4_peak = 4.0 * float(peaks.get("bf16_tflops", BF16_FALLBACK_TFLOPS))
+    bf16x4 = 4.0 * float(peaks.get("bf16_tflops", BF16_FALLBACK_TFLOPS))
     assert nv.device_status() == 0
 
     # end to end through the public API with host buffers: every step copies its operands from
@@ -488,73 +560,35 @@ def run_ours(args):
     d2h = M_ * N_ * 2
     dev_sets = [(pa, sa, pb, sb, d), tuple(torch.empty_like(t) for t in (pa, sa, pb, sb, d))]
     host_out = [torch.empty((M_, N_), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    s_in, s_mm, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
 
-    def e2e_run(n_steps):
-        done_out = [None, None]                       # D2H of the step that last used a buffer set
-        for i in range(n_steps):
-            j = i & 1
-            da, dsa, db, dsb, dd = dev_sets[j]
-            ev_in = torch.cuda.Event()
-            with torch.cuda.stream(s_in):
-                if done_out[j] is not None:
-                    s_in.wait_event(done_out[j])
-                for h, dv in zip(host, (da, dsa, db, dsb)):
-                    dv.copy_(h, non_blocking=True)
-                ev_in.record(s_in)
-            ev_mm = torch.cuda.Event()
-            with torch.cuda.stream(s_mm):
-                s_mm.wait_event(ev_in)
-                nv.gemm(da, dsa, db, dsb, M_, N_, K_, alpha=alpha, out=dd, stream=s_mm)
-                ev_mm.record(s_mm)
-            ev_out = torch.cuda.Event()
-            with torch.cuda.stream(s_out):
-                s_out.wait_event(ev_mm)
-                host_out[j].copy_(dd, non_blocking=True)
-                ev_out.record(s_out)
-            done_out[j] = ev_out
+    def gemm_step(dev, stream):
+        da, dsa, db, dsb, dd = dev
+        nv.gemm(da, dsa, db, dsb, M_, N_, K_, alpha=alpha, out=dd, stream=stream)
 
-    e2e_run(3)
-    torch.cuda.synchronize()
     e2e_steps = max(4, min(args.steps, 12))
-    barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda._sleep(HIDE_HOST_CYCLES * 8)
-    e0.record()
-    for st in (s_in, s_mm, s_out):
-        st.wait_stream(torch.cuda.current_stream())
-    e2e_run(e2e_steps)
-    for st in (s_in, s_mm, s_out):
-        torch.cuda.current_stream().wait_stream(st)
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world)
+    e2e_ms = pipelined_e2e(host, dev_sets, host_out, gemm_step, e2e_steps)
     assert torch.equal(host_out[(e2e_steps - 1) & 1], d.cpu())
 
+    fp4 = None
+    try:
+        fp4 = fp4_peak_measure(local)
+    except Exception as e:  # reported, not fatal
+        fp4 = {"error": str(e)}
     extra = {}
-    if rank == 0:
+    for key, fn_ in (("quantize", lambda: quantize_bench(nv, max(5, args.steps), 3, flush)),
+                     ("gemm_decode", lambda: decode_bench(nv, max(5, args.steps), 3, flush)),
+                     ("gemm_quantize", lambda: gemm_quantize_bench(nv, min(max(5, args.steps), 20), flush))):
         try:
-            extra["quantize"] = quantize_bench(nv, max(5, args.steps), 3, flush)
+            extra[key] = fn_()
         except Exception as e:  # reported, not fatal
-            extra["quantize"] = {"error": str(e)}
-        try:
-            extra["gemm_decode"] = decode_bench(nv, max(5, args.steps), 3, flush)
-        except Exception as e:  # reported, not fatal
-            extra["gemm_decode"] = {"error": str(e)}
-        try:
-            extra["gemm_quantize"] = gemm_quantize_bench(nv, min(max(5, args.steps), 20), flush)
-        except Exception as e:  # reported, not fatal
-            extra["gemm_quantize"] = {"error": str(e)}
-    if world > 1:
-        extra["allreduce"] = allreduce_bench(nv, world, rank, args, flush=flush)
-        extra["gemm_allreduce"] = gemm_allreduce_bench(nv, world, rank, args, flush=flush)
+            extra[key] = {"error": str(e)}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if not args.no_cpu_baseline:
         cpu = cpu_baseline_gemm()
-        for key, fn in (("quantize", cpu_baseline_quantize), ("allreduce_cpu_baseline", cpu_baseline_allreduce)):
+        for key, fn_ in (("quantize", cpu_baseline_quantize), ("allreduce_cpu_baseline", cpu_baseline_allreduce)):
             try:
-                res = fn()
+                res = fn_()
             except Exception as e:  # reported, not fatal
                 res = {"error": str(e)}
             if key == "quantize":
@@ -563,9 +597,21 @@ def run_ours(args):
             else:
                 extra[key] = res
 
-    traffic = read_profile_traffic("gemm_cfg3")
+    fp4_tf = fp4.get("tflops") if isinstance(fp4, dict) else None
+    peak = fp4_tf if fp4_tf else bf16x4
+    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4),
+                "peak_source": ("FP4 MMA issue rate measured live on this GPU (peak_measured_fp4)" if fp4_tf else
+                                f"4 x {peak_kind} cuBLAS bf16 burst (no live FP4 measurement)"),
+                "peak_measured_fp4": fp4,
+                "frac_of_measured_fp4": round(achieved / fp4_tf, 4) if fp4_tf else None,
+                "peak_4x_bf16_burst": round(bf16x4, 1),
+                "frac_of_4x_bf16_burst": round(achieved / bf16x4, 4),
+                "frac_of_nominal_fp4_9000": round(achieved / FP4_NOMINAL_TFLOPS, 4),
+                "traffic": read_profile_traffic("gemm_cfg3"),
+                "algorithmic_flops_per_launch": flops}
     line = {
-        "metric": "NVFP4 GEMM TFLOPS (1 GPU); NVFP4 all-reduce bf16-equiv GB/s at 2/4/8 B200",
+        "metric": METRIC,
         "value": round(value, 1),
         "unit": "TFLOPS",
         "n_gpus": world,
@@ -578,16 +624,11 @@ def run_ours(args):
         "dtype": "e2m1 x e2m1 (ue4m3 per-16 scales) -> fp32 accumulate -> bf16",
         "data": "synthetic (seeded N(0,1)+0.1% x50 outliers / N(0,0.02), quantized on device)",
         "config": {"workload": "cfg3 NVFP4 GEMM M=N=K=8192, bf16 out", "M": M_, "N": N_, "K": K_,
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "parallelism": "single GPU",
                    "l2": "flushed between timed steps (256 MB write, then 256 MB read)",
                    "tile": "CTA pair (tcgen05 cta_group::2) 256x256, BK=256, 5 stages, persistent"},
-        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(fp4_peak, 1),
-                     "unit": "TFLOP/s", "frac": round(achieved / fp4_peak, 4),
-                     "peak_source": f"4 x {peak_kind} cuBLAS bf16 burst ({peaks.get('bf16_tflops')}) = dense FP4 rate",
-                     "frac_of_nominal_fp4_9000": round(achieved / FP4_NOMINAL_TFLOPS, 4),
-                     "traffic": traffic,
-                     "algorithmic_flops_per_launch": flops},
-        "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12 * world, 2), "unit": "TFLOPS",
+        "roofline": roofline,
+        "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOPS",
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "path": "pinned host A/B/SF -> device, nvfp4_gemm_bf16, device D -> pinned host; steps pipelined "
                         "over two buffer sets (copies of neighbouring steps overlap the GEMM)"},
@@ -597,14 +638,60 @@ def run_ours(args):
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
+    print(json.dumps(line), flush=True)
 
 
-NVLINK_PEER_GBS = 770.0      # measured peer copy per direction per GPU on this pool (900 nominal)
+def pipelined_e2e(host_in, dev_sets, host_out, step_fn, n_steps, world=1):
+    """End-to-end steps through a public entry point with host buffers: per step, H2D copies of
+    `host_in` into one of two device buffer sets, step_fn(dev_set, stream), and a D2H copy of the
+    set's last tensor into host_out; copies of neighbouring steps overlap the step on three
+    streams.  Returns ms per step (device events around the whole run, max over ranks)."""
+    import torch
+    s_in, s_mm, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+
+    def run(n):
+        done_out = [None, None]                       # D2H of the step that last used a buffer set
+        for i in range(n):
+            j = i & 1
+            dev = dev_sets[j]
+            ev_in = torch.cuda.Event()
+            with torch.cuda.stream(s_in):
+                if done_out[j] is not None:
+                    s_in.wait_event(done_out[j])
+                for h, dv in zip(host_in, dev):
+                    dv.copy_(h, non_blocking=True)
+                ev_in.record(s_in)
+            ev_mm = torch.cuda.Event()
+            with torch.cuda.stream(s_mm):
+                s_mm.wait_event(ev_in)
+                step_fn(dev, s_mm)
+                ev_mm.record(s_mm)
+            ev_out = torch.cuda.Event()
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_mm)
+                host_out[j].copy_(dev[-1], non_blocking=True)
+                ev_out.record(s_out)
+            done_out[j] = ev_out
+
+    run(3)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(HIDE_HOST_CYCLES * 8)
+    e0.record()
+    for st in (s_in, s_mm, s_out):
+        st.wait_stream(torch.cuda.current_stream())
+    run(n_steps)
+    for st in (s_in, s_mm, s_out):
+        torch.cuda.current_stream().wait_stream(st)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(e0.elapsed_time(e1) / n_steps, world)
+
+
+NVLINK_PEER_GBS = 770.0      # measured peer copy per direction per GPU on this pool
+NVLINK_NOMINAL_GBS = 900.0   # NVLink 5, per direction per GPU
 
 
 def _ar_time(fn, steps, warmup, flush, world):
@@ -643,71 +730,382 @@ def _ar_time_b2b(fn, calls, warmup, world):
     return max_over_ranks(e0.elapsed_time(e1) / calls, world)
 
 
+def _wire_bytes(name, numel, world, payload_bytes_per_elt):
+    """Bytes one rank sends over NVLink per call: two-shot 2 (n-1)/n of the payload, one-shot
+    (n-1) times the payload."""
+    two = "twoshot" in name
+    return (2.0 * (world - 1) / world if two else (world - 1)) * payload_bytes_per_elt * numel
+
+
 def _ar_entry(name, numel, world, ms, payload_bytes_per_elt):
     """bf16-equivalent algbw / busbw (nccl-tests convention) and wire rate of one algorithm."""
     t = ms * 1e-3
     algbw = 2.0 * numel / t / 1e9
     busbw = algbw * 2.0 * (world - 1) / world
-    two = "twoshot" in name
-    wire = (2.0 * (world - 1) / world if two else (world - 1)) * payload_bytes_per_elt * numel
+    wire = _wire_bytes(name, numel, world, payload_bytes_per_elt)
     return {"us": round(ms * 1e3, 2), "algbw_gbs": round(algbw, 1), "busbw_gbs": round(busbw, 1),
             "wire_bytes_per_rank": int(wire), "wire_gbs_per_rank": round(wire / t / 1e9, 1),
-            "frac_of_nvlink_770": round(wire / t / 1e9 / NVLINK_PEER_GBS, 4)}
+            "frac_of_nvlink_770": round(wire / t / 1e9 / NVLINK_PEER_GBS, 4),
+            "frac_of_nvlink_900": round(wire / t / 1e9 / NVLINK_NOMINAL_GBS, 4)}
 
 
-def allreduce_bench(nv, world, rank, args, numel=None, steps=None, flush=None):
-    """cfg4: every rank holds 4096 x 7168 bf16 N(0, 1), seed = rank.  NVFP4 two-shot / one-shot
-    and the in-house bf16 P2P all-reduce, device time per call (max over ranks), L2 flushed
-    between calls; plus the NVFP4 error against the exact sum and an end-to-end number through
-    the public API with the input copied from pinned host memory and the result copied back."""
+ORACLE_AR = {"nvfp4_twoshot": "ar_twoshot", "nvfp4_oneshot": "ar_oneshot", "nvfp4_lowlat": "ar_oneshot",
+             "bf16_twoshot": "ar_bf16", "bf16_oneshot": "ar_bf16"}
+
+
+def ar_parity(ctx, x, out, gs, world, rank, windows=12, win=8192):
+    """Bit-exact check of every algorithm against the CPU oracle (its fixed-order restatement of
+    the two-shot / one-shot data flow) on sampled windows of the output.  A window of aligned
+    16-element blocks depends only on the same window of every rank's input (quantization blocks,
+    shard boundaries and requantization blocks are all aligned), so rank 0 gathers the ranks'
+    input and output windows and runs the oracle on them.  The low-latency one-shot is checked on
+    a prefix within its size cap."""
+    import numpy as np
     import torch
     import torch.distributed as dist
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import py_oracle
+    from tensorcore_ptx_example_b200 import allreduce as ar
+    numel = x.numel()
+    res = {"windows": windows, "window_elems": win}
+    ok_all = True
+    cases = [("nvfp4_twoshot", numel), ("nvfp4_oneshot", numel), ("bf16_twoshot", numel),
+             ("bf16_oneshot", numel), ("nvfp4_lowlat", min(numel, ar.LOWLAT_CAP_BYTES // 2))]
+    for name, n in cases:
+        nw = min(windows, n // win)
+        rng = np.random.default_rng(1234 + n)
+        starts = np.sort(rng.choice(n // win, size=nw, replace=False)) * win
+        idx = torch.from_numpy(np.concatenate([np.arange(s0, s0 + win) for s0 in starts])).cuda()
+        xs, os_ = x[:n], out[:n]
+        algo = name.split("_", 1)[1]
+        if name.startswith("bf16"):
+            ctx.bf16_allreduce(xs, os_, algo=algo)
+        else:
+            ctx.allreduce(xs, os_, global_scale=gs, algo=algo)
+        xin = x[idx].contiguous()
+        xout = out[idx].contiguous()
+        ins = [torch.empty_like(xin) for _ in range(world)]
+        outs = [torch.empty_like(xout) for _ in range(world)]
+        dist.all_gather(ins, xin)
+        dist.all_gather(outs, xout)
+        ok = True
+        if rank == 0:
+            u16 = [t.view(torch.int16).cpu().numpy().view(np.uint16) for t in ins]
+            fn = getattr(py_oracle, ORACLE_AR[name])
+            want = fn(u16) if name.startswith("bf16") else fn(u16, gs)
+            for r in range(world):
+                got = outs[r].view(torch.int16).cpu().numpy().view(np.uint16)
+                ok = ok and bool(np.array_equal(got, want))
+        res[name] = ok
+        ok_all = ok_all and ok
+    torch.cuda.synchronize()
+    flag = torch.tensor([1 if ok_all else 0], dtype=torch.int32, device="cuda")
+    dist.broadcast(flag, 0)
+    res["all"] = bool(flag.item())
+    return res
 
+
+def allreduce_algos(ctx, x, out, gs, world, steps, flush):
+    """cfg4, every algorithm: device time per call (max over ranks, L2 flushed between calls),
+    and the NVFP4 error against the exact fp32 sum."""
+    import torch
+    import torch.distributed as dist
+    numel = x.numel()
+    res = {}
+    runs = [("nvfp4_twoshot", lambda: ctx.allreduce(x, out, global_scale=gs, algo="twoshot"), 0.5625),
+            ("nvfp4_oneshot", lambda: ctx.allreduce(x, out, global_scale=gs, algo="oneshot"), 0.5625),
+            ("bf16_twoshot", lambda: ctx.bf16_allreduce(x, out, algo="twoshot"), 2.0),
+            ("bf16_oneshot", lambda: ctx.bf16_allreduce(x, out, algo="oneshot"), 2.0)]
+    for name, fn, bpe in runs:
+        res[name] = _ar_entry(name, numel, world, _ar_time(fn, steps, 3, flush, world), bpe)
+    exact = x.float().clone()
+    dist.all_reduce(exact)
+    for algo in ("twoshot", "oneshot"):
+        o = ctx.allreduce(x, out, global_scale=gs, algo=algo).float()
+        res[f"nvfp4_{algo}"]["rel_rmse_vs_fp32_sum"] = round(float((o - exact).norm() / exact.norm()), 5)
+        res[f"nvfp4_{algo}"]["max_abs_err_vs_fp32_sum"] = round(float((o - exact).abs().max()), 4)
+    torch.cuda.synchronize()
+    return res, exact
+
+
+SWEEP_ROWS_BYTES = [64 << 10, 1 << 20, 4 << 20, 16 << 20, 64 << 20, 256 << 20]
+
+
+def ar_sweep_rows(ctx, xfull, ofull, gs, world, sizes=SWEEP_ROWS_BYTES):
+    """cfg5 rows: every algorithm at each size, back-to-back calls (max over ranks); best NVFP4
+    against best bf16."""
+    from tensorcore_ptx_example_b200 import allreduce as ar
+    rows = []
+    for b in sizes:
+        n = b // 2
+        if n % (32 * world) or n > xfull.numel():
+            continue
+        x, o = xfull[:n], ofull[:n]
+        calls = 50 if b <= (16 << 20) else 10
+        algos = [("nvfp4_lowlat", lambda: ctx.allreduce(x, o, global_scale=gs, algo="lowlat")),
+                 ("nvfp4_oneshot", lambda: ctx.allreduce(x, o, global_scale=gs, algo="oneshot")),
+                 ("nvfp4_twoshot", lambda: ctx.allreduce(x, o, global_scale=gs, algo="twoshot")),
+                 ("bf16_oneshot", lambda: ctx.bf16_allreduce(x, o, algo="oneshot")),
+                 ("bf16_twoshot", lambda: ctx.bf16_allreduce(x, o, algo="twoshot"))]
+        if b > ar.LOWLAT_CAP_BYTES:
+            algos = algos[1:]
+        row = {"bytes": b}
+        for name, fn in algos:
+            row[name + "_us"] = round(_ar_time_b2b(fn, calls, 3, world) * 1e3, 2)
+        best_fp4 = min((k for k in row if k.startswith("nvfp4")), key=lambda k: row[k])
+        best_bf16 = min((k for k in row if k.startswith("bf16")), key=lambda k: row[k])
+        row["best_nvfp4"] = best_fp4[:-3]
+        row["best_bf16"] = best_bf16[:-3]
+        row["best_nvfp4_algbw_gbs"] = round(2.0 * n / (row[best_fp4] * 1e-6) / 1e9, 1)
+        row["best_bf16_algbw_gbs"] = round(2.0 * n / (row[best_bf16] * 1e-6) / 1e9, 1)
+        row["nvfp4_speedup_vs_bf16"] = round(row[best_bf16] / row[best_fp4], 3)
+        rows.append(row)
+    return rows
+
+
+def reference_ar_kernels(world, rank, x, gs, steps, flush, exact):
+    """Same-box baseline: the reference's own fused two-shot and one-shot kernels
+    (launch_fused_rank / launch_oneshot_fused_rank, nvfp4_allreduce.cuh:650-682), compiled from
+    the reference header into oracle/_ref/libref_ar.so, on the same GPUs and inputs (SFScaleVal =
+    1 / gs), their buffers shared through CUDA IPC: device time per call (max over ranks) and
+    error against the exact fp32 sum.  Each grid is the launcher's NVLink default capped at the
+    blocks that are resident at once (the fused kernels' block barriers wait for the same block
+    index on every rank).  Every rank takes the same steps; the kernels launch only after every
+    rank has confirmed its buffers and peer mappings."""
+    import ctypes
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import py_oracle
+
+    def all_ok(flag):
+        t = torch.tensor([1 if flag else 0], dtype=torch.int32, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        return bool(t.item())
+
+    def all_min(v):
+        t = torch.tensor([int(v)], dtype=torch.int64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        return int(t.item())
+
+    if not all_ok(py_oracle.ref_ar_available() and world in (2, 4, 8)):
+        return {"unavailable": "oracle/_ref/libref_ar.so not built, or world not in {2, 4, 8}"}
+    L = py_oracle.ref_ar_lib()
+    numel = x.numel()
+    shard = numel // world
+    sizes = {"comm2": L.ref_fused_comm_bytes(shard, world), "bin": 4 * L.ref_fused_barrier_words(world),
+             "bout": 4 * L.ref_fused_barrier_words(world), "comm1": L.ref_oneshot_comm_bytes(numel, world),
+             "bar1": 4 * L.ref_fused_barrier_words(world)}
+    own, opened, arrays = {}, [], {}
+    res = {}
+    try:
+        ok = True
+        for k, nbytes in sizes.items():
+            p = ctypes.c_void_p()
+            ok = ok and L.ref_dev_alloc_zero(nbytes, ctypes.byref(p)) == 0
+            own[k] = p
+        if not all_ok(ok):
+            return {"unavailable": "allocation failed"}
+        hb = int(L.ref_ipc_handle_bytes())
+        mine = {}
+        for k, p in own.items():
+            buf = ctypes.create_string_buffer(hb)
+            ok = ok and L.ref_ipc_get(p, buf) == 0
+            mine[k] = buf.raw
+        gathered = [None] * world
+        dist.all_gather_object(gathered, mine)
+        for k in sizes:
+            ptrs = []
+            for r in range(world):
+                if r == rank:
+                    ptrs.append(own[k].value)
+                    continue
+                q = ctypes.c_void_p()
+                ok = ok and L.ref_ipc_open(gathered[r][k], ctypes.byref(q)) == 0
+                opened.append(q)
+                ptrs.append(q.value)
+            arr = ctypes.c_void_p()
+            host = (ctypes.c_void_p * world)(*ptrs)
+            ok = ok and L.ref_dev_ptr_array(host, world, ctypes.byref(arr)) == 0
+            arrays[k] = arr
+        grid2 = min(int(L.ref_default_fused_grid(shard, 256)), int(L.ref_fused_resident_blocks(world, 0)))
+        grid1 = min(int(L.ref_default_fused_grid(numel, 256)), int(L.ref_fused_resident_blocks(world, 1)))
+        grid2, grid1 = all_min(grid2), all_min(grid1)
+        if not all_ok(ok and grid2 > 0 and grid1 > 0):
+            return {"unavailable": "IPC mapping or occupancy query failed"}
+        torch.cuda.synchronize()
+        out = torch.empty_like(x)
+        sf_val = float(np.float32(1.0) / np.float32(gs))
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        xp, op = ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(out.data_ptr())
+        flags = {"two": 0, "one": 0}
+
+        def twoshot():
+            flags["two"] += 1
+            rc = L.ref_launch_twoshot(world, xp, op, arrays["comm2"], arrays["bin"], arrays["bout"], rank, numel,
+                                      sf_val, flags["two"], st, grid2)
+            if rc:
+                raise RuntimeError(f"ref_launch_twoshot: cuda error {rc}")
+
+        def oneshot():
+            flags["one"] += 1
+            rc = L.ref_launch_oneshot(world, xp, op, arrays["comm1"], arrays["bar1"], rank, numel, sf_val,
+                                      flags["one"], st, grid1)
+            if rc:
+                raise RuntimeError(f"ref_launch_oneshot: cuda error {rc}")
+
+        for name, fn in (("reference_twoshot", twoshot), ("reference_oneshot", oneshot)):
+            ms = _ar_time(fn, steps, 3, flush, world)
+            e = _ar_entry(name, numel, world, ms, 0.5625)
+            fn()
+            o = out.float()
+            e["rel_rmse_vs_fp32_sum"] = round(float((o - exact).norm() / exact.norm()), 5)
+            e["grid"] = grid2 if "two" in name else grid1
+            res[name] = e
+        torch.cuda.synchronize()
+        res["kernels"] = "nvfp4_ar::twoshot_fused_kernel / oneshot_fused_kernel (reference, oracle/_ref/libref_ar.so)"
+        return res
+    finally:
+        torch.cuda.synchronize()
+        barrier(world)
+        for q in opened:
+            L.ref_ipc_close(q)
+        for arr in arrays.values():
+            L.ref_dev_free(arr)
+        for p in own.values():
+            if p.value:
+                L.ref_dev_free(p)
+        torch.cuda.synchronize()
+        barrier(world)
+
+
+def gemm_replicas(nv, world, rank, steps, flush):
+    """Every rank runs its own cfg3 GEMM (independent replicas, no exchange): aggregate TFLOPS."""
+    import torch
+    pa, sa, pb, sb, alpha, d = gemm_setup(nv, rank)
+    fn = lambda: nv.gemm(pa, sa, pb, sb, M_, N_, K_, alpha=alpha, out=d)  # noqa: E731
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    ts = timed_steps(fn, steps, flush)
+    barrier(world)
+    total = max_over_ranks(sum(ts), world)
+    return {"workload": "cfg3 GEMM 8192^3 on every rank (replicas)", "steps": steps,
+            "aggregate_tflops": round(2.0 * M_ * N_ * K_ * steps * world / (total * 1e-3) / 1e12, 1)}
+
+
+def run_allreduce_line(args):
+    """N > 1: the cfg4 NVFP4 all-reduce as the headline (see the module docstring)."""
+    import torch
+
+    import tensorcore_ptx_example_b200 as nv
     from tensorcore_ptx_example_b200 import allreduce as ar
     from tensorcore_ptx_example_b200 import workloads
+    world, rank, local = dist_setup(args)
+    flush = L2Flush()
     rows, cols = workloads.CFG4_SHAPE
-    numel = numel or rows * cols
-    steps = steps or max(5, min(args.steps, 20))
+    numel = rows * cols
+    sweep_max = max(SWEEP_ROWS_BYTES) // 2
     x = workloads.gaussian(1, numel, seed=rank).view(-1)
     gs = ar.agree_global_scale(float(nv.amax(x).item()))
-    ctx = ar.AllReduce.from_process_group(numel)
+    ctx = ar.AllReduce.from_process_group(max(numel, sweep_max))
     out = torch.empty_like(x)
-    res = {"workload": f"cfg4 all-reduce {numel} bf16 elements per rank (N(0,1), seed = rank)",
-           "world": world, "global_scale": gs, "l2": "flushed between calls" if flush is not None else "not flushed"}
+    algo = {ar.ONESHOT: "oneshot", ar.TWOSHOT: "twoshot", ar.LOWLAT: "lowlat"}[ar.choose_algo(world, numel)]
+    extra = {}
     try:
-        runs = [("nvfp4_twoshot", lambda: ctx.allreduce(x, out, global_scale=gs, algo="twoshot"), 0.5625),
-                ("nvfp4_oneshot", lambda: ctx.allreduce(x, out, global_scale=gs, algo="oneshot"), 0.5625),
-                ("bf16_twoshot", lambda: ctx.bf16_allreduce(x, out, algo="twoshot"), 2.0),
-                ("bf16_oneshot", lambda: ctx.bf16_allreduce(x, out, algo="oneshot"), 2.0)]
-        for name, fn, bpe in runs:
-            ms = _ar_time(fn, steps, 3, flush, world)
-            res[name] = _ar_entry(name, numel, world, ms, bpe)
-        # accuracy of both NVFP4 algorithms against the exact (fp32, NCCL) sum
-        exact = x.float().clone()
-        dist.all_reduce(exact)
-        for algo in ("twoshot", "oneshot"):
-            o = ctx.allreduce(x, out, global_scale=gs, algo=algo).float()
-            res[f"nvfp4_{algo}"]["rel_rmse_vs_fp32_sum"] = round(float((o - exact).norm() / exact.norm()), 5)
+        fn = lambda: ctx.allreduce(x, out, global_scale=gs, algo="auto")  # noqa: E731
+        for _ in range(args.warmup):
+            fn()
         torch.cuda.synchronize()
-        res["device_status"] = nv.device_status()
-        # end to end: pinned host input -> device, all-reduce (two-shot), device -> pinned host
-        hx = x.cpu().pin_memory()
-        ho = torch.empty_like(hx).pin_memory()
+        barrier(world)
+        torch.cuda.synchronize()
+        sampler = ClockSampler(local)
+        sampler.start()
+        ts = timed_steps(fn, args.steps, flush)
+        clocks = sampler.stop()
+        barrier(world)
+        total_ms = max_over_ranks(sum(ts), world)
+        mean_ms = max_over_ranks(sum(ts) / len(ts), world)
+        status = nv.device_status()
+        value = 2.0 * numel * args.steps / (total_ms * 1e-3) / 1e9
+        wire = _wire_bytes(algo, numel, world, 0.5625)
+        achieved = wire / (mean_ms * 1e-3) / 1e9
 
-        def e2e():
-            x.copy_(hx, non_blocking=True)
-            ctx.allreduce(x, out, global_scale=gs, algo="twoshot")
-            ho.copy_(out, non_blocking=True)
-        e2e_ms = _ar_time(e2e, max(3, steps // 2), 2, None, world)
-        res["e2e_nvfp4_twoshot"] = {"us": round(e2e_ms * 1e3, 2),
-                                    "algbw_gbs": round(2.0 * numel / (e2e_ms * 1e-3) / 1e9, 1),
-                                    "h2d_bytes_per_step": numel * 2, "d2h_bytes_per_step": numel * 2}
-        res["gpu_launches_per_call"] = 1
+        parity = ar_parity(ctx, x, out, gs, world, rank)
+        algos, exact = allreduce_algos(ctx, x, out, gs, world, max(5, min(args.steps, 20)), flush)
+
+        # end to end through the public API with host buffers: the input copied from pinned
+        # host memory and the result copied back every step (pipelined like the GEMM's)
+        hx = x.cpu().pin_memory()
+        dev_sets = [(x, out), (torch.empty_like(x), torch.empty_like(x))]
+        host_out = [torch.empty_like(hx).pin_memory() for _ in range(2)]
+        e2e_steps = max(4, min(args.steps, 12))
+        e2e_ms = pipelined_e2e([hx], dev_sets, host_out,
+                               lambda dev, s: ctx.allreduce(dev[0], dev[1], global_scale=gs, algo="auto", stream=s),
+                               e2e_steps, world)
+        ok_e2e = bool(torch.equal(host_out[(e2e_steps - 1) & 1], out.cpu()))
+
+        xfull = workloads.gaussian(1, sweep_max, seed=100 + rank).view(-1)
+        gs_sweep = ar.agree_global_scale(float(nv.amax(xfull).item()))
+        ofull = torch.empty_like(xfull)
+        sweep = ar_sweep_rows(ctx, xfull, ofull, gs_sweep, world)
+        del xfull, ofull
+        status = status or nv.device_status()
     finally:
         torch.cuda.synchronize()
         barrier(world)
         ctx.close()
-    return res
+    for key, fn_ in (("gemm_allreduce", lambda: gemm_allreduce_bench(nv, world, rank, args, flush=flush)),
+                     ("gemm_replicas", lambda: gemm_replicas(nv, world, rank, 10, flush))):
+        extra[key] = fn_()
+    # the reference's kernels last: they wait without a time limit, so they run only after every
+    # measurement of ours is in
+    extra["reference_kernels"] = reference_ar_kernels(world, rank, x, gs, max(5, min(args.steps, 20)), flush, exact)
+
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 in/out; NVFP4 (e2m1 + ue4m3 per 16) on the wire; fp32 sums in rank order",
+        "data": "synthetic (seeded N(0,1) bf16 per rank, seed = rank)",
+        "config": {"workload": f"cfg4 NVFP4 all-reduce, {rows}x{cols} bf16 per rank", "numel_per_rank": numel,
+                   "algorithm": f"NVFP4_AR_AUTO -> {algo}", "parallelism": f"all-reduce over {world} GPUs (NVLink P2P)",
+                   "value_convention": "bf16-equivalent algbw = 2 * numel_per_rank / t (nccl-tests)",
+                   "l2": "flushed between timed steps (256 MB write, then 256 MB read); input 58.7 MB per rank"},
+        "busbw_gbs": round(value * 2.0 * (world - 1) / world, 1),
+        "roofline": {"bound": "nvlink", "achieved": round(achieved, 1), "peak": NVLINK_PEER_GBS, "unit": "GB/s",
+                     "frac": round(achieved / NVLINK_PEER_GBS, 4),
+                     "frac_of_900": round(achieved / NVLINK_NOMINAL_GBS, 4),
+                     "peak_source": "measured peer copy per direction per GPU on this pool (900 nominal)",
+                     "achieved_is": "wire bytes one rank sends per call / mean call time",
+                     "wire_bytes_per_launch": int(wire), "traffic": None},
+        "parity_ok": parity["all"],
+        "parity": parity,
+        "device_status": status,
+        "algorithms": algos,
+        "sweep_rows": sweep,
+        "e2e": {"value": round(2.0 * numel / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": numel * 2, "d2h_bytes_per_step": numel * 2, "result_matches": ok_e2e,
+                "path": "pinned host bf16 -> device, nvfp4_ar_allreduce (AUTO), device -> pinned host; steps "
+                        "pipelined over two buffer sets"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        **extra,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    import torch.distributed as dist
+    dist.destroy_process_group()
 
 
 def gemm_allreduce_bench(nv, world, rank, args, flush=None):
@@ -825,29 +1223,45 @@ def read_profile_traffic(name):
 
 
 def run_reference(args):
+    """The reference arm: the reference's CPU path on rank 0 (the other ranks exit without work),
+    on this line's metric and config, each step a bounded sample."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     vals = []
     res = None
-    for i in range(args.warmup + args.steps):
-        res = cpu_baseline_gemm(target_s=2.0)
-        if i >= args.warmup:
-            vals.append(res["value"])
+    if world > 1:
+        sample = CpuAllReduceSample(world)
+        for i in range(args.warmup + args.steps):
+            res = sample.measure(target_s=0.5)
+            if i >= args.warmup:
+                vals.append(res["value"])
+        unit = "GB/s"
+        config = {"workload": "cfg4 NVFP4 all-reduce, 4096x7168 bf16 per rank (bounded CPU sample per step)",
+                  "numel_per_rank": 4096 * 7168, "ranks": world,
+                  "value_convention": "bf16-equivalent algbw = 2 * numel_per_rank / t (nccl-tests)"}
+        dtype = "fp32 sums in rank order (CPU restatement of the NVFP4 two-shot; the reference has no CPU all-reduce)"
+        data = "synthetic (seeded N(0,1) bf16 per rank)"
+    else:
+        for i in range(args.warmup + args.steps):
+            res = cpu_baseline_gemm(target_s=2.0)
+            if i >= args.warmup:
+                vals.append(res["value"])
+        unit = "TFLOPS"
+        config = {"workload": "cfg3 NVFP4 GEMM M=N=K=8192 (bounded CPU sample per step)", "M": M_, "N": N_, "K": K_}
+        dtype = "fp32 (reference CPU path on decoded E2M1 values)"
+        data = "synthetic (seeded E2M1 values)"
     v = sum(vals) / len(vals)
     line = {
         "impl": "reference",
-        "metric": "NVFP4 GEMM TFLOPS (1 GPU); NVFP4 all-reduce bf16-equiv GB/s at 2/4/8 B200",
-        "value": v, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "metric": METRIC,
+        "value": v, "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "fp32 (reference CPU path on decoded E2M1 values)",
-        "data": "synthetic (seeded E2M1 values)",
-        "config": {"workload": "cfg3 NVFP4 GEMM M=N=K=8192 (bounded CPU sample per step)",
-                   "M": M_, "N": N_, "K": K_},
-        "cpu_baseline": {"value": v, "unit": "TFLOPS", "cores": res["cores"], "kind": res["kind"],
+        "dtype": dtype, "data": data, "config": config,
+        "cpu_baseline": {"value": v, "unit": unit, "cores": res["cores"], "kind": res["kind"],
                          "sample": res["sample"]},
-        "e2e": {"value": v, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -917,8 +1331,10 @@ def main():
         run_only(args)
     elif args.impl == "reference":
         run_reference(args)
+    elif int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        run_allreduce_line(args)
     else:
-        run_ours(args)
+        run_gemm_line(args)
 
 
 if __name__ == "__main__":

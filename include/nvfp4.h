@@ -37,9 +37,9 @@
  *   - blackwell/allreduce_sm100_sm120/nvfp4_allreduce.cuh:344-352,398  fused_comm_bytes /
  *     oneshot_comm_bytes / fused_barrier_words (caller-allocated)   -> nvfp4_ar_create (library-owned)
  *   - blackwell/allreduce_sm100_sm120/bench_ar.cu:770-772,833-850   peer pointer setup ->
- *     nvfp4_ar_set_peers_inprocess / nvfp4_ar_ipc_handle + nvfp4_ar_open_peers
+ *     nvfp4_ar_set_peers (one process) / nvfp4_ar_export_handle + nvfp4_ar_open_peers (IPC)
  *   - blackwell/allreduce_sm100_sm120/bench_ar.cu:83,132 (third-party bf16 kernels used as
- *     the baseline)                                                  -> nvfp4_bf16_allreduce (own code)
+ *     the baseline)                                                  -> nvfp4_ar_bf16_allreduce (own code)
  */
 #ifndef NVFP4_B200_H
 #define NVFP4_B200_H
@@ -88,18 +88,23 @@ NVFP4_API int64_t nvfp4_sf_bytes(int64_t rows, int64_t cols);
 NVFP4_API int64_t nvfp4_sf_offset(int64_t row, int64_t kblock, int64_t cols);
 
 /* ----------------------------------------------------------- quantizer ---- */
-/* amax_dev[0] = max |x| over numel bf16 values (device float; overwritten).
- * numel % 8 == 0, x 16-byte aligned. */
+/* amax_dev[0] = max |x| over the finite values among numel bf16 values (device float;
+ * overwritten).  NaN and Inf are skipped and recorded as a device status (DEV_NONFINITE_INPUT,
+ * 0x302, read with nvfp4_device_status).  numel % 8 == 0, x 16-byte aligned. */
 NVFP4_API nvfp4_status_t nvfp4_amax_bf16(const void* x, int64_t numel, float* amax_dev, void* stream);
 
 /* Quantize a rows x cols bf16 tensor with a given global scale gs (> 0).
  * cols % 64 == 0; x, packed and sf 16-byte aligned.  Writes rows*cols/2 bytes of packed
- * data and all nvfp4_sf_bytes(rows, cols) scale bytes (padding rows get scale 0). */
+ * data and all nvfp4_sf_bytes(rows, cols) scale bytes (padding rows get scale 0).
+ * Non-finite input: a 16-element block holding a NaN or an Inf gets scale byte 0x7F (the E4M3
+ * NaN, so the block dequantizes to NaN; NVFP4 has no encoding for non-finite values) and zero
+ * codes, and the device status DEV_NONFINITE_INPUT (0x302) is recorded. */
 NVFP4_API nvfp4_status_t nvfp4_quantize_bf16(const void* x, int64_t rows, int64_t cols, float global_scale,
                                    void* packed, void* sf, void* stream);
 
-/* Same, with the global scale computed on the device from the tensor's own amax
- * (gs = amax / 2688, amax 0 -> gs 1).  Writes gs to global_scale_dev[0].  Two kernels
+/* Same, with the global scale computed on the device from the tensor's own amax over its finite
+ * values (gs = amax / 2688, amax 0 -> gs 1; an empty tensor also gets gs 1).  Writes gs to
+ * global_scale_dev[0].  Two kernels
  * (amax reduction, then quantize); no host synchronisation.  The amax travels between the
  * two kernels through `workspace`, a device scratch buffer of at least
  * nvfp4_quantize_workspace_bytes() bytes (its contents on entry do not matter). */
@@ -113,8 +118,10 @@ NVFP4_API nvfp4_status_t nvfp4_quantize_bf16_auto(const void* x, int64_t rows, i
  * fixed 256-byte file-scope device array of this library instead (one per device, held until
  * the process exits; the scratch it needs does not grow with rows x cols).  It calls no
  * cudaMalloc / cudaFree.  The first call on a device looks the array's address up with
- * cudaGetSymbolAddress: make that call before any stream capture.  All calls on a device share
- * the array and clear it on `stream` before use, so calls that overlap on the GPU race. */
+ * cudaGetSymbolAddress and keeps it for the life of the process: make that call before any
+ * stream capture, and do not use this entry point on a device after cudaDeviceReset (the reset
+ * reloads the module, and the kept address would be stale).  All calls on a device share the
+ * array and clear it on `stream` before use, so calls that overlap on the GPU race. */
 NVFP4_API nvfp4_status_t nvfp4_quantize_bf16_auto_noalloc(const void* x, int64_t rows, int64_t cols, void* packed,
                                                 void* sf, float* global_scale_dev, void* stream);
 
@@ -253,18 +260,6 @@ NVFP4_API nvfp4_status_t nvfp4_gemm_allreduce_emulated(nvfp4_ar_t const* handles
                                                        const void* const* sfb, const float* alpha,
                                                        float global_scale, void* const* outs, int64_t M, int64_t N,
                                                        int64_t K, void* stream);
-
-/* ----------------------------------------------------------- diagnostics ---- */
-/* Device codec probes (used by the parity tests to pin the hardware conversions):
- * out[i] = E2M1 code of x[i] (RNE, satfinite) / E4M3 code of x[i]. */
-NVFP4_API nvfp4_status_t nvfp4_diag_e2m1_encode(const float* x, uint8_t* out, int64_t n, void* stream);
-NVFP4_API nvfp4_status_t nvfp4_diag_e4m3_encode(const float* x, uint8_t* out, int64_t n, void* stream);
-/* FP4 tensor-core issue-rate microbenchmark: every SM (cta_group 1, M128 N256) or SM pair
- * (cta_group 2, M256 N256) issues `iters` K64 block-scaled MMAs from resident shared memory,
- * on sparse constant operands or (random_operands != 0) pseudo-random E2M1 codes.
- * FLOPs = 2 * 128 * 256 * 64 * iters * (number of SMs); time it with events around the call.
- * The measured rate is the roofline denominator of nvfp4_gemm_bf16. */
-NVFP4_API nvfp4_status_t nvfp4_diag_mma_peak(int cta_group, int iters, int random_operands, void* stream);
 
 #ifdef __cplusplus
 }

@@ -118,11 +118,12 @@ void orc_global_scale(float amax, float* gs, float* gs_inv) {
     *gs_inv = 1.0f / g;
 }
 
+/* max |x| over the finite values (NaN and Inf are skipped, as the GPU amax kernel does). */
 float orc_amax_bf16(const uint16_t* x, int64_t n) {
     float m = 0.0f;
     for (int64_t i = 0; i < n; i++) {
         const float a = fabsf(orc_bf16_to_f32(x[i]));
-        if (a > m) m = a;
+        if (isfinite(a) && a > m) m = a;
     }
     return m;
 }
@@ -138,7 +139,18 @@ float orc_amax_f32(const float* x, int64_t n) {
 
 void orc_q16(const float* v, float gs_inv, uint8_t* nib, uint8_t* sf) {
     float amax = 0.0f;
-    for (int i = 0; i < 16; i++) amax = fmaxf(amax, fabsf(v[i]));
+    int nonfinite = 0;
+    for (int i = 0; i < 16; i++) {
+        amax = fmaxf(amax, fabsf(v[i]));
+        nonfinite |= !isfinite(v[i]);
+    }
+    /* a block with a NaN or an Inf: scale = E4M3 NaN (0x7F), codes 0 (NVFP4 has no encoding
+     * for non-finite values; the block dequantizes to NaN) */
+    if (nonfinite) {
+        *sf = 0x7F;
+        for (int i = 0; i < 16; i++) nib[i] = 0;
+        return;
+    }
     /* fp32(1/6) rounded to nearest (0x3E2AAAAB) */
     const float rcp6 = 0.16666667163372039794921875f;
     const float t = amax * rcp6;

@@ -293,3 +293,45 @@ def ref_lib():
         L.ref_vr_verify_cpu.argtypes = [ctypes.c_int] * 4 + [ctypes.c_uint32]
         _ref = L
     return _ref
+
+
+_ref_ar = None
+
+
+def ref_ar_available() -> bool:
+    return os.path.exists(REF_AR_PATH)
+
+
+def ref_ar_lib():
+    """The reference's nvfp4_allreduce.cuh kernels compiled into oracle/_ref/libref_ar.so
+    (oracle/ref_ar_shim.cu): the reference's own GPU quantizer and fused all-reduce launchers,
+    run on the GPU box beside this project's kernels as a same-box comparator."""
+    global _ref_ar
+    if _ref_ar is None:
+        L = ctypes.CDLL(REF_AR_PATH)
+        P, I, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
+        sigs = {
+            "ref_column_bytes": (SZ, [SZ]),
+            "ref_fused_comm_bytes": (SZ, [SZ, I]),
+            "ref_oneshot_comm_bytes": (SZ, [SZ, I]),
+            "ref_fused_barrier_words": (SZ, [I]),
+            "ref_default_fused_grid": (I, [SZ, I]),
+            "ref_layout_total_bytes": (SZ, [SZ]),
+            "ref_quantize": (I, [P, P, SZ, ctypes.c_float, P]),
+            "ref_launch_twoshot": (I, [I, P, P, P, P, P, I, SZ, ctypes.c_float, ctypes.c_uint32, P, I]),
+            "ref_launch_oneshot": (I, [I, P, P, P, P, I, SZ, ctypes.c_float, ctypes.c_uint32, P, I]),
+            "ref_fused_resident_blocks": (I, [I, I]),
+            "ref_dev_alloc_zero": (I, [SZ, ctypes.POINTER(P)]),
+            "ref_dev_free": (I, [P]),
+            "ref_dev_ptr_array": (I, [P, I, ctypes.POINTER(P)]),
+            "ref_ipc_handle_bytes": (SZ, []),
+            "ref_ipc_get": (I, [P, P]),
+            "ref_ipc_open": (I, [P, ctypes.POINTER(P)]),
+            "ref_ipc_close": (I, [P]),
+        }
+        for name, (res, args) in sigs.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _ref_ar = L
+    return _ref_ar

@@ -4,12 +4,27 @@
 // blackwell/allreduce_sm100_sm120/nvfp4_allreduce.cuh from the read-only reference tree
 // (include path set by oracle/Makefile).  The built library (oracle/_ref/libref_ar.so) lets
 // the GPU box run the reference's own quantize / fused one-shot / fused two-shot kernels
-// beside this project's kernels for a same-box comparison.  Nothing in the product links
-// against it.
+// beside this project's kernels for a same-box comparison (the quantizer parity test, and the
+// benchmark's reference-kernel baselines).  Nothing in the product links against it.  The
+// ref_ipc_* / ref_dev_* helpers at the end only allocate and share the buffers the reference
+// launchers require (zeroed device memory, CUDA IPC handles, device arrays of peer pointers).
 #include <cstdint>
 #include <cstddef>
+#include <cstring>
 
 #include "nvfp4_allreduce.cuh"   // the reference header, found through -I
+
+// Blocks of a fused kernel that can be resident at once on the current device (256 threads per
+// block, the launchers' default).  The fused kernels wait in block_barrier for the same block
+// index on every rank, so a grid no larger than this always makes progress.
+template <typename K>
+static int resident_blocks(K kernel) {
+    int per_sm = 0, dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, 0) != cudaSuccess) return -1;
+    return per_sm * sms;
+}
 
 extern "C" {
 
@@ -66,5 +81,41 @@ int ref_launch_oneshot(int world, const void* in, void* out, void* peer_comm, vo
     }
     return (int)cudaGetLastError();
 }
+
+int ref_fused_resident_blocks(int world, int oneshot) {
+    switch (world) {
+        case 2: return oneshot ? resident_blocks(nvfp4_ar::oneshot_fused_kernel<2>) : resident_blocks(nvfp4_ar::twoshot_fused_kernel<2>);
+        case 4: return oneshot ? resident_blocks(nvfp4_ar::oneshot_fused_kernel<4>) : resident_blocks(nvfp4_ar::twoshot_fused_kernel<4>);
+        case 8: return oneshot ? resident_blocks(nvfp4_ar::oneshot_fused_kernel<8>) : resident_blocks(nvfp4_ar::twoshot_fused_kernel<8>);
+        default: return -1;
+    }
+}
+
+// ---- buffer plumbing for the reference launchers (not reference code) ----
+// Zeroed device allocation of `bytes`.
+int ref_dev_alloc_zero(size_t bytes, void** ptr) {
+    *ptr = nullptr;
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return (int)e;
+}
+int ref_dev_free(void* ptr) { return (int)cudaFree(ptr); }
+// Device array of n pointers (the peer tables the launchers take).
+int ref_dev_ptr_array(void* const* host_ptrs, int n, void** dev_array) {
+    cudaError_t e = cudaMalloc(dev_array, sizeof(void*) * (size_t)n);
+    if (e == cudaSuccess) e = cudaMemcpy(*dev_array, host_ptrs, sizeof(void*) * (size_t)n, cudaMemcpyHostToDevice);
+    return (int)e;
+}
+size_t ref_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+int ref_ipc_get(void* ptr, void* handle_out) {
+    return (int)cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(handle_out), ptr);
+}
+int ref_ipc_open(const void* handle, void** ptr) {
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    return (int)cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+}
+int ref_ipc_close(void* ptr) { return (int)cudaIpcCloseMemHandle(ptr); }
 
 }  // extern "C"

@@ -44,9 +44,6 @@ SIGNATURES = {
     "nvfp4_gemm_bf16_ws": (_I, [_P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
     "nvfp4_gemm_quantize": (_I, [_P, _P, _P, _P, _F, _F, _P, _P, _I64, _I64, _I64, _P]),
     "nvfp4_gemm_bf16_flags": (_I, [_P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _I, _P]),
-    "nvfp4_diag_e2m1_encode": (_I, [_P, _P, _I64, _P]),
-    "nvfp4_diag_e4m3_encode": (_I, [_P, _P, _I64, _P]),
-    "nvfp4_diag_mma_peak": (_I, [_I, _I, _I, _P]),
     "nvfp4_ar_buffer_bytes": (_I64, [_I, _I64]),
     "nvfp4_ar_create": (_I, [_I, _I, _I64, ctypes.POINTER(ctypes.c_void_p)]),
     "nvfp4_ar_destroy": (_I, [_P]),
@@ -106,6 +103,18 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr())
 
 
+def _empty(shape, dtype, device, stream=None):
+    """torch.empty for a buffer that kernels on `stream` will use.  Allocations come from torch's
+    caching allocator on the current stream; when the caller names another stream, the buffer is
+    also recorded on that one, so the allocator does not hand its memory out again (after this
+    function drops it, or after the caller frees it) before the work queued on `stream` is done."""
+    import torch
+    t = torch.empty(shape, dtype=dtype, device=device)
+    if stream is not None and stream != torch.cuda.current_stream(t.device):
+        t.record_stream(stream)
+    return t
+
+
 def device_status(clear: bool = True) -> int:
     v = ctypes.c_uint(0)
     check(lib().nvfp4_device_status(ctypes.byref(v), 1 if clear else 0))
@@ -131,7 +140,7 @@ def amax(x, out=None, stream=None):
     import torch
     assert x.dtype == torch.bfloat16 and x.is_cuda and x.is_contiguous()
     if out is None:
-        out = torch.empty(1, dtype=torch.float32, device=x.device)
+        out = _empty(1, torch.float32, x.device, stream)
     check(lib().nvfp4_amax_bf16(_ptr(x), x.numel(), _ptr(out), _stream(stream)))
     return out
 
@@ -155,12 +164,12 @@ def quantize(x, global_scale: float | None = None, packed=None, sf=None, stream=
     assert x.dtype == torch.bfloat16 and x.is_cuda and x.is_contiguous() and x.dim() == 2
     rows, cols = x.shape
     if packed is None:
-        packed = torch.empty((rows, cols // 2), dtype=torch.uint8, device=x.device)
+        packed = _empty((rows, cols // 2), torch.uint8, x.device, stream)
     if sf is None:
-        sf = torch.empty(sf_bytes(rows, cols), dtype=torch.uint8, device=x.device)
+        sf = _empty(sf_bytes(rows, cols), torch.uint8, x.device, stream)
     if global_scale is None:
-        gs = torch.empty(1, dtype=torch.float32, device=x.device)
-        ws = torch.empty(int(lib().nvfp4_quantize_workspace_bytes()), dtype=torch.uint8, device=x.device)
+        gs = _empty(1, torch.float32, x.device, stream)
+        ws = _empty(int(lib().nvfp4_quantize_workspace_bytes()), torch.uint8, x.device, stream)
         check(lib().nvfp4_quantize_bf16_auto(_ptr(x), rows, cols, _ptr(packed), _ptr(sf), _ptr(gs),
                                              _ptr(ws), _stream(stream)))
         return packed, sf, gs
@@ -172,7 +181,7 @@ def quantize(x, global_scale: float | None = None, packed=None, sf=None, stream=
 def dequantize(packed, sf, rows: int, cols: int, global_scale: float, out=None, stream=None):
     import torch
     if out is None:
-        out = torch.empty((rows, cols), dtype=torch.bfloat16, device=packed.device)
+        out = _empty((rows, cols), torch.bfloat16, packed.device, stream)
     check(lib().nvfp4_dequantize_bf16(_ptr(packed), _ptr(sf), rows, cols, ctypes.c_float(global_scale),
                                       _ptr(out), _stream(stream)))
     return out
@@ -189,7 +198,7 @@ def gemm(a_packed, sfa, b_packed, sfb, M: int, N: int, K: int, alpha: float = 1.
     before its dependency wait)."""
     import torch
     if out is None:
-        out = torch.empty((M, N), dtype=torch.bfloat16, device=a_packed.device)
+        out = _empty((M, N), torch.bfloat16, a_packed.device, stream)
     if weights_const:
         check(lib().nvfp4_gemm_bf16_flags(_ptr(a_packed), _ptr(sfa), _ptr(b_packed), _ptr(sfb), ctypes.c_float(alpha),
                                           _ptr(out), M, N, K, NVFP4_GEMM_WEIGHTS_CONST, _stream(stream)))
@@ -205,9 +214,9 @@ def gemm_quantize(a_packed, sfa, b_packed, sfb, M: int, N: int, K: int, alpha: f
     epilogue: (packed [M, N/2] uint8, scales in the tcgen05 layout)."""
     import torch
     if packed is None:
-        packed = torch.empty((M, N // 2), dtype=torch.uint8, device=a_packed.device)
+        packed = _empty((M, N // 2), torch.uint8, a_packed.device, stream)
     if sf is None:
-        sf = torch.empty(sf_bytes(M, N), dtype=torch.uint8, device=a_packed.device)
+        sf = _empty(sf_bytes(M, N), torch.uint8, a_packed.device, stream)
     check(lib().nvfp4_gemm_quantize(_ptr(a_packed), _ptr(sfa), _ptr(b_packed), _ptr(sfb), ctypes.c_float(alpha),
                                     ctypes.c_float(global_scale), _ptr(packed), _ptr(sf), M, N, K, _stream(stream)))
     return packed, sf
@@ -217,44 +226,7 @@ def gemm_f32(a_packed, sfa, b_packed, sfb, M: int, N: int, K: int, out=None, str
     """Raw fp32 accumulators of the same kernel (tile checks)."""
     import torch
     if out is None:
-        out = torch.empty((M, N), dtype=torch.float32, device=a_packed.device)
+        out = _empty((M, N), torch.float32, a_packed.device, stream)
     check(lib().nvfp4_gemm_f32(_ptr(a_packed), _ptr(sfa), _ptr(b_packed), _ptr(sfb), _ptr(out), M, N, K,
                                _stream(stream)))
     return out
-
-
-# ------------------------------------------------------------- diagnostics ----
-def diag_e2m1_encode(x, stream=None):
-    import torch
-    out = torch.empty(x.numel(), dtype=torch.uint8, device=x.device)
-    check(lib().nvfp4_diag_e2m1_encode(_ptr(x), _ptr(out), x.numel(), _stream(stream)))
-    return out
-
-
-def diag_e4m3_encode(x, stream=None):
-    import torch
-    out = torch.empty(x.numel(), dtype=torch.uint8, device=x.device)
-    check(lib().nvfp4_diag_e4m3_encode(_ptr(x), _ptr(out), x.numel(), _stream(stream)))
-    return out
-
-
-def diag_mma_peak(cta_group: int = 2, iters: int = 4096, repeats: int = 3, random_operands: bool = True,
-                  stream=None) -> float:
-    """Measured FP4 block-scaled MMA rate in TFLOP/s (best of `repeats` launches)."""
-    import torch
-    s = stream if stream is not None else torch.cuda.current_stream()
-    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-    if cta_group == 2:
-        sms = 2 * (sms // 2)
-    flops = 2.0 * 128 * 256 * 64 * iters * sms
-    ro = 1 if random_operands else 0
-    check(lib().nvfp4_diag_mma_peak(cta_group, iters, ro, _stream(s)))     # warm-up
-    best = 0.0
-    for _ in range(repeats):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(s)
-        check(lib().nvfp4_diag_mma_peak(cta_group, iters, ro, _stream(s)))
-        b.record(s)
-        b.synchronize()
-        best = max(best, flops / (a.elapsed_time(b) * 1e-3) / 1e12)
-    return best

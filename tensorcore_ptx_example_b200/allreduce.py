@@ -20,7 +20,7 @@ from __future__ import annotations
 
 import ctypes
 
-from . import _ptr, _stream, check, lib
+from . import _empty, _ptr, _stream, check, lib
 
 AUTO, ONESHOT, TWOSHOT, LOWLAT = 0, 1, 2, 3
 LOWLAT_CAP_BYTES = 1 << 20          # NVFP4_AR_LOWLAT_CAP_BYTES: largest low-latency call (bf16 bytes)
@@ -116,7 +116,7 @@ class AllReduce:
             raise ValueError("global_scale is required (the same on every rank)")
         assert x.dtype == torch.bfloat16 and x.is_cuda and x.is_contiguous()
         if out is None:
-            out = torch.empty_like(x)
+            out = _empty(x.shape, x.dtype, x.device, stream)
         check(lib().nvfp4_ar_allreduce(self.handle, _ptr(x), _ptr(out), x.numel(), ctypes.c_float(global_scale),
                                        _algo(algo), _stream(stream)))
         return out
@@ -129,7 +129,7 @@ class AllReduce:
         allreduce(algo="twoshot").  global_scale: the same on every rank."""
         import torch
         if out is None:
-            out = torch.empty((M, N), dtype=torch.bfloat16, device=a_packed.device)
+            out = _empty((M, N), torch.bfloat16, a_packed.device, stream)
         check(lib().nvfp4_gemm_allreduce(self.handle, _ptr(a_packed), _ptr(sfa), _ptr(b_packed), _ptr(sfb),
                                          ctypes.c_float(alpha), ctypes.c_float(global_scale), _ptr(out), M, N, K,
                                          _stream(stream)))
@@ -140,7 +140,7 @@ class AllReduce:
         import torch
         assert x.dtype == torch.bfloat16 and x.is_cuda and x.is_contiguous()
         if out is None:
-            out = torch.empty_like(x)
+            out = _empty(x.shape, x.dtype, x.device, stream)
         check(lib().nvfp4_ar_bf16_allreduce(self.handle, _ptr(x), _ptr(out), x.numel(), _algo(algo),
                                             _stream(stream)))
         return out
@@ -204,7 +204,7 @@ def emulated_allreduce(inputs, global_scale: float = 1.0, algo="auto", bf16: boo
         contexts = [AllReduce(world, r, numel) for r in range(world)]
         join_in_process(contexts)
     try:
-        outs = [torch.empty_like(x) for x in inputs]
+        outs = [_empty(x.shape, x.dtype, x.device, stream) for x in inputs]
         hs = (ctypes.c_void_p * world)(*[c.handle for c in contexts])
         ins = (ctypes.c_void_p * world)(*[ctypes.c_void_p(x.data_ptr()) for x in inputs])
         os_ = (ctypes.c_void_p * world)(*[ctypes.c_void_p(o.data_ptr()) for o in outs])
@@ -223,7 +223,7 @@ def emulated_gemm_allreduce(operands, M: int, N: int, K: int, alphas, global_sca
     (a_packed, sfa, b_packed, sfb) of rank r.  Returns the per-rank outputs."""
     import torch
     world = len(operands)
-    outs = [torch.empty((M, N), dtype=torch.bfloat16, device="cuda") for _ in range(world)]
+    outs = [_empty((M, N), torch.bfloat16, operands[0][0].device, stream) for _ in range(world)]
 
     def arr(i):
         return (ctypes.c_void_p * world)(*[ctypes.c_void_p(op[i].data_ptr()) for op in operands])

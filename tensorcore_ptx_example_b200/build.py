@@ -2,10 +2,11 @@
 
     python -m tensorcore_ptx_example_b200.build
 
-compiles csrc/nvfp4_lib.cu (the whole library, one translation unit) into
-tensorcore_ptx_example_b200/libnvfp4_b200.so with
-``nvcc -gencode arch=compute_100a,code=sm_100a -lineinfo -O3``.  nvcc cross-compiles, so this
-works on a machine without a GPU; the .so then travels with the source tree.
+compiles csrc/nvfp4_lib.cu (the whole product library, one translation unit) into
+tensorcore_ptx_example_b200/libnvfp4_b200.so and csrc/diag_lib.cu (hardware probes and the MMA
+issue-rate microbenchmark, off the data path) into tensorcore_ptx_example_b200/libnvfp4_diag.so,
+both with ``nvcc -gencode arch=compute_100a,code=sm_100a -lineinfo -O3``.  nvcc cross-compiles, so
+this works on a machine without a GPU; the .so files then travel with the source tree.
 """
 from __future__ import annotations
 
@@ -17,13 +18,15 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libnvfp4_b200.so")
+DIAG_LIB = os.path.join(PKG, "libnvfp4_diag.so")
 NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
 def _sources():
     return [os.path.join(CSRC, f) for f in sorted(os.listdir(CSRC))
-            if f.endswith((".cu", ".cuh", ".h"))] + [os.path.join(ROOT, "include", "nvfp4.h")]
+            if f.endswith((".cu", ".cuh", ".h"))] + [os.path.join(ROOT, "include", h)
+                                                      for h in ("nvfp4.h", "nvfp4_diag.h")]
 
 
 def _stale(target: str, deps) -> bool:
@@ -33,16 +36,23 @@ def _stale(target: str, deps) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build_library(force: bool = False, verbose: bool = False) -> str:
-    if not force and not _stale(LIB, _sources()):
-        return LIB
+def _nvcc_shared(out: str, tu: str, verbose: bool) -> None:
     cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
            "-Xcompiler", "-fvisibility=hidden", "-I", os.path.join(ROOT, "include"),
-           "-o", LIB + ".tmp", os.path.join(CSRC, "nvfp4_lib.cu")]
+           "-o", out + ".tmp", os.path.join(CSRC, tu)]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)
-    os.replace(LIB + ".tmp", LIB)
+    os.replace(out + ".tmp", out)
+
+
+def build_library(force: bool = False, verbose: bool = False) -> str:
+    """Both libraries; returns the product library's path."""
+    srcs = _sources()
+    if force or _stale(LIB, srcs):
+        _nvcc_shared(LIB, "nvfp4_lib.cu", verbose)
+    if force or _stale(DIAG_LIB, srcs):
+        _nvcc_shared(DIAG_LIB, "diag_lib.cu", verbose)
     return LIB
 
 

@@ -760,6 +760,17 @@ int nvfp4_ar_choose_algo(int world, int64_t numel) {
     return numel * 2 <= NVFP4_AR_ONESHOT_MAX_BYTES ? NVFP4_AR_ONESHOT : NVFP4_AR_TWOSHOT;
 }
 
+// The algorithm a call runs.  AUTO resolves by size (nvfp4_ar_choose_algo).  The low-latency
+// one-shot exists only for NVFP4 payloads within the context's low-latency area, so a LOWLAT that
+// AUTO picked for a bf16 payload or a larger call runs as ONESHOT; an explicit NVFP4_AR_LOWLAT
+// outside those limits never gets here (check_call rejects it).  Every entry point resolves
+// through this one rule.
+static int resolve_algo(nvfp4_ar_t h, int algo, int64_t numel, bool nvfp4_payload) {
+    if (algo == NVFP4_AR_AUTO) algo = nvfp4_ar_choose_algo(h->world, numel);
+    if (algo == NVFP4_AR_LOWLAT && (!nvfp4_payload || numel > h->ll_numel)) algo = NVFP4_AR_ONESHOT;
+    return algo;
+}
+
 static Params make_params(nvfp4_ar_t h, const void* in, void* out, int64_t numel, float gs, int phase) {
     Params p = {};
     for (int r = 0; r < h->world; r++) p.comm[r] = h->peer[r];
@@ -808,8 +819,7 @@ nvfp4_status_t nvfp4_ar_allreduce(nvfp4_ar_t h, const void* in, void* out, int64
     if (st || numel == 0) return st;
     if (!(global_scale > 0.0f) || !isfinite(global_scale))
         return fail(NVFP4_ERR_INVALID_ARG, "ar_allreduce: global_scale must be finite and > 0");
-    if (algo == NVFP4_AR_AUTO) algo = nvfp4_ar_choose_algo(h->world, numel);
-    if (algo == NVFP4_AR_LOWLAT && numel > h->ll_numel) algo = NVFP4_AR_ONESHOT;
+    algo = resolve_algo(h, algo, numel, true);
     h->epoch++;
     const Params p = make_params(h, in, out, numel, global_scale, -1);
     if (algo == NVFP4_AR_LOWLAT) return launch_nvfp4_ll(h, p, (cudaStream_t)stream);
@@ -821,8 +831,7 @@ nvfp4_status_t nvfp4_ar_bf16_allreduce(nvfp4_ar_t h, const void* in, void* out, 
     clear_error();
     nvfp4_status_t st = check_call(h, "ar_bf16_allreduce", in, out, numel, algo, 8);
     if (st || numel == 0) return st;
-    if (algo == NVFP4_AR_AUTO) algo = nvfp4_ar_choose_algo(h->world, numel);
-    if (algo == NVFP4_AR_LOWLAT) algo = NVFP4_AR_ONESHOT;
+    algo = resolve_algo(h, algo, numel, false);
     h->epoch++;
     return launch_bf16(h, make_params(h, in, out, numel, 0.0f, -1), algo == NVFP4_AR_TWOSHOT, (cudaStream_t)stream);
 }
@@ -928,8 +937,7 @@ nvfp4_status_t nvfp4_ar_allreduce_emulated(nvfp4_ar_t const* handles, int world,
     if (numel == 0) return NVFP4_OK;
     if (!bf16_payload && (!(global_scale > 0.0f) || !isfinite(global_scale)))
         return fail(NVFP4_ERR_INVALID_ARG, "ar_allreduce_emulated: global_scale must be finite and > 0");
-    if (algo == NVFP4_AR_AUTO) algo = nvfp4_ar_choose_algo(world, numel);
-    if (algo == NVFP4_AR_LOWLAT && (bf16_payload || numel > handles[0]->ll_numel)) algo = NVFP4_AR_ONESHOT;
+    algo = resolve_algo(handles[0], algo, numel, !bf16_payload);
     const bool two = algo == NVFP4_AR_TWOSHOT;
     for (int r = 0; r < world; r++) handles[r]->epoch++;
     if (algo == NVFP4_AR_LOWLAT) {

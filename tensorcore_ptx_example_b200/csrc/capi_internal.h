@@ -12,6 +12,8 @@ namespace nvfp4 {
 nvfp4_status_t fail(nvfp4_status_t code, const char* fmt, ...);
 // Clears the calling thread's last error.
 void clear_error();
+// The calling thread's last error message ("" if none).
+const char* last_error();
 // Maps the last CUDA launch error (if any) to NVFP4_ERR_CUDA with a message.
 nvfp4_status_t check_launch(const char* what);
 // Number of SMs of the current device (cached per device).

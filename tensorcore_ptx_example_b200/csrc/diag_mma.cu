@@ -1,4 +1,5 @@
 // diag_mma.cu -- FP4 tensor-core issue-rate microbenchmark (the measured roofline of the GEMM).
+// Part of the diagnostics library (diag_lib.cu -> libnvfp4_diag.so), not of the product library.
 //
 // Every CTA (or CTA pair) issues `iters` block-scaled MMAs back to back on operands that stay
 // in shared memory and TMEM (no global traffic), committing every 32 MMAs and keeping at most
@@ -7,6 +8,7 @@
 // the run sees.
 #include "capi_internal.h"
 #include "nvfp4_common.cuh"
+#include "nvfp4_diag.h"
 
 namespace nvfp4 {
 namespace diag {

@@ -184,18 +184,6 @@ __device__ __forceinline__ void spin_ns(uint64_t ns) {
     }
 }
 
-#ifdef GEMM2_PROF
-__device__ unsigned long long g_gemm2_prof[296][16];
-#define PROF_WAIT(slot, expr)                                               \
-    ([&]() {                                                                \
-        const unsigned long long _t0 = clock64();                          \
-        const bool _r = (expr);                                             \
-        if ((slot) != 7) atomicAdd(&g_gemm2_prof[blockIdx.x][slot], clock64() - _t0); \
-        return _r;                                                          \
-    }())
-#else
-#define PROF_WAIT(slot, expr) (expr)
-#endif
 
 // Output of the epilogue:
 //   OUT_BF16 / OUT_F32  D through shared-memory staging and TMA stores;
@@ -299,7 +287,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                 const int a_row = tm * 256 + (int)rank * BM;
                 const int b_row = tn * BN + (int)rank * (BN / 2);
                 for (int kb = 0; kb < nkb; kb++) {
-                    if (!PROF_WAIT(5, mbar_wait(empty_bar(stage), phase ^ 1u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_PRODUCER))) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_PRODUCER)) {
                         ok = false;
                         break;
                     }
@@ -336,8 +324,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
             int sf_slot = 0;
             for (int tile = pair; tile < ntiles && ok; tile += npairs, iter++) {
                 if (iter > 0 &&
-                    !PROF_WAIT(2, mbar_wait_spin(tmem_empty, (uint32_t)((iter - 1) & 1), WAIT_LIMIT_NS,
-                                                 DEV_TIMEOUT_GEMM_MMA))) {
+                    !mbar_wait_spin(tmem_empty, (uint32_t)((iter - 1) & 1), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA)) {
                     ok = false;
                     break;
                 }
@@ -346,7 +333,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                 for (int kb = 0; kb < nkb; kb++) {
                     // A/B of the stage have landed and its scales are in TMEM.  One wait per
                     // stage: each wait in this thread costs tensor-pipe time.
-                    if (!PROF_WAIT(0, mbar_wait_spin(full_bar(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA))) {
+                    if (!mbar_wait_spin(full_bar(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA)) {
                         ok = false;
                         break;
                     }
@@ -434,12 +421,10 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                 bool w = true;
                 if (g >= SF_SLOTS) {
                     const long p = g - SF_SLOTS;
-                    w = PROF_WAIT((warp == 6 && lane == 0) ? 4 : 7,
-                                  mbar_wait(empty_bar((int)(p % STAGES)), (uint32_t)((p / STAGES) & 1),
-                                            WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_SF));
+                    w = mbar_wait(empty_bar((int)(p % STAGES)), (uint32_t)((p / STAGES) & 1), WAIT_LIMIT_NS,
+                                  DEV_TIMEOUT_GEMM_SF);
                 }
-                w = w && PROF_WAIT((warp == 6 && lane == 0) ? 3 : 7,
-                                   mbar_wait(sf_landed(sm), smph, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_SF));
+                w = w && mbar_wait(sf_landed(sm), smph, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_SF);
                 if (!__all_sync(0xFFFFFFFFu, w)) {
                     ok = false;
                     break;
@@ -491,9 +476,8 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
         for (int tile = pair; tile < ntiles; tile += npairs, iter++) {
             const int tm = tile % num_m, tn = tile / num_m;
             // The four epilogue warps give up together (they meet at named barriers below).
-            const bool ok = __all_sync(0xFFFFFFFFu, PROF_WAIT((warp == 2 && lane == 0) ? 6 : 7,
-                                                              mbar_wait(tmem_full, (uint32_t)(iter & 1), WAIT_LIMIT_NS,
-                                                                        DEV_TIMEOUT_GEMM_EPILOGUE)));
+            const bool ok = __all_sync(
+                0xFFFFFFFFu, mbar_wait(tmem_full, (uint32_t)(iter & 1), WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_EPILOGUE));
             if (!ok && lane == 0) *abort_flag = 1u;
             epi_bar_set(eset);
             if (*abort_flag) break;
@@ -658,14 +642,3 @@ nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void*
 
 }  // namespace gemm2
 }  // namespace nvfp4
-
-#ifdef GEMM2_PROF
-extern "C" NVFP4_API int nvfp4_diag_gemm2_prof(unsigned long long* out, int clear) {
-    cudaMemcpyFromSymbol(out, nvfp4::gemm2::g_gemm2_prof, sizeof(unsigned long long) * 296 * 16);
-    if (clear) {
-        static unsigned long long zero[296 * 16] = {};
-        cudaMemcpyToSymbol(nvfp4::gemm2::g_gemm2_prof, zero, sizeof(zero));
-    }
-    return (int)cudaGetLastError();
-}
-#endif

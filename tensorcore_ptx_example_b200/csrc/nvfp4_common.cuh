@@ -36,6 +36,7 @@ enum DeviceError : unsigned int {
     DEV_TIMEOUT_GEMM_SF = 0x106,
     DEV_TMEM_BASE = 0x105,
     DEV_TIMEOUT_QUANT = 0x301,
+    DEV_NONFINITE_INPUT = 0x302,      // a quantized block or an amax input held NaN or Inf
     DEV_TIMEOUT_AR_BARRIER = 0x201,
 };
 
@@ -135,11 +136,28 @@ __device__ __forceinline__ void mul2_rn(float a, float b, float s, float& ya, fl
         : "f"(a), "f"(b), "f"(s));
 }
 
-// Quantize 16 floats: writes two 32-bit nibble words, returns the scale byte.
+// Scale byte of a block that holds a NaN or an Inf: the E4M3 NaN encoding, so the whole block
+// dequantizes to NaN (NVFP4 has no encoding for non-finite values); its codes are 0.
+constexpr uint32_t NONFINITE_SCALE = 0x7Fu;
+
+// Quantize 16 floats: writes two 32-bit nibble words, returns the scale byte.  A block with a
+// non-finite value gets NONFINITE_SCALE and zero codes, and records DEV_NONFINITE_INPUT.
 __device__ __forceinline__ uint32_t q16(const float* v, float gs_inv, uint32_t& w0, uint32_t& w1) {
-    float amax = 0.0f;
+    // block amax with three-input max.NaN.abs: NaN propagates, so one compare finds NaN or Inf
+    float m[6];
 #pragma unroll
-    for (int i = 0; i < 16; i++) amax = fmaxf(amax, fabsf(v[i]));
+    for (int i = 0; i < 5; i++) asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m[i]) : "f"(v[3 * i]), "f"(v[3 * i + 1]), "f"(v[3 * i + 2]));
+    m[5] = fabsf(v[15]);
+    float amax, a2;
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(amax) : "f"(m[0]), "f"(m[1]), "f"(m[2]));
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(a2) : "f"(m[3]), "f"(m[4]), "f"(m[5]));
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(amax) : "f"(amax), "f"(a2));
+    if (!(amax <= 3.402823466e38f)) {
+        record_error(DEV_NONFINITE_INPUT);
+        w0 = 0u;
+        w1 = 0u;
+        return NONFINITE_SCALE;
+    }
     float inv;
     const uint32_t code = block_scale(amax, gs_inv, inv);
     float y[16];
@@ -152,15 +170,23 @@ __device__ __forceinline__ uint32_t q16(const float* v, float gs_inv, uint32_t& 
 }
 
 // The same for 16 bf16 values packed two per word (element 2i in the low half of word i).
-// The amax: max.xorsign.abs.bf16x2 keeps per lane the larger magnitude of two bf16 pairs (its
-// sign is the xor of the signs, cleared afterwards), one instruction per word; for finite
-// values that is exactly max |x| of each half.
+// The amax: max.NaN.xorsign.abs.bf16x2 keeps per lane the larger magnitude of two bf16 pairs
+// (its sign is the xor of the signs, cleared afterwards) and propagates NaN, one instruction per
+// word; for finite values that is exactly max |x| of each half, and a NaN or Inf anywhere in the
+// block leaves a magnitude of at least 0x7F80 (the non-finite path above).
 __device__ __forceinline__ uint32_t q16_bf16(const uint32_t* w, float gs_inv, uint32_t& w0, uint32_t& w1) {
     uint32_t m = w[0];
 #pragma unroll
-    for (int i = 1; i < 8; i++) asm("max.xorsign.abs.bf16x2 %0, %0, %1;" : "+r"(m) : "r"(w[i]));
+    for (int i = 1; i < 8; i++) asm("max.NaN.xorsign.abs.bf16x2 %0, %0, %1;" : "+r"(m) : "r"(w[i]));
     m &= 0x7FFF7FFFu;
-    const float amax = __uint_as_float(((m >> 16) > (m & 0xFFFFu) ? (m >> 16) : (m & 0xFFFFu)) << 16);
+    const uint32_t abits = (m >> 16) > (m & 0xFFFFu) ? (m >> 16) : (m & 0xFFFFu);
+    if (abits >= 0x7F80u) {
+        record_error(DEV_NONFINITE_INPUT);
+        w0 = 0u;
+        w1 = 0u;
+        return NONFINITE_SCALE;
+    }
+    const float amax = __uint_as_float(abits << 16);
     float inv;
     const uint32_t code = block_scale(amax, gs_inv, inv);
     float y[16];

@@ -150,30 +150,93 @@ dequantize_kernel(const uint8_t* __restrict__ packed, const uint32_t* __restrict
     }
 }
 
-// max |x| of bf16 data, accumulated with atomicMax on the float bit pattern (non-negative
+// max |x| over the finite bf16 values, accumulated with atomicMax on the bit pattern (non-negative
 // floats order like their bit patterns).  *out must be zero before the launch.
-__global__ void __launch_bounds__(256)
-amax_kernel(const uint4* __restrict__ x, int64_t nvec, uint32_t* __restrict__ out) {
+//   HBM-bound: 2 bytes per element read once.  At B200 bandwidth an SM must retire ~5.6 32-bit
+//   words per cycle, so the loop spends one instruction per word: max.NaN.xorsign.abs.bf16x2
+//   folds a word into the running pair-maximum (magnitudes; NaN propagates), with 32-byte loads
+//   (AMAX_UNROLL of them in flight per thread before any arithmetic).
+//   Non-finite values: a NaN or Inf leaves a magnitude >= 0x7F80 in the running maximum; only
+//   then does the thread walk its elements again, skipping NaN and Inf, and record
+//   DEV_NONFINITE_INPUT, so the result is the amax of the finite values.
+constexpr int AMAX_THREADS = 256;
+constexpr int AMAX_UNROLL = 4;
+
+__device__ __forceinline__ uint32_t amax_fold(uint32_t m, uint32_t w) {
+    asm("max.NaN.xorsign.abs.bf16x2 %0, %0, %1;" : "+r"(m) : "r"(w));
+    return m;
+}
+// larger of the two magnitudes of a pair, skipping NaN and Inf (>= 0x7F80)
+__device__ __forceinline__ uint32_t finite_max2(uint32_t m, uint32_t w) {
+    const uint32_t lo = w & 0x7FFFu, hi = (w >> 16) & 0x7FFFu;
+    if (lo < 0x7F80u && lo > m) m = lo;
+    if (hi < 0x7F80u && hi > m) m = hi;
+    return m;
+}
+
+template <bool kLoad32>
+__global__ void __launch_bounds__(AMAX_THREADS)
+amax_kernel(const uint8_t* __restrict__ x, int64_t numel, uint32_t* __restrict__ out) {
+    constexpr int VB = kLoad32 ? 32 : 16;                  // bytes per load
+    constexpr int VW = VB / 4;                             // words per load
+    const int64_t nvec = numel * 2 / VB;
+    const int64_t stride = (int64_t)gridDim.x * AMAX_THREADS;
+    const int64_t first = (int64_t)blockIdx.x * AMAX_THREADS + threadIdx.x;
     uint32_t m = 0;
 #pragma unroll 1
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const uint4 v = ld_nc_v4(x + i);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    for (int64_t i = first; i < nvec; i += stride * AMAX_UNROLL) {
+        uint32_t r[AMAX_UNROLL][VW];
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            m = max(m, w[j] & 0x7FFFu);
-            m = max(m, (w[j] >> 16) & 0x7FFFu);
+        for (int u = 0; u < AMAX_UNROLL; u++) {
+            const int64_t v = i + u * stride;
+            if (v < nvec) {
+                if constexpr (kLoad32) {
+                    ld_nc_v8(x + v * VB, r[u]);
+                } else {
+                    const uint4 q = ld_nc_v4(x + v * VB);
+                    r[u][0] = q.x; r[u][1] = q.y; r[u][2] = q.z; r[u][3] = q.w;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < VW; j++) r[u][j] = 0u;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < AMAX_UNROLL; u++)
+#pragma unroll
+            for (int j = 0; j < VW; j++) m = amax_fold(m, r[u][j]);
+    }
+    // a tail of 8 elements when numel is not a multiple of VB / 2
+    const int64_t tail = nvec * VB;
+    if (first == 0 && tail < numel * 2) {
+        const uint4 q = ld_nc_v4(x + tail);
+        m = amax_fold(amax_fold(amax_fold(amax_fold(m, q.x), q.y), q.z), q.w);
+    }
+    m &= 0x7FFF7FFFu;
+    uint32_t a = max(m & 0xFFFFu, m >> 16);
+    if (a >= 0x7F80u) {
+        // rare path: this thread saw a NaN or Inf; walk its elements again without them
+        record_error(DEV_NONFINITE_INPUT);
+        a = 0;
+#pragma unroll 1
+        for (int64_t v = first; v < nvec; v += stride) {
+            const uint32_t* p = reinterpret_cast<const uint32_t*>(x + v * VB);
+#pragma unroll
+            for (int j = 0; j < VW; j++) a = finite_max2(a, p[j]);
+        }
+        if (first == 0 && tail < numel * 2) {
+            const uint32_t* p = reinterpret_cast<const uint32_t*>(x + tail);
+            for (int j = 0; j < 4; j++) a = finite_max2(a, p[j]);
         }
     }
-    m = __reduce_max_sync(0xFFFFFFFFu, m);
-    __shared__ uint32_t warp_max[8];
-    if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+    a = __reduce_max_sync(0xFFFFFFFFu, a);
+    __shared__ uint32_t warp_max[AMAX_THREADS / 32];
+    if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = a;
     __syncthreads();
     if (threadIdx.x < 32) {
-        m = threadIdx.x < (blockDim.x >> 5) ? warp_max[threadIdx.x] : 0u;
-        m = __reduce_max_sync(0xFFFFFFFFu, m);
-        if (threadIdx.x == 0 && m != 0) atomicMax(out, m << 16);
+        a = threadIdx.x < AMAX_THREADS / 32 ? warp_max[threadIdx.x] : 0u;
+        a = __reduce_max_sync(0xFFFFFFFFu, a);
+        if (threadIdx.x == 0 && a != 0) atomicMax(out, a << 16);
     }
 }
 
@@ -187,11 +250,14 @@ template <bool kDevScale>
 static nvfp4_status_t launch_quantize(const void* x, int64_t rows, int64_t cols, float gs, const uint32_t* amax_word,
                                       float* gs_out, void* packed, void* sf, cudaStream_t s) {
     const int64_t nblocks = rows * cols / 16;
-    if (nblocks == 0) return NVFP4_OK;
+    // an empty tensor still gets its global scale written on the auto-scaled path (gs 1 from
+    // amax 0): one block runs, with no element to quantize
+    if (nblocks == 0 && !kDevScale) return NVFP4_OK;
     const int64_t per_cta = (int64_t)QR_THREADS * QR_UNROLL;
     const int64_t cap = (int64_t)sm_count() * QUANT_CTAS_PER_SM;
     int64_t grid = (nblocks + per_cta - 1) / per_cta;
     if (grid > cap) grid = cap;
+    if (grid < 1) grid = 1;
     // 32-byte loads when the input allows them (16-byte alignment is the API's minimum)
     if ((reinterpret_cast<uintptr_t>(x) & 31) == 0)
         quantize_kernel<kDevScale, true><<<(unsigned)grid, QR_THREADS, 0, s>>>(
@@ -210,12 +276,17 @@ static nvfp4_status_t launch_quantize(const void* x, int64_t rows, int64_t cols,
 static nvfp4_status_t launch_amax(const void* x, int64_t numel, uint32_t* word, cudaStream_t s) {
     cudaError_t e = cudaMemsetAsync(word, 0, sizeof(uint32_t), s);
     if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "amax memset: %s", cudaGetErrorString(e));
-    const int64_t nvec = numel / 8;
-    if (nvec == 0) return NVFP4_OK;
-    int64_t grid = (nvec + 255) / 256;
+    if (numel == 0) return NVFP4_OK;
+    const bool load32 = (reinterpret_cast<uintptr_t>(x) & 31) == 0;
+    const int64_t per_cta = (int64_t)AMAX_THREADS * AMAX_UNROLL * (load32 ? 16 : 8);   // elements
+    int64_t grid = (numel + per_cta - 1) / per_cta;
     const int64_t cap = (int64_t)sm_count() * 8;
     if (grid > cap) grid = cap;
-    amax_kernel<<<(unsigned)grid, 256, 0, s>>>(reinterpret_cast<const uint4*>(x), nvec, word);
+    if (grid < 1) grid = 1;
+    if (load32)
+        amax_kernel<true><<<(unsigned)grid, AMAX_THREADS, 0, s>>>(reinterpret_cast<const uint8_t*>(x), numel, word);
+    else
+        amax_kernel<false><<<(unsigned)grid, AMAX_THREADS, 0, s>>>(reinterpret_cast<const uint8_t*>(x), numel, word);
     return check_launch("amax_kernel");
 }
 

@@ -14,8 +14,10 @@
 //     build whose workspace requirement exceeded the array would be rejected with
 //     NVFP4_ERR_UNSUPPORTED.
 //   - set-up: the first call on a device looks up the device address of the array with
-//     cudaGetSymbolAddress while that device is current, and caches it.  Make that first call
-//     before any stream capture.
+//     cudaGetSymbolAddress while that device is current, and caches it for the life of the
+//     process.  Make that first call before any stream capture.  Do not use the entry point on
+//     a device after cudaDeviceReset: the reset reloads the module and the cached address
+//     would be stale.
 //   - no cudaMalloc, cudaFree or allocating library routine is called; the amax word is
 //     cleared with cudaMemsetAsync on `stream` before every use.
 //   - every call on a device shares the one array: calls that overlap on the GPU (different

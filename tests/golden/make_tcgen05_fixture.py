@@ -2,14 +2,20 @@
 
     python tests/golden/make_tcgen05_fixture.py [out.npz]
 
-Runs the production GEMM kernel (nvfp4_gemm_f32) on experiments that expose the arithmetic of
-tcgen05.mma kind::mxf4nvf4.block_scale.scale_vec::4X and stores the raw fp32 outputs:
+Runs the stand-alone single-tile probe of the diagnostics library (nvfp4_diag_mma_tile: one CTA,
+operands in the no-swizzle core-matrix layout loaded with plain loads, scales placed with
+tcgen05.cp, four K64 MMAs, tcgen05.ld read-back) -- not the production GEMM, whose parity the
+fixture is used to check -- on experiments that expose the arithmetic of tcgen05.mma
+kind::mxf4nvf4.block_scale.scale_vec::4X, and stores the raw fp32 outputs:
   cfg1_<seed>      cfg1 tiles (M128 N256 K256, all 16 E2M1 codes, scales 2^[-4,4])
   P1..P4           one K step: +big, -big and a small term in varying block positions
                    (exactness of the in-step sum over >= 38 bits)
   P5..P8           one K step: big +- small (rounding direction of the step result)
   X1..X4           big and small in two different K steps (width of the accumulate step)
-The oracle model ORC_ACC_TCGEN05 must reproduce every value (tests/test_oracle_pins.py).
+The oracle model ORC_ACC_TCGEN05 must reproduce every value (tests/test_oracle_pins.py); the
+production GEMM is then checked against that model (tests/test_gemm_gpu.py).  As a consistency
+check the script also runs the production kernel on every experiment and reports whether it
+agrees with the probe (the fixture holds the probe's outputs either way).
 """
 import os
 import sys
@@ -21,18 +27,26 @@ ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)
 sys.path[:0] = [ROOT, os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests")]
 import py_oracle as po  # noqa: E402
 import tensorcore_ptx_example_b200 as nv  # noqa: E402
+from tensorcore_ptx_example_b200 import diag  # noqa: E402
 from test_gemm_gpu import cfg1_tile  # noqa: E402  (same generator as the GPU tests)
 
 OUT_PATH = sys.argv[1] if len(sys.argv) > 1 else os.path.join(ROOT, "tests", "golden", "tcgen05_b200_outputs.npz")
 
 
 
+PRODUCTION_AGREES = []
+
+
 def run(pa, sa, pb, sb, M, N, K):
+    assert (M, N, K) == (128, 256, 256)
     t = [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (pa, sa, pb, sb)]
-    D = nv.gemm_f32(t[0], t[1], t[2], t[3], M, N, K)
+    D = diag.mma_tile(t[0], t[1], t[2], t[3])
+    P = nv.gemm_f32(t[0], t[1], t[2], t[3], M, N, K)
     torch.cuda.synchronize()
-    assert nv.device_status() == 0
-    return D.cpu().numpy()
+    assert diag.device_status() == 0 and nv.device_status() == 0
+    D = D.cpu().numpy()
+    PRODUCTION_AGREES.append(bool(np.array_equal(D, P.cpu().numpy())))
+    return D
 
 
 def pack(codes):
@@ -124,5 +138,7 @@ for name, (v0, v1) in {"X1": (6, 1), "X2": (6, 1.5), "X3": (-6, 1.5), "X4": (1, 
     res[f"{name}_pa"], res[f"{name}_sa"], res[f"{name}_sb"] = pa, sa, sb
     res[name] = run(pa, sa, pb, sb, M, N, K)
 res["pb_ones"] = pb
+res["source"] = np.array("nvfp4_diag_mma_tile (stand-alone single-CTA probe)")
 np.savez_compressed(OUT_PATH, **res)
-print("saved", len(res))
+print("saved", len(res), "arrays; production GEMM agrees with the probe on",
+      sum(PRODUCTION_AGREES), "of", len(PRODUCTION_AGREES), "experiments")

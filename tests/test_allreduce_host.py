@@ -141,3 +141,19 @@ def test_handle_exchange_and_scale_agreement_on_gloo_ranks():
         got, gs = res[r]
         assert got == [bytes([q]) * 64 for q in range(world)]
         assert gs == want_gs
+
+
+def test_oracle_nonfinite_blocks(oracle):
+    """Oracle side of the non-finite contract: a block with NaN or Inf gets scale 0x7F and zero
+    codes; amax skips non-finite values."""
+    x = np.zeros((1, 64), np.uint16)
+    x[0, :] = 0x3F80                       # 1.0
+    x[0, 3] = 0x7FC0                       # NaN in block 0
+    x[0, 40] = 0xFF80                      # -Inf in block 2
+    assert oracle.amax_bf16(x) == 1.0
+    packed, sf = oracle.quantize_bf16(x, 1.0 / 2688)
+    offs = oracle.sf_offsets(1, 64)[0]
+    assert sf[offs[0]] == 0x7F and sf[offs[2]] == 0x7F
+    assert sf[offs[1]] != 0x7F and sf[offs[3]] != 0x7F
+    assert np.all(packed[0, 0:8] == 0) and np.all(packed[0, 16:24] == 0)
+    assert np.any(packed[0, 8:16] != 0)

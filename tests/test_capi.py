@@ -10,14 +10,21 @@ import numpy as np
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def declared_functions():
+def declared_functions(macro="NVFP4_API"):
     names = []
     for hdr in os.listdir(os.path.join(ROOT, "include")):
         if not hdr.endswith(".h"):
             continue
         text = open(os.path.join(ROOT, "include", hdr)).read()
-        names += re.findall(r"^NVFP4_API [^(]*?\b(nvfp4_\w+)\(", text, flags=re.M)
+        names += re.findall(rf"^{macro} [^(]*?\b(nvfp4_\w+)\(", text, flags=re.M)
     return sorted(set(names))
+
+
+def exported(path):
+    """Dynamic symbols a shared library defines (nm -D --defined-only)."""
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", path], check=True, capture_output=True, text=True).stdout
+    return {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
 
 
 def test_library_exports_every_declared_symbol(nv):
@@ -26,8 +33,23 @@ def test_library_exports_every_declared_symbol(nv):
     L = nv.lib()
     for n in names:
         assert hasattr(L, n), n
-    # the Python mirror binds exactly the declared set
+    # the Python mirror binds exactly the declared set, and the library exports nothing else
     assert sorted(nv.SIGNATURES) == names
+    assert sorted(exported(nv.LIB_PATH)) == names
+
+
+def test_diag_library_exports_every_declared_symbol():
+    from tensorcore_ptx_example_b200 import diag
+    names = declared_functions("NVFP4_DIAG_API")
+    assert len(names) >= 6
+    L = diag.lib()
+    for n in names:
+        assert hasattr(L, n), n
+    assert sorted(diag.SIGNATURES) == names
+    assert sorted(exported(diag.DIAG_LIB_PATH)) == names
+    # the probes are not part of the product library
+    assert not any(n.startswith("nvfp4_diag") for n in exported(
+        __import__("tensorcore_ptx_example_b200").LIB_PATH))
 
 
 def test_abi_version(nv):
@@ -104,4 +126,6 @@ def test_zero_sized_calls_are_noops(nv):
     L = nv.lib()
     fake = ctypes.c_void_p(1 << 20)
     assert L.nvfp4_quantize_bf16(fake, 0, 64, ctypes.c_float(1.0), fake, fake, None) == 0
-    assert L.nvfp4_diag_e2m1_encode(fake, fake, 0, None) == 0
+    from tensorcore_ptx_example_b200 import diag
+    assert diag.lib().nvfp4_diag_e2m1_encode(fake, fake, 0, None) == 0
+    assert diag.lib().nvfp4_diag_rcp_approx(fake, fake, 0, None) == 0

@@ -58,6 +58,27 @@ def run_f32(nv, pa, sa, pb, sb, M, N, K):
     return D.cpu().numpy()
 
 
+def test_independent_tile_probe_matches_fixture_and_gemm(nv, oracle):
+    """The stand-alone tcgen05 tile probe (diagnostics library; plain loads, no-swizzle layout,
+    tcgen05.cp scales, one CTA) reproduces the committed B200 fixture on every experiment, and
+    the production GEMM gives the same bits on the same inputs."""
+    import os
+
+    from tensorcore_ptx_example_b200 import diag
+    d = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "tcgen05_b200_outputs.npz"))
+    M, N, K = 128, 256, 256
+    cases = [(f"cfg1_{s}", cfg1_tile(oracle, s)) for s in range(1, 5)]
+    cases += [(n, (d[n + "_pa"], d[n + "_sa"], d["pb_ones"], d[n + "_sb"]))
+              for n in ["P1", "P2", "P3", "P4", "P5", "P6", "P7", "P8", "X1", "X2", "X3", "X4"]]
+    for name, ops in cases:
+        t = [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in ops]
+        probe = diag.mma_tile(*t).cpu().numpy()
+        assert diag.device_status() == 0
+        assert np.array_equal(probe, d[name]), name
+        assert np.array_equal(run_f32(nv, *ops, M, N, K), probe), name
+        assert np.array_equal(oracle.gemm_f32(*ops, M, N, K, model=oracle.ACC_TCGEN05), probe), name
+
+
 @pytest.mark.parametrize("seed", [1, 2, 3])
 def test_cfg1_tile_bitexact(nv, oracle, seed):
     M, N, K = 128, 256, 256

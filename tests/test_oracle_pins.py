@@ -214,10 +214,11 @@ def test_live_reference_fill_and_gemm(oracle):
 
 # --------------------------------------- tcgen05 arithmetic, pinned on B200 ----
 def test_oracle_tcgen05_model_reproduces_b200_outputs(oracle):
-    """tests/golden/tcgen05_b200_outputs.npz holds raw fp32 outputs of the production GEMM
-    kernel measured on a B200 (script: tests/golden/make_tcgen05_fixture.py).  The oracle's
-    hardware model must reproduce all of them bit for bit, and the simpler round-to-nearest
-    models must not (they are what the hardware does NOT do)."""
+    """tests/golden/tcgen05_b200_outputs.npz holds raw fp32 outputs of a stand-alone single-tile
+    tcgen05 probe measured on a B200 (nvfp4_diag_mma_tile, independent of the production GEMM;
+    script: tests/golden/make_tcgen05_fixture.py).  The oracle's hardware model must reproduce
+    all of them bit for bit, and the simpler round-to-nearest models must not (they are what the
+    hardware does NOT do)."""
     import sys
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     from test_gemm_gpu import cfg1_tile

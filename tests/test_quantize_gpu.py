@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from tensorcore_ptx_example_b200 import workloads
+from tensorcore_ptx_example_b200 import diag, workloads
 
 pytestmark = pytest.mark.gpu
 
@@ -43,7 +43,7 @@ def test_e2m1_cvt_matches_oracle(nv, oracle):
         (np.arange(0, 0x7F80, dtype=np.uint32) << 16).view(np.float32),
     ])
     x = np.concatenate([pos, -pos]).astype(np.float32)
-    got = nv.diag_e2m1_encode(torch.from_numpy(x).cuda()).cpu().numpy()
+    got = diag.e2m1_encode(torch.from_numpy(x).cuda()).cpu().numpy()
     torch.cuda.synchronize()
     want = oracle.e2m1_encode(x)
     bad = np.nonzero(got != want)[0]
@@ -65,7 +65,7 @@ def test_e4m3_cvt_matches_oracle(nv, oracle):
         np.array([0.0, 1e-45, 2.0 ** -10, 2.0 ** -9, 3 * 2.0 ** -11, 1e6, 3e38], dtype=np.float32),
     ])
     x = np.concatenate([pos, -pos]).astype(np.float32)
-    got = nv.diag_e4m3_encode(torch.from_numpy(x).cuda()).cpu().numpy()
+    got = diag.e4m3_encode(torch.from_numpy(x).cuda()).cpu().numpy()
     want = oracle.e4m3_encode(x)
     bad = np.nonzero(got != want)[0]
     assert bad.size == 0, f"{bad.size} mismatches, first: x={x[bad[:8]]} gpu={got[bad[:8]]} cpu={want[bad[:8]]}"
@@ -156,3 +156,46 @@ def test_quantize_edge_cases(nv, oracle):
     packed, sf, gsd = nv.quantize(zeros, None)
     torch.cuda.synchronize()
     assert gsd.item() == 1.0 and int(packed.sum()) == 0 and int(sf.sum()) == 0
+
+
+DEV_NONFINITE_INPUT = 0x302
+
+
+def test_nonfinite_input_defined_behaviour(nv, oracle):
+    """NaN and +-Inf inputs: amax skips them, a block holding one gets scale 0x7F (E4M3 NaN) and
+    zero codes, every other block is quantized as usual (bit-exact against the oracle), and the
+    device status records DEV_NONFINITE_INPUT."""
+    rows, cols = 256, 1024
+    x = workloads.activations(rows, cols, seed=77)
+    xu = to_np_u16(x).copy()
+    rng = np.random.default_rng(5)
+    pos = rng.choice(rows * cols, size=40, replace=False)
+    specials = np.array([0x7FC0, 0xFFC0, 0x7F80, 0xFF80, 0x7F81], dtype=np.uint16)   # NaN, -NaN, Inf, -Inf, sNaN
+    xu.reshape(-1)[pos] = specials[np.arange(pos.size) % specials.size]
+    xd = from_np_u16(xu)
+    nv.device_status()                                   # clear
+    am = float(nv.amax(xd).item())
+    torch.cuda.synchronize()
+    assert nv.device_status() == DEV_NONFINITE_INPUT
+    assert am == oracle.amax_bf16(xu) and np.isfinite(am)
+    gs, _ = oracle.global_scale(am)
+    packed, sf, _ = nv.quantize(xd, gs)
+    torch.cuda.synchronize()
+    assert nv.device_status() == DEV_NONFINITE_INPUT
+    p_ref, s_ref = oracle.quantize_bf16(xu, gs)
+    assert np.array_equal(packed.cpu().numpy(), p_ref)
+    assert np.array_equal(sf.cpu().numpy(), s_ref)
+    blocks = np.unique(pos // 16)
+    offs = oracle.sf_offsets(rows, cols).reshape(-1)
+    assert np.all(s_ref[offs[blocks]] == 0x7F)
+    # the auto-scaled path takes the finite amax
+    packed2, sf2, gs_dev = nv.quantize(xd, None)
+    torch.cuda.synchronize()
+    assert nv.device_status() == DEV_NONFINITE_INPUT
+    assert np.float32(gs_dev.item()) == np.float32(gs)
+    assert torch.equal(packed2, packed) and torch.equal(sf2, sf)
+    # finite input leaves the status clear
+    nv.quantize(x, gs)
+    nv.amax(x)
+    torch.cuda.synchronize()
+    assert nv.device_status() == 0

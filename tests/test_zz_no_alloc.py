@@ -59,3 +59,18 @@ def test_noalloc_matches_workspace_entry_point(nv):
         assert torch.equal(got[2], want[2]), (got[2].item(), want[2].item())
         assert torch.equal(got[0], want[0])
         assert torch.equal(got[1], want[1])
+
+
+@pytest.mark.gpu
+def test_noalloc_empty_tensor_writes_global_scale(nv):
+    """rows = 0: nothing to quantize, but the global scale is still written (amax 0 -> gs 1)."""
+    L = nv.lib()
+    x = torch.zeros(64, dtype=torch.bfloat16, device="cuda")          # valid pointers, 0 rows used
+    packed = torch.zeros(64, dtype=torch.uint8, device="cuda")
+    sf = torch.zeros(64, dtype=torch.uint8, device="cuda")
+    gs = torch.full((1,), -1.0, dtype=torch.float32, device="cuda")
+    rc = L.nvfp4_quantize_bf16_auto_noalloc(_p(x), 0, 64, _p(packed), _p(sf), _p(gs), None)
+    assert rc == 0, L.nvfp4_last_error_string()
+    torch.cuda.synchronize()
+    assert nv.device_status() == 0
+    assert gs.item() == 1.0
