@@ -135,12 +135,14 @@ NVFP4_API nvfp4_status_t nvfp4_dequantize_bf16(const void* packed, const void* s
  * sfb: nvfp4_sf_bytes(N, K); D: bf16 row-major M x N.  alpha = gsA * gsB.
  * Requires K % 256 == 0, 16-byte aligned buffers, and either M % 128 == 0 with N % 256 == 0
  * (tiled kernels), or 0 < M < 128 with N % 128 == 0 (decode shapes: a split-K kernel over
- * 128-row tiles of B; its fp32 partials go to a workspace -- a buffer the library allocates once
- * per device for nvfp4_gemm_bf16, or the caller's for nvfp4_gemm_bf16_ws -- and are summed in
- * split order 0..S-1 before alpha and the bf16 rounding). */
+ * 128-row tiles of B whose fp32 partials are summed in split order 0..S-1 before alpha and the
+ * bf16 rounding -- inside thread-block clusters when the S <= 8 splits of a tile fit one, which
+ * needs no workspace, else through a workspace: a buffer the library allocates once per device
+ * for nvfp4_gemm_bf16, or the caller's for nvfp4_gemm_bf16_ws). */
 NVFP4_API nvfp4_status_t nvfp4_gemm_bf16(const void* A, const void* sfa, const void* B, const void* sfb,
                                float alpha, void* D, int64_t M, int64_t N, int64_t K, void* stream);
-/* Workspace bytes nvfp4_gemm_bf16_ws needs for this shape (0 for M % 128 == 0). */
+/* Workspace bytes nvfp4_gemm_bf16_ws needs for this shape (0 for M % 128 == 0 and for decode
+ * shapes reduced in-cluster; the workspace may then be NULL). */
 NVFP4_API size_t nvfp4_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 NVFP4_API nvfp4_status_t nvfp4_gemm_bf16_ws(const void* A, const void* sfa, const void* B, const void* sfb,
                                   float alpha, void* D, int64_t M, int64_t N, int64_t K, void* workspace,

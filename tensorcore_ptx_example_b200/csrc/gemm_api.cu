@@ -1,5 +1,7 @@
 // gemm_api.cu -- C ABI of the NVFP4 GEMM: shape checks and kernel choice.
-//   0 < M < 128     : small-M split-K kernel (gemm_small.cu; decode shapes), N % 128 == 0
+//   0 < M < 128     : small-M split-K kernel (gemm_small.cu; decode shapes), N % 128 == 0; its
+//                     partials are summed inside thread-block clusters when the splits of an
+//                     n-tile fit one (no workspace), else through a workspace and a second kernel
 //   M % 128 == 0    : CTA-pair kernel (gemm_2sm.cu, tcgen05 cta_group::2, 256x256 pair tiles; with
 //                     M % 256 == 128 the last pair's second CTA covers zero-filled rows)
 #include <cmath>
@@ -62,7 +64,7 @@ static nvfp4_status_t dispatch(const void* A, const void* sfa, const void* B, co
     if (small_m(M)) {
         if (!ws) {
             ws_bytes = gsmall::workspace_bytes(M, N, K);
-            if ((st = internal_workspace(ws_bytes, &ws))) return st;
+            if (ws_bytes && (st = internal_workspace(ws_bytes, &ws))) return st;
         } else if (!aligned16(ws)) {
             return fail(NVFP4_ERR_INVALID_ARG, "gemm: workspace must be 16-byte aligned");
         }
@@ -100,7 +102,9 @@ nvfp4_status_t nvfp4_gemm_bf16_ws(const void* A, const void* sfa, const void* B,
                                   int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes,
                                   void* stream) {
     clear_error();
-    if (M > 0 && M < 128 && !workspace) return fail(NVFP4_ERR_INVALID_ARG, "gemm_ws: null workspace");
+    if (M > 0 && M < 128 && !workspace && gsmall::workspace_bytes(M, N, K) > 0)
+        return fail(NVFP4_ERR_INVALID_ARG, "gemm_ws: null workspace (this shape needs %zu bytes)",
+                    gsmall::workspace_bytes(M, N, K));
     return gemm::dispatch<false>(A, sfa, B, sfb, alpha, D, M, N, K, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 

@@ -7,12 +7,18 @@
 // the MMA computes D^T tiles [128 n][Mp m] (Mp = M rounded up to 16) with B as the M-side operand
 // and A as the N-side operand of tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X.
 // Split-K gives enough work units to stream B from every SM: unit (n-tile, s) covers K range
-// [s * Ks, (s + 1) * Ks) and writes its fp32 partial tile to a workspace.  A second kernel (four
-// outputs per thread, all S partial loads in flight) sums the partials in split order 0..S-1
-// (fp32, round to nearest) and applies alpha -> bf16.  Both kernels are programmatic dependent
-// launches: the GEMM's set-up overlaps the previous kernel and the reduction is resident and
-// waiting when the GEMM finishes.  (Summing in the CTA that finishes a tile's last unit was
-// measured slower: the sum then runs on 56 CTAs at the tail.)
+// [s * Ks, (s + 1) * Ks).  The partial tiles are summed in split order 0..S-1 (fp32, round to
+// nearest) and alpha -> bf16 is applied, in one of two ways:
+//   in-cluster (one launch; when every unit gets its own CTA and S <= 8): the S CTAs of an n-tile
+//     form a thread-block cluster; each writes its partial tile into its own shared memory (the
+//     drained stage ring), and CTA s then sums rows [s * 128 / S, (s + 1) * 128 / S) of the tile
+//     from all S partials through distributed shared memory (ld.shared::cluster) and stores D.
+//     Two mbarriers per CTA, arrived on remotely by every CTA of the cluster, hand the partials
+//     over ("ready") and keep each CTA resident until every peer has read it ("read");
+//   workspace (otherwise): the partials go to a global workspace and a second kernel (four
+//     outputs per thread, all S partial loads in flight) sums them.  Both kernels are
+//     programmatic dependent launches.
+// Both give the same bits.
 //
 // Persistent CTAs walk the work units (n-tile, split), split fastest so that the SMs stream
 // neighbouring stretches of B.  For Mp <= 64 two CTAs share an SM (about 100 KB of shared memory
@@ -33,9 +39,10 @@
 // TMEM: two accumulator buffers of Mp columns at [0, Mp) and [Mp, 2 Mp), then one 32-column scale
 // slot per stage (B scales +0..15, A scales +16..31); the allocation is the next power of two.
 //
-// Timeline at cfg3 (M16 N7168 K8192, 224 CTAs, measured with global timestamps): CTA starts spread
-// over 0.9 us, set-up 0.8 us, first stage lands 2 us later, the stream of B then runs at
-// ~6.6 TB/s for ~5 us, the last CTA exits at ~8.5 us and the reduction ends at ~11.5 us.
+// Timeline at cfg3 with the workspace reduction (M16 N7168 K8192, 224 CTAs, measured with global
+// timestamps): CTA starts spread over 0.9 us, set-up 0.8 us, first stage lands 2 us later, the
+// stream of B then runs at ~6.6 TB/s for ~5 us, the last CTA exits at ~8.5 us and the reduction
+// kernel ends at ~11.5 us; the in-cluster reduction removes that second kernel.
 #include "capi_internal.h"
 #include "nvfp4_common.cuh"
 #include "tma_host.h"
@@ -80,9 +87,57 @@ __host__ __device__ constexpr int tmem_cols(int mp) {
 static_assert(sf_col0(128) + SF_SLOT_COLS * MAX_STAGES <= 512, "scale slots fit in TMEM");
 static_assert(ctas_per_sm(64) == 1 || (tmem_cols(64) <= 256 && tmem_cols(16) <= 256),
               "two CTAs per SM share the 512 TMEM columns");
-// [stages][full, empty, sf_landed per stage][acc_full 2][acc_empty 2][drain][tmem slot]
+// [stages][full, empty, sf_landed per stage][acc_full 2][acc_empty 2][drain][ready][read][tmem slot]
+constexpr int NUM_BARS = 3 * MAX_STAGES + 7;
 __host__ __device__ constexpr int smem_bytes(int mp) {
-    return 1024 + num_stages(mp) * stage_bytes(mp) + (3 * MAX_STAGES + 5) * 8 + 16;
+    return 1024 + num_stages(mp) * stage_bytes(mp) + NUM_BARS * 8 + 16;
+}
+// The in-cluster reduction keeps a partial tile [Mp][128] fp32 in the drained stage ring.
+static_assert(128 * 16 * 4 <= 4 * stage_bytes(16) && 128 * 64 * 4 <= num_stages(64) * stage_bytes(64) &&
+                  128 * 128 * 4 <= num_stages(128) * stage_bytes(128),
+              "partial tile fits in the stage ring");
+constexpr int MAX_CLUSTER_SPLITS = 8;
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t mapa_rank(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+// One arrival on the mbarrier at `addr` (this CTA's or a peer's, a shared::cluster address),
+// ordered after this thread's earlier memory operations at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+// Bounded wait whose completion acquires at cluster scope (the arrivals came from peer CTAs).
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, uint64_t limit_ns, unsigned int err) {
+    uint64_t t0 = 0;
+#pragma unroll 1
+    for (int i = 0;; i++) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if (i == 64) t0 = globaltimer_ns();
+        if (i > 64 && globaltimer_ns() - t0 > limit_ns) {
+            record_error(err);
+            return false;
+        }
+    }
 }
 
 __device__ __forceinline__ void tc_st_x16(uint32_t taddr, const uint4* v) {
@@ -111,11 +166,14 @@ __device__ __forceinline__ void tc_mma_rt(uint32_t d, uint64_t a, uint64_t b, ui
         : "memory");
 }
 
-// ws[s][m][n] = partial of split s (fp32, the tensor core's accumulation over that K range);
+// Workspace path (csplits == 0): ws[s][m][n] = partial of split s (fp32, the tensor core's
+// accumulation over that K range).  In-cluster path (csplits = S, launched with cluster dims
+// (S, 1, 1) and one CTA per unit): D (bf16, or fp32 for out_f32) is written directly.
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                   const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb, float* __restrict__ ws, int M,
-                  int N, int K, int ks, int mp, int b_const) {
+                  int N, int K, int ks, int mp, int b_const, int csplits, void* __restrict__ D, float alpha,
+                  int out_f32) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -130,7 +188,8 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
     auto sf_landed = [&](int st) { return bar0 + 8u * (2 * MAX_STAGES + st); };
     const int acc_cols = mp, sf0 = sf_col0(mp), tcols = tmem_cols(mp);
     const uint32_t acc_full = bar0 + 8u * (3 * MAX_STAGES), acc_empty = acc_full + 16, drain = acc_full + 32;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S * SB + (3 * MAX_STAGES + 5) * 8);
+    const uint32_t ready_bar = acc_full + 40, read_bar = acc_full + 48;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S * SB + NUM_BARS * 8);
     uint32_t* abort_flag = tmem_slot + 1;       // the epilogue warps give up together
 
     if (warp == 0 && lane == 0) {
@@ -146,6 +205,8 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
             mbar_init(acc_empty + 8 * b, 4);           // the four epilogue warps
         }
         mbar_init(drain, 1);
+        mbar_init(ready_bar, csplits > 0 ? csplits : 1);   // one arrival per CTA of the cluster
+        mbar_init(read_bar, csplits > 0 ? csplits : 1);
         *abort_flag = 0u;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -157,6 +218,8 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
         tc_fence_before();
     }
     __syncthreads();
+    // peers arrive on this CTA's barriers only after they are initialised
+    if (csplits > 0) asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     // Programmatic dependent launch: the set-up above overlapped the previous kernel in the
@@ -293,8 +356,54 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
             }
             if (!ok) break;
         }
+    } else if (csplits > 0) {
+        // ------------------------------------------ epilogue, in-cluster reduction ----
+        // One unit per CTA: split sp = this CTA's rank in the cluster, n-tile nt = cluster index.
+        const uint32_t q = (uint32_t)(warp & 3);
+        const int t = (int)threadIdx.x - 64;                  // 0..127 over the four epilogue warps
+        const int sp = blockIdx.x % csplits, nt = blockIdx.x / csplits;
+        const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(acc_full, 0u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_EPILOGUE));
+        tc_fence_after();
+        // partial tile into this CTA's drained stage ring, [m][128 n] (every MMA that read the ring
+        // has completed: acc_full is their commit)
+        float* part = reinterpret_cast<float*>(smem);
+        if (ok) {
+            const int n = (int)q * 32 + lane;                 // TMEM lane = row n of the D^T tile
+            for (int c = 0; c < mp; c += 16) {
+                uint32_t r[16];
+                tc_ld_x16(tmem + ((q * 32u) << 16) + c, r);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int i = 0; i < 16; i++) part[(c + i) * 128 + n] = __uint_as_float(r[i]);
+            }
+        }
+        if (!ok && lane == 0) *abort_flag = 1u;
+        named_bar_sync(1, 128);
+        const bool wrote = *abort_flag == 0u;
+        if (t == 0 && wrote)
+            for (int r = 0; r < csplits; r++) mbar_arrive_cluster(mapa_rank(ready_bar, (uint32_t)r));
+        // every split's partial is in place: sum this CTA's rows in split order, store D
+        const bool ready = mbar_wait_cluster(ready_bar, 0u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_EPILOGUE);
+        if (ready) {
+            const int rows = 128 / csplits, n0 = sp * rows;
+            const uint32_t pbase = smem_u32(part);
+            for (int i = t; i < rows * M; i += 128) {
+                const int m = i / rows, nn = n0 + i % rows;
+                const uint32_t off = pbase + (uint32_t)((m * 128 + nn) * 4);
+                float acc = 0.0f;
+                for (int r = 0; r < csplits; r++) acc = __fadd_rn(acc, ld_cluster_f32(mapa_rank(off, (uint32_t)r)));
+                const int64_t o = (int64_t)m * N + (int64_t)nt * 128 + nn;
+                if (out_f32) reinterpret_cast<float*>(D)[o] = acc;
+                else reinterpret_cast<__nv_bfloat16*>(D)[o] = __float2bfloat16_rn(__fmul_rn(acc, alpha));
+            }
+        }
+        named_bar_sync(1, 128);
+        // this CTA has read every peer: tell them; then stay until every peer has read this one
+        if (t == 0)
+            for (int r = 0; r < csplits; r++) mbar_arrive_cluster(mapa_rank(read_bar, (uint32_t)r));
+        mbar_wait_cluster(read_bar, 0u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_TEARDOWN);
     } else {
-        // ----------------------------------------------------------- epilogue ----
+        // ------------------------------------------------ epilogue, workspace path ----
         const uint32_t q = (uint32_t)(warp & 3);
         const uint32_t lane_base = (q * 32u) << 16;
         int iter = 0;
@@ -404,10 +513,18 @@ inline int persistent_grid(int units, int sms) {
     return sms;
 }
 
-// Workspace: the fp32 partials [splits][M][N].
+// The in-cluster reduction applies when the splits of an n-tile fit one cluster and divide its
+// 128 rows; a function of N and K only.
+inline bool in_cluster_reduce(int64_t N, int64_t K) {
+    const int ks = split_k(N, K);
+    return ks && K / ks <= MAX_CLUSTER_SPLITS && 128 % (K / ks) == 0;
+}
+
+// Workspace: the fp32 partials [splits][M][N] of the workspace path (none in-cluster).
 inline size_t workspace_bytes(int64_t M, int64_t N, int64_t K) {
     const int ks = split_k(N, K);
-    return ks ? (size_t)(K / ks) * (size_t)M * (size_t)N * sizeof(float) : 0;
+    if (!ks || in_cluster_reduce(N, K)) return 0;
+    return (size_t)(K / ks) * (size_t)M * (size_t)N * sizeof(float);
 }
 
 template <bool kOutF32>
@@ -441,24 +558,31 @@ nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void*
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     const int units = (int)(N / 128) * splits;
-    const int grid = persistent_grid(units, ctas_per_sm(mp) * sm_count());
+    // in-cluster reduction: one CTA per unit, the S splits of an n-tile in one cluster
+    const bool in_cluster = in_cluster_reduce(N, K);
+    const int grid = in_cluster ? units : persistent_grid(units, ctas_per_sm(mp) * sm_count());
     float* w = reinterpret_cast<float*>(ws);
-    // Both kernels are launched as programmatic dependents of the previous work in the stream.
-    cudaLaunchAttribute pdl[1];
-    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    // Launched as a programmatic dependent of the previous work in the stream (and, in-cluster,
+    // with cluster dims (S, 1, 1)).
+    cudaLaunchAttribute attrs[2];
+    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[0].val.programmaticStreamSerializationAllowed = 1;
+    attrs[1].id = cudaLaunchAttributeClusterDimension;
+    attrs[1].val.clusterDim.x = (unsigned)splits;
+    attrs[1].val.clusterDim.y = 1;
+    attrs[1].val.clusterDim.z = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
     cfg.blockDim = dim3(THREADS, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cfg.attrs = pdl;
-    cfg.numAttrs = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = in_cluster ? 2 : 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_small_kernel, ta, tb, reinterpret_cast<const uint8_t*>(sfa),
                                        reinterpret_cast<const uint8_t*>(sfb), w, (int)M, (int)N, (int)K, ks, mp,
-                                       b_const ? 1 : 0);
+                                       b_const ? 1 : 0, in_cluster ? splits : 0, D, alpha, kOutF32 ? 1 : 0);
     if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "gemm_small_kernel: %s", cudaGetErrorString(e));
-    if ((st = check_launch("gemm_small_kernel"))) return st;
+    if ((st = check_launch("gemm_small_kernel")) || in_cluster) return st;
     const int64_t mn = M * N;
     int64_t rg = (mn / 4 + 255) / 256;
     const int64_t cap = (int64_t)sm_count() * 8;
@@ -466,6 +590,7 @@ nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void*
     cfg.gridDim = dim3((unsigned)rg, 1, 1);
     cfg.blockDim = dim3(256, 1, 1);
     cfg.dynamicSmemBytes = 0;
+    cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<kOutF32>, (const float*)w, D, mn, splits, alpha);
     if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "splitk_reduce_kernel: %s", cudaGetErrorString(e));
     return check_launch("splitk_reduce_kernel");

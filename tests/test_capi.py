@@ -99,8 +99,11 @@ def test_argument_checks_reject_before_launch(nv):
     assert "M % 128" in msg
     msg = _err(nv, L.nvfp4_gemm_bf16(fake, fake, fake, fake, ctypes.c_float(1.0), fake, 16, 200, 256, None))
     assert "N % 128" in msg
-    msg = _err(nv, L.nvfp4_gemm_bf16_ws(fake, fake, fake, fake, ctypes.c_float(1.0), fake, 16, 256, 256, None, 0, None))
+    # 16 splits of 256 K on one 128-row tile: more than a cluster holds, so a workspace is needed
+    msg = _err(nv, L.nvfp4_gemm_bf16_ws(fake, fake, fake, fake, ctypes.c_float(1.0), fake, 16, 128, 4096, None, 0, None))
     assert "workspace" in msg
+    assert L.nvfp4_gemm_workspace_bytes(16, 128, 4096) == 16 * 16 * 128 * 4
+    assert L.nvfp4_gemm_workspace_bytes(16, 7168, 8192) == 0          # cfg3 decode: reduced in-cluster
     msg = _err(nv, L.nvfp4_gemm_f32(fake, fake, fake, fake, fake, 128, 256, 100, None))
     assert "K % 256" in msg
     f1 = ctypes.c_float(1.0)
