@@ -733,7 +733,7 @@ def _ar_time_b2b(fn, calls, warmup, world):
 def _wire_bytes(name, numel, world, payload_bytes_per_elt):
     """Bytes one rank sends over NVLink per call: two-shot 2 (n-1)/n of the payload, one-shot
     (n-1) times the payload."""
-    two = "twoshot" in name
+    two = "twoshot" in name or "nvls" in name          # NVLS: each shard's sum leaves and returns once
     return (2.0 * (world - 1) / world if two else (world - 1)) * payload_bytes_per_elt * numel
 
 
@@ -753,7 +753,7 @@ ORACLE_AR = {"nvfp4_twoshot": "ar_twoshot", "nvfp4_oneshot": "ar_oneshot", "nvfp
              "bf16_twoshot": "ar_bf16", "bf16_oneshot": "ar_bf16"}
 
 
-def ar_parity(ctx, x, out, gs, world, rank, windows=12, win=8192):
+def ar_parity(ctx, x, out, gs, world, rank, windows=12, win=8192, nvls=False):
     """Bit-exact check of every algorithm against the CPU oracle (its fixed-order restatement of
     the two-shot / one-shot data flow) on sampled windows of the output.  A window of aligned
     16-element blocks depends only on the same window of every rank's input (quantization blocks,
@@ -771,6 +771,8 @@ def ar_parity(ctx, x, out, gs, world, rank, windows=12, win=8192):
     ok_all = True
     cases = [("nvfp4_twoshot", numel), ("nvfp4_oneshot", numel), ("bf16_twoshot", numel),
              ("bf16_oneshot", numel), ("nvfp4_lowlat", min(numel, ar.LOWLAT_CAP_BYTES // 2))]
+    if nvls:
+        cases.append(("bf16_nvls", numel))
     for name, n in cases:
         nw = min(windows, n // win)
         rng = np.random.default_rng(1234 + n)
@@ -789,7 +791,18 @@ def ar_parity(ctx, x, out, gs, world, rank, windows=12, win=8192):
         dist.all_gather(ins, xin)
         dist.all_gather(outs, xout)
         ok = True
-        if rank == 0:
+        if rank == 0 and name == "bf16_nvls":
+            # the switch orders the fp32 additions: within 1 bf16 ulp of the exact sum, and the
+            # same on every rank
+            u16 = [t.view(torch.int16).cpu().numpy().view(np.uint16) for t in ins]
+            exact = py_oracle.sum_f64(u16)
+            got0 = outs[0].view(torch.int16).cpu().numpy().view(np.uint16)
+            g = py_oracle.bf16_to_f32(got0).astype(np.float64)
+            ulp = np.abs(py_oracle.bf16_to_f32(py_oracle.f32_to_bf16(exact.astype(np.float32)))) * 2.0 ** -7
+            ok = bool(np.all(np.abs(g - exact) <= np.maximum(ulp, 2.0 ** -133)))
+            for r in range(world):
+                ok = ok and bool(np.array_equal(outs[r].view(torch.int16).cpu().numpy().view(np.uint16), got0))
+        elif rank == 0:
             u16 = [t.view(torch.int16).cpu().numpy().view(np.uint16) for t in ins]
             fn = getattr(py_oracle, ORACLE_AR[name])
             want = fn(u16) if name.startswith("bf16") else fn(u16, gs)
@@ -805,7 +818,7 @@ def ar_parity(ctx, x, out, gs, world, rank, windows=12, win=8192):
     return res
 
 
-def allreduce_algos(ctx, x, out, gs, world, steps, flush):
+def allreduce_algos(ctx, x, out, gs, world, steps, flush, nvls=False):
     """cfg4, every algorithm: device time per call (max over ranks, L2 flushed between calls),
     and the NVFP4 error against the exact fp32 sum."""
     import torch
@@ -816,6 +829,8 @@ def allreduce_algos(ctx, x, out, gs, world, steps, flush):
             ("nvfp4_oneshot", lambda: ctx.allreduce(x, out, global_scale=gs, algo="oneshot"), 0.5625),
             ("bf16_twoshot", lambda: ctx.bf16_allreduce(x, out, algo="twoshot"), 2.0),
             ("bf16_oneshot", lambda: ctx.bf16_allreduce(x, out, algo="oneshot"), 2.0)]
+    if nvls:
+        runs.append(("bf16_nvls", lambda: ctx.bf16_allreduce(x, out, algo="nvls"), 2.0))
     for name, fn, bpe in runs:
         res[name] = _ar_entry(name, numel, world, _ar_time(fn, steps, 3, flush, world), bpe)
     exact = x.float().clone()
@@ -831,7 +846,7 @@ def allreduce_algos(ctx, x, out, gs, world, steps, flush):
 SWEEP_ROWS_BYTES = [64 << 10, 1 << 20, 4 << 20, 16 << 20, 64 << 20, 256 << 20]
 
 
-def ar_sweep_rows(ctx, xfull, ofull, gs, world, sizes=SWEEP_ROWS_BYTES):
+def ar_sweep_rows(ctx, xfull, ofull, gs, world, sizes=SWEEP_ROWS_BYTES, nvls=False):
     """cfg5 rows: every algorithm at each size, back-to-back calls (max over ranks); best NVFP4
     against best bf16."""
     from tensorcore_ptx_example_b200 import allreduce as ar
@@ -847,6 +862,8 @@ def ar_sweep_rows(ctx, xfull, ofull, gs, world, sizes=SWEEP_ROWS_BYTES):
                  ("nvfp4_twoshot", lambda: ctx.allreduce(x, o, global_scale=gs, algo="twoshot")),
                  ("bf16_oneshot", lambda: ctx.bf16_allreduce(x, o, algo="oneshot")),
                  ("bf16_twoshot", lambda: ctx.bf16_allreduce(x, o, algo="twoshot"))]
+        if nvls:
+            algos.append(("bf16_nvls", lambda: ctx.bf16_allreduce(x, o, algo="nvls")))
         if b > ar.LOWLAT_CAP_BYTES:
             algos = algos[1:]
         row = {"bytes": b}
@@ -1012,6 +1029,11 @@ def run_allreduce_line(args):
     x = workloads.gaussian(1, numel, seed=rank).view(-1)
     gs = ar.agree_global_scale(float(nv.amax(x).item()))
     ctx = ar.AllReduce.from_process_group(max(numel, sweep_max))
+    nvls_error = None
+    try:
+        nvls = ctx.enable_nvls()          # in-switch bf16 baseline, where the GPUs offer multicast
+    except Exception as e:  # reported, not fatal
+        nvls, nvls_error = False, str(e)
     out = torch.empty_like(x)
     algo = {ar.ONESHOT: "oneshot", ar.TWOSHOT: "twoshot", ar.LOWLAT: "lowlat"}[ar.choose_algo(world, numel)]
     extra = {}
@@ -1034,8 +1056,8 @@ def run_allreduce_line(args):
         wire = _wire_bytes(algo, numel, world, 0.5625)
         achieved = wire / (mean_ms * 1e-3) / 1e9
 
-        parity = ar_parity(ctx, x, out, gs, world, rank)
-        algos, exact = allreduce_algos(ctx, x, out, gs, world, max(5, min(args.steps, 20)), flush)
+        parity = ar_parity(ctx, x, out, gs, world, rank, nvls=nvls)
+        algos, exact = allreduce_algos(ctx, x, out, gs, world, max(5, min(args.steps, 20)), flush, nvls=nvls)
 
         # end to end through the public API with host buffers: the input copied from pinned
         # host memory and the result copied back every step (pipelined like the GEMM's)
@@ -1051,7 +1073,7 @@ def run_allreduce_line(args):
         xfull = workloads.gaussian(1, sweep_max, seed=100 + rank).view(-1)
         gs_sweep = ar.agree_global_scale(float(nv.amax(xfull).item()))
         ofull = torch.empty_like(xfull)
-        sweep = ar_sweep_rows(ctx, xfull, ofull, gs_sweep, world)
+        sweep = ar_sweep_rows(ctx, xfull, ofull, gs_sweep, world, nvls=nvls)
         del xfull, ofull
         status = status or nv.device_status()
     finally:
@@ -1091,6 +1113,7 @@ def run_allreduce_line(args):
                      "wire_bytes_per_launch": int(wire), "traffic": None},
         "parity_ok": parity["all"],
         "parity": parity,
+        "nvls": nvls if nvls_error is None else {"error": nvls_error},
         "device_status": status,
         "algorithms": algos,
         "sweep_rows": sweep,

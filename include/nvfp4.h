@@ -197,6 +197,14 @@ typedef struct nvfp4_ar* nvfp4_ar_t;
  * NVFP4_AR_LOWLAT_CAP_BYTES of bf16 per call. */
 #define NVFP4_AR_LOWLAT 3
 #define NVFP4_AR_LOWLAT_CAP_BYTES (1 << 20)
+/* bf16 all-reduce whose sum is done inside the NVSwitch (NVLS): multimem.ld_reduce.add.acc::f32
+ * through a multicast address returns the fp32 sum over every rank's buffer, multimem.st writes
+ * it back to every rank (reference: the multimem reduction demo,
+ * blackwell/comm_primitives_sm100_sm120/minimal_multimem_reduce.cu:68-80).  nvfp4_ar_bf16_allreduce
+ * only, after nvfp4_ar_set_multicast; never chosen by NVFP4_AR_AUTO.  The switch orders the fp32
+ * additions, so results equal the exact sum rounded once to bf16 except where fp32 rounding of
+ * the partial sums moves a value across a bf16 rounding boundary (within 1 bf16 ulp). */
+#define NVFP4_AR_NVLS 4
 /* NVFP4_AR_AUTO picks the low-latency one-shot up to NVFP4_AR_LOWLAT_MAX_BYTES of bf16,
  * one-shot up to NVFP4_AR_ONESHOT_MAX_BYTES, two-shot above. */
 #define NVFP4_AR_LOWLAT_MAX_BYTES (1 << 20)
@@ -218,6 +226,12 @@ NVFP4_API nvfp4_status_t nvfp4_ar_open_peers(nvfp4_ar_t h, const void* handles);
  * enabled here. */
 NVFP4_API nvfp4_status_t nvfp4_ar_local_base(nvfp4_ar_t h, void** base);
 NVFP4_API nvfp4_status_t nvfp4_ar_set_peers(nvfp4_ar_t h, void* const* bases);
+/* Registers the buffer NVFP4_AR_NVLS works in: `bytes` bytes that every rank has bound to the same
+ * NVLink multicast object (e.g. torch symmetric memory with multicast support); mc_base is its
+ * multicast address, uc_base this rank's unicast address of it.  Calls alternate between its two
+ * halves, so one call may reduce at most bytes / 4 bf16 elements.  The buffer must outlive the
+ * context's last NVLS call; every rank registers one of the same size. */
+NVFP4_API nvfp4_status_t nvfp4_ar_set_multicast(nvfp4_ar_t h, void* mc_base, void* uc_base, int64_t bytes);
 /* Time limit of each cross-GPU wait (default 5 s); a wait that runs out records a device status
  * (nvfp4_device_status) and the kernel returns. */
 NVFP4_API nvfp4_status_t nvfp4_ar_set_timeout(nvfp4_ar_t h, uint64_t timeout_ns);
@@ -231,7 +245,8 @@ NVFP4_API int nvfp4_ar_choose_algo(int world, int64_t numel);
  * in and out may not alias. */
 NVFP4_API nvfp4_status_t nvfp4_ar_allreduce(nvfp4_ar_t h, const void* in, void* out, int64_t numel,
                                             float global_scale, int algo, void* stream);
-/* bf16 peer-to-peer all-reduce (fp32 sum in rank order, one bf16 rounding): numel % (8 * world) == 0. */
+/* bf16 all-reduce: peer-to-peer (ONESHOT / TWOSHOT / AUTO: fp32 sum in rank order, one bf16
+ * rounding) or in the switch (NVFP4_AR_NVLS, see above): numel % (8 * world) == 0. */
 NVFP4_API nvfp4_status_t nvfp4_ar_bf16_allreduce(nvfp4_ar_t h, const void* in, void* out, int64_t numel, int algo,
                                                  void* stream);
 /* The same data path for `world` ranks that all live on ONE GPU (contexts created on it with

@@ -53,6 +53,7 @@ SIGNATURES = {
     "nvfp4_ar_local_base": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
     "nvfp4_ar_set_peers": (_I, [_P, _P]),
     "nvfp4_ar_set_timeout": (_I, [_P, ctypes.c_uint64]),
+    "nvfp4_ar_set_multicast": (_I, [_P, _P, _P, _I64]),
     "nvfp4_ar_reset": (_I, [_P]),
     "nvfp4_ar_choose_algo": (_I, [_I, _I64]),
     "nvfp4_ar_allreduce": (_I, [_P, _P, _P, _I64, _F, _I, _P]),

@@ -22,10 +22,10 @@ import ctypes
 
 from . import _empty, _ptr, _stream, check, lib
 
-AUTO, ONESHOT, TWOSHOT, LOWLAT = 0, 1, 2, 3
+AUTO, ONESHOT, TWOSHOT, LOWLAT, NVLS = 0, 1, 2, 3, 4
 LOWLAT_CAP_BYTES = 1 << 20          # NVFP4_AR_LOWLAT_CAP_BYTES: largest low-latency call (bf16 bytes)
-_ALGOS = {"auto": AUTO, "oneshot": ONESHOT, "twoshot": TWOSHOT, "lowlat": LOWLAT,
-          AUTO: AUTO, ONESHOT: ONESHOT, TWOSHOT: TWOSHOT, LOWLAT: LOWLAT}
+_ALGOS = {"auto": AUTO, "oneshot": ONESHOT, "twoshot": TWOSHOT, "lowlat": LOWLAT, "nvls": NVLS,
+          AUTO: AUTO, ONESHOT: ONESHOT, TWOSHOT: TWOSHOT, LOWLAT: LOWLAT, NVLS: NVLS}
 
 
 def buffer_bytes(world: int, max_numel: int) -> int:
@@ -39,7 +39,7 @@ def choose_algo(world: int, numel: int) -> int:
 
 def _algo(a) -> int:
     if a not in _ALGOS:
-        raise ValueError(f"algo must be one of auto/oneshot/twoshot/lowlat, got {a!r}")
+        raise ValueError(f"algo must be one of auto/oneshot/twoshot/lowlat/nvls, got {a!r}")
     return _ALGOS[a]
 
 
@@ -53,6 +53,7 @@ class AllReduce:
         h = ctypes.c_void_p()
         check(lib().nvfp4_ar_create(self.world, self.rank, self.max_numel, ctypes.byref(h)))
         self._h = h
+        self._nvls = None
 
     # ------------------------------------------------------------ set-up ----
     @property
@@ -83,6 +84,31 @@ class AllReduce:
     def set_peers(self, bases) -> None:
         arr = (ctypes.c_void_p * self.world)(*[ctypes.c_void_p(int(b)) for b in bases])
         check(lib().nvfp4_ar_set_peers(self.handle, arr))
+
+    def enable_nvls(self, group=None) -> bool:
+        """Give this context a buffer bound to an NVLink multicast object, for the in-switch bf16
+        all-reduce (bf16_allreduce(..., algo="nvls")).  Collective over `group` (every rank calls
+        it): torch symmetric memory allocates the buffer and binds every rank's to one multicast
+        object; this library only receives the two addresses.  Returns False on every rank (and
+        leaves NVLS off) when any rank's GPU or driver offers no multicast."""
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+        group = group or dist.group.WORLD
+        nbytes = 2 * ((self.max_numel * 2 + 15) // 16 * 16)
+        buf = symm.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", self.device))
+        hdl = symm.rendezvous(buf, group)
+        mc = int(hdl.multicast_ptr) if hdl.has_multicast_support() else 0
+        backend = dist.get_backend(group)
+        dev = torch.device("cuda", self.device) if backend == "nccl" else torch.device("cpu")
+        ok = torch.tensor([1 if mc else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if not int(ok.item()):
+            return False
+        check(lib().nvfp4_ar_set_multicast(self.handle, ctypes.c_void_p(mc), ctypes.c_void_p(buf.data_ptr()),
+                                           nbytes))
+        self._nvls = (buf, hdl)          # keep the buffer and its mapping alive with the context
+        return True
 
     def set_timeout(self, seconds: float) -> None:
         check(lib().nvfp4_ar_set_timeout(self.handle, int(seconds * 1e9)))
@@ -136,7 +162,8 @@ class AllReduce:
         return out
 
     def bf16_allreduce(self, x, out=None, algo="auto", stream=None):
-        """In-house bf16 peer-to-peer all-reduce (numel % (8 * world) == 0)."""
+        """In-house bf16 all-reduce (numel % (8 * world) == 0): peer-to-peer ("oneshot",
+        "twoshot", "auto") or summed in the NVSwitch ("nvls", after enable_nvls)."""
         import torch
         assert x.dtype == torch.bfloat16 and x.is_cuda and x.is_contiguous()
         if out is None:
@@ -149,6 +176,7 @@ class AllReduce:
         if self._h is not None:
             check(lib().nvfp4_ar_destroy(self._h))
             self._h = None
+        self._nvls = None
 
     def __del__(self):
         try:

@@ -38,6 +38,17 @@
 // rank's data of the call in between).  A word with a tag therefore always belongs to the
 // current call.
 //
+// NVLS bf16 all-reduce (NVFP4_AR_NVLS, bf16 payloads only): the sum is done inside the NVSwitch.
+// Every rank has bound one buffer to an NVLink multicast object (registered with
+// nvfp4_ar_set_multicast: its multicast address and this rank's unicast address).  A: copy the
+// input into this rank's buffer (unicast); barrier; B: for the chunks of this rank's shard,
+// multimem.ld_reduce.add.acc::f32 through the multicast address returns the fp32 sum over every
+// rank's buffer (rounded once to bf16) and multimem.st writes it back to every rank's buffer;
+// barrier; C: copy the buffer to the output.  On the wire each GPU sends and receives about
+// 2 (n-1)/n x 2 bytes per element.  The switch fixes the order of the fp32 additions, not this
+// code, so results are checked against the exact sum within a tolerance, not bit for bit.
+// The buffer has two parity halves, alternated per call like the P2P regions.
+//
 // Synchronisation: block b of every rank handles the same chunks in every phase, so a phase
 // only needs block b of every rank to have finished the previous phase: after its pushes block
 // b does __syncthreads and stores the barrier value into flag [b][me] of every rank with
@@ -84,6 +95,8 @@ struct Params {
     const uint8_t* q_scales;         // [numel / 16] of the whole input, flat
     int64_t ll_off;                  // byte offset of the low-latency area in every rank's buffer
     int64_t ll_slot;                 // bytes of one low-latency slot
+    uint8_t* nvls_mc;                // NVLS: multicast address of this call's parity half
+    uint8_t* nvls_uc;                // NVLS: this rank's unicast address of the same half
 };
 
 __device__ __forceinline__ uint32_t* flags_of(const Params& p, int r) {
@@ -485,6 +498,61 @@ __global__ void __launch_bounds__(AR_THREADS) ar_bf16_kernel(const Params p) {
     }
 }
 
+// ---------------------------------------------------------------- NVLS (in-switch) bf16 ----
+// 8 bf16 per 16-byte vector: the in-switch sum of one chunk over every rank's buffer (fp32
+// accumulation, one rounding to bf16), and its store back to every rank's buffer.
+__device__ __forceinline__ uint4 multimem_ld_reduce_bf16x8(const uint8_t* mc) {
+    uint4 r;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(mc)
+                 : "memory");
+    return r;
+}
+__device__ __forceinline__ void multimem_st_bf16x8(uint8_t* mc, uint4 v) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+// The same memory is written through one address (unicast or multicast) and read through the
+// other: order the accesses across the two aliases.
+__device__ __forceinline__ void fence_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
+
+__global__ void __launch_bounds__(AR_THREADS) ar_bf16_nvls_kernel(const Params p) {
+    const int n = p.world, me = p.rank;
+    const uint32_t v1 = p.epoch * 2u + 1u, v2 = p.epoch * 2u + 2u;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint8_t* in = reinterpret_cast<const uint8_t*>(p.in);
+    uint8_t* out = reinterpret_cast<uint8_t*>(p.out);
+    const int64_t shard = p.numel / n;                 // elements
+    const int64_t schunks = shard / 8;                 // 16-byte chunks of one shard
+    // A: this rank's input into its buffer -- the chunks of every shard that block b of any rank
+    // reduces in B, so that B only needs block b of every rank to have finished A
+    for (int64_t c = first; c < schunks; c += stride)
+        for (int q = 0; q < n; q++) {
+            const int64_t off = ((int64_t)q * shard) * 2 + c * 16;
+            st_v4(p.nvls_uc + off, ld_nc_v4(in + off));
+        }
+    fence_alias();
+    if (!block_barrier(p, v1)) return;
+    fence_alias();
+    // B: the in-switch sum of this rank's shard, written back to every rank
+    for (int64_t c = first; c < schunks; c += stride) {
+        uint8_t* a = p.nvls_mc + ((int64_t)me * shard) * 2 + c * 16;
+        multimem_st_bf16x8(a, multimem_ld_reduce_bf16x8(a));
+    }
+    fence_alias();
+    if (!block_barrier(p, v2)) return;
+    fence_alias();
+    // C: the reduced tensor out of this rank's buffer
+    for (int64_t c = first; c < schunks; c += stride)
+        for (int q = 0; q < n; q++) {
+            const int64_t off = ((int64_t)q * shard) * 2 + c * 16;
+            st_v4(out + off, ld_cg_v4(p.nvls_uc + off));
+        }
+}
+
 }  // namespace ar
 }  // namespace nvfp4
 
@@ -505,6 +573,9 @@ struct nvfp4_ar {
     uint32_t epoch = 0;
     uint64_t timeout_ns = AR_DEFAULT_TIMEOUT_NS;
     int max_grid = 0, ll_max_grid = 0;
+    uint8_t* nvls_mc = nullptr;      // NVLS buffer (nvfp4_ar_set_multicast): multicast address,
+    uint8_t* nvls_uc = nullptr;      // this rank's unicast address,
+    int64_t nvls_half = 0;           // bytes of one parity half
 };
 
 namespace {
@@ -562,8 +633,17 @@ nvfp4_status_t check_call(nvfp4_ar_t h, const char* who, const void* in, const v
     if (numel < 0 || numel > h->max_numel)
         return fail(NVFP4_ERR_INVALID_ARG, "%s: numel %lld outside [0, max_numel=%lld]", who, (long long)numel,
                     (long long)h->max_numel);
-    if (algo != NVFP4_AR_AUTO && algo != NVFP4_AR_ONESHOT && algo != NVFP4_AR_TWOSHOT && algo != NVFP4_AR_LOWLAT)
-        return fail(NVFP4_ERR_INVALID_ARG, "%s: algo must be NVFP4_AR_AUTO, _ONESHOT, _TWOSHOT or _LOWLAT", who);
+    if (algo != NVFP4_AR_AUTO && algo != NVFP4_AR_ONESHOT && algo != NVFP4_AR_TWOSHOT && algo != NVFP4_AR_LOWLAT &&
+        algo != NVFP4_AR_NVLS)
+        return fail(NVFP4_ERR_INVALID_ARG, "%s: algo must be NVFP4_AR_AUTO, _ONESHOT, _TWOSHOT, _LOWLAT or _NVLS", who);
+    if (algo == NVFP4_AR_NVLS && elems_per_chunk != 8)
+        return fail(NVFP4_ERR_UNSUPPORTED, "%s: NVFP4_AR_NVLS sums bf16 in the switch; NVFP4 payloads cannot be summed there",
+                    who);
+    if (algo == NVFP4_AR_NVLS && !h->nvls_mc)
+        return fail(NVFP4_ERR_NOT_READY, "%s: NVFP4_AR_NVLS needs a multicast buffer (nvfp4_ar_set_multicast)", who);
+    if (algo == NVFP4_AR_NVLS && numel * 2 > h->nvls_half)
+        return fail(NVFP4_ERR_INVALID_ARG, "%s: %lld bf16 elements exceed the multicast buffer's half of %lld bytes", who,
+                    (long long)numel, (long long)h->nvls_half);
     if (algo == NVFP4_AR_LOWLAT && elems_per_chunk != 32)
         return fail(NVFP4_ERR_INVALID_ARG, "%s: NVFP4_AR_LOWLAT is an NVFP4 algorithm", who);
     if (algo == NVFP4_AR_LOWLAT && numel > h->ll_numel)
@@ -727,6 +807,20 @@ nvfp4_status_t nvfp4_ar_set_peers(nvfp4_ar_t h, void* const* bases) {
     return NVFP4_OK;
 }
 
+nvfp4_status_t nvfp4_ar_set_multicast(nvfp4_ar_t h, void* mc_base, void* uc_base, int64_t bytes) {
+    clear_error();
+    nvfp4_status_t st = check_ctx(h, "ar_set_multicast");
+    if (st) return st;
+    if (!mc_base || !uc_base || bytes < 32)
+        return fail(NVFP4_ERR_INVALID_ARG, "ar_set_multicast: need multicast and unicast addresses and >= 32 bytes");
+    if (!aligned16(mc_base) || !aligned16(uc_base))
+        return fail(NVFP4_ERR_INVALID_ARG, "ar_set_multicast: addresses must be 16-byte aligned");
+    h->nvls_mc = reinterpret_cast<uint8_t*>(mc_base);
+    h->nvls_uc = reinterpret_cast<uint8_t*>(uc_base);
+    h->nvls_half = (bytes / 2) & ~(int64_t)15;
+    return NVFP4_OK;
+}
+
 nvfp4_status_t nvfp4_ar_set_timeout(nvfp4_ar_t h, uint64_t timeout_ns) {
     clear_error();
     if (!h) return fail(NVFP4_ERR_INVALID_ARG, "ar_set_timeout: null context");
@@ -804,6 +898,12 @@ static nvfp4_status_t launch_nvfp4(nvfp4_ar_t h, const Params& p, bool twoshot, 
     else ar_nvfp4_kernel<false><<<grid, AR_THREADS, 0, s>>>(p);
     return check_launch("ar_nvfp4_kernel");
 }
+static nvfp4_status_t launch_bf16_nvls(nvfp4_ar_t h, Params p, cudaStream_t s) {
+    p.nvls_mc = h->nvls_mc + (int64_t)(p.epoch & 1u) * h->nvls_half;
+    p.nvls_uc = h->nvls_uc + (int64_t)(p.epoch & 1u) * h->nvls_half;
+    ar_bf16_nvls_kernel<<<grid_for(h, p.numel / p.world / 8), AR_THREADS, 0, s>>>(p);
+    return check_launch("ar_bf16_nvls_kernel");
+}
 static nvfp4_status_t launch_bf16(nvfp4_ar_t h, const Params& p, bool twoshot, cudaStream_t s) {
     const int64_t work = twoshot ? p.numel / p.world / 8 : p.numel / 8;
     const int grid = grid_for(h, work);
@@ -833,6 +933,7 @@ nvfp4_status_t nvfp4_ar_bf16_allreduce(nvfp4_ar_t h, const void* in, void* out, 
     if (st || numel == 0) return st;
     algo = resolve_algo(h, algo, numel, false);
     h->epoch++;
+    if (algo == NVFP4_AR_NVLS) return launch_bf16_nvls(h, make_params(h, in, out, numel, 0.0f, -1), (cudaStream_t)stream);
     return launch_bf16(h, make_params(h, in, out, numel, 0.0f, -1), algo == NVFP4_AR_TWOSHOT, (cudaStream_t)stream);
 }
 
@@ -934,6 +1035,8 @@ nvfp4_status_t nvfp4_ar_allreduce_emulated(nvfp4_ar_t const* handles, int world,
         if (handles[r]->world != world || handles[r]->rank != r || handles[r]->device != handles[0]->device)
             return fail(NVFP4_ERR_INVALID_ARG, "ar_allreduce_emulated: contexts must be ranks 0..%d of one device", world - 1);
     }
+    if (algo == NVFP4_AR_NVLS)
+        return fail(NVFP4_ERR_UNSUPPORTED, "ar_allreduce_emulated: NVFP4_AR_NVLS needs a multicast object across GPUs");
     if (numel == 0) return NVFP4_OK;
     if (!bf16_payload && (!(global_scale > 0.0f) || !isfinite(global_scale)))
         return fail(NVFP4_ERR_INVALID_ARG, "ar_allreduce_emulated: global_scale must be finite and > 0");

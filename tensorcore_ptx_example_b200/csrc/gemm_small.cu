@@ -69,10 +69,14 @@ constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 
 __host__ __device__ constexpr int stage_bytes(int mp) { return B_BOX + mp * 128 + SF_STAGE; }
 __host__ __device__ constexpr int ctas_per_sm(int mp) { return (GSMALL_CTAS_PER_SM == 2 && mp <= 64) ? 2 : 1; }
-__host__ __device__ constexpr int num_stages(int mp) {
-    return (ctas_per_sm(mp) == 2 ? SMEM_BUDGET_2 : SMEM_BUDGET_1) / stage_bytes(mp) < MAX_STAGES
-               ? (ctas_per_sm(mp) == 2 ? SMEM_BUDGET_2 : SMEM_BUDGET_1) / stage_bytes(mp)
-               : MAX_STAGES;
+// In-cluster reduction: a receive buffer for the partial rows this CTA sums, [split][mp][rows]
+// fp32 (128 x mp floats in all), after the stage ring.
+__host__ __device__ constexpr int recv_bytes(int mp) { return 128 * mp * 4; }
+__host__ __device__ constexpr int stage_budget(int mp, bool cl) {
+    return (ctas_per_sm(mp) == 2 ? SMEM_BUDGET_2 : SMEM_BUDGET_1) - (cl ? recv_bytes(mp) : 0);
+}
+__host__ __device__ constexpr int num_stages(int mp, bool cl = false) {
+    return stage_budget(mp, cl) / stage_bytes(mp) < MAX_STAGES ? stage_budget(mp, cl) / stage_bytes(mp) : MAX_STAGES;
 }
 // TMEM: accumulator buffers [0, mp) and [mp, 2 mp) (fp32 D^T tile, one column per output
 // column), then one 32-column scale slot per stage; the allocation is the next power of two.
@@ -87,15 +91,14 @@ __host__ __device__ constexpr int tmem_cols(int mp) {
 static_assert(sf_col0(128) + SF_SLOT_COLS * MAX_STAGES <= 512, "scale slots fit in TMEM");
 static_assert(ctas_per_sm(64) == 1 || (tmem_cols(64) <= 256 && tmem_cols(16) <= 256),
               "two CTAs per SM share the 512 TMEM columns");
-// [stages][full, empty, sf_landed per stage][acc_full 2][acc_empty 2][drain][ready][read][tmem slot]
-constexpr int NUM_BARS = 3 * MAX_STAGES + 7;
-__host__ __device__ constexpr int smem_bytes(int mp) {
-    return 1024 + num_stages(mp) * stage_bytes(mp) + NUM_BARS * 8 + 16;
+// [stages][receive buffer (in-cluster)][full, empty, sf_landed per stage][acc_full 2][acc_empty 2]
+// [drain][ready][tmem slot]
+constexpr int NUM_BARS = 3 * MAX_STAGES + 6;
+__host__ __device__ constexpr int smem_bytes(int mp, bool cl) {
+    return 1024 + num_stages(mp, cl) * stage_bytes(mp) + (cl ? recv_bytes(mp) : 0) + NUM_BARS * 8 + 16;
 }
-// The in-cluster reduction keeps a partial tile [Mp][128] fp32 in the drained stage ring.
-static_assert(128 * 16 * 4 <= 4 * stage_bytes(16) && 128 * 64 * 4 <= num_stages(64) * stage_bytes(64) &&
-                  128 * 128 * 4 <= num_stages(128) * stage_bytes(128),
-              "partial tile fits in the stage ring");
+static_assert(num_stages(16, true) == 4 && num_stages(64, true) >= 2 && num_stages(128, true) >= 2,
+              "stages left next to the receive buffer");
 constexpr int MAX_CLUSTER_SPLITS = 8;
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -108,10 +111,8 @@ __device__ __forceinline__ uint32_t mapa_rank(uint32_t addr, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
     return r;
 }
-__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-    return v;
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 // One arrival on the mbarrier at `addr` (this CTA's or a peer's, a shared::cluster address),
 // ordered after this thread's earlier memory operations at cluster scope.
@@ -179,17 +180,18 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
     const uint32_t base = (raw_addr + 1023u) & ~1023u;
     uint8_t* smem = smem_raw + (base - raw_addr);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int S = num_stages(mp), SB = stage_bytes(mp);
+    const int S = num_stages(mp, csplits > 0), SB = stage_bytes(mp);
     const int n_tiles = N / 128, splits = K / ks, units = n_tiles * splits;
     const int katoms = K / 64, nbox = ks / 256;
-    const uint32_t bar0 = base + S * SB;
+    const uint32_t recv0 = base + S * SB;                 // in-cluster receive buffer
+    const uint32_t bar0 = recv0 + (csplits > 0 ? recv_bytes(mp) : 0);
     auto full_bar = [&](int st) { return bar0 + 8u * st; };
     auto empty_bar = [&](int st) { return bar0 + 8u * (MAX_STAGES + st); };
     auto sf_landed = [&](int st) { return bar0 + 8u * (2 * MAX_STAGES + st); };
     const int acc_cols = mp, sf0 = sf_col0(mp), tcols = tmem_cols(mp);
     const uint32_t acc_full = bar0 + 8u * (3 * MAX_STAGES), acc_empty = acc_full + 16, drain = acc_full + 32;
-    const uint32_t ready_bar = acc_full + 40, read_bar = acc_full + 48;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S * SB + NUM_BARS * 8);
+    const uint32_t ready_bar = acc_full + 40;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar0 - base) + NUM_BARS * 8);
     uint32_t* abort_flag = tmem_slot + 1;       // the epilogue warps give up together
 
     if (warp == 0 && lane == 0) {
@@ -205,8 +207,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
             mbar_init(acc_empty + 8 * b, 4);           // the four epilogue warps
         }
         mbar_init(drain, 1);
-        mbar_init(ready_bar, csplits > 0 ? csplits : 1);   // one arrival per CTA of the cluster
-        mbar_init(read_bar, csplits > 0 ? csplits : 1);
+        mbar_init(ready_bar, csplits > 0 ? 4 * csplits : 1);   // each epilogue warp of every CTA
         *abort_flag = 0u;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -218,8 +219,10 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
         tc_fence_before();
     }
     __syncthreads();
-    // peers arrive on this CTA's barriers only after they are initialised
-    if (csplits > 0) asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    // Peers write into this CTA's receive buffer and arrive on its barrier only after it is
+    // initialised: every thread arrives on the cluster barrier here and waits on it only before
+    // its first access to a peer (the epilogue) or at exit.
+    if (csplits > 0) asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     // Programmatic dependent launch: the set-up above overlapped the previous kernel in the
@@ -359,49 +362,46 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
     } else if (csplits > 0) {
         // ------------------------------------------ epilogue, in-cluster reduction ----
         // One unit per CTA: split sp = this CTA's rank in the cluster, n-tile nt = cluster index.
+        // CTA r of the cluster owns rows [r * rows, (r + 1) * rows) of the n-tile: every CTA
+        // pushes its partial of those rows into CTA r's receive buffer (one-way stores to peer
+        // shared memory) and arrives on CTA r's "ready" barrier; CTA r then sums the partials in
+        // split order from its own shared memory and stores D.
         const uint32_t q = (uint32_t)(warp & 3);
         const int t = (int)threadIdx.x - 64;                  // 0..127 over the four epilogue warps
         const int sp = blockIdx.x % csplits, nt = blockIdx.x / csplits;
+        const int rows = 128 / csplits;
         const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(acc_full, 0u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_EPILOGUE));
         tc_fence_after();
-        // partial tile into this CTA's drained stage ring, [m][128 n] (every MMA that read the ring
-        // has completed: acc_full is their commit)
-        float* part = reinterpret_cast<float*>(smem);
+        asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");   // peers initialised
+        const int n = (int)q * 32 + lane;                     // TMEM lane = row n of the D^T tile
+        const int owner = n / rows, nn = n - owner * rows;
+        const uint32_t dst = mapa_rank(recv0, (uint32_t)owner) + (uint32_t)((sp * mp * rows + nn) * 4);
         if (ok) {
-            const int n = (int)q * 32 + lane;                 // TMEM lane = row n of the D^T tile
             for (int c = 0; c < mp; c += 16) {
                 uint32_t r[16];
                 tc_ld_x16(tmem + ((q * 32u) << 16) + c, r);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-                for (int i = 0; i < 16; i++) part[(c + i) * 128 + n] = __uint_as_float(r[i]);
+                for (int i = 0; i < 16; i++) st_cluster_f32(dst + (uint32_t)((c + i) * rows * 4), __uint_as_float(r[i]));
             }
         }
-        if (!ok && lane == 0) *abort_flag = 1u;
-        named_bar_sync(1, 128);
-        const bool wrote = *abort_flag == 0u;
-        if (t == 0 && wrote)
+        __syncwarp();
+        // (a warp that gave up arrives too, so no owner waits out its time limit; the status word
+        // already records the failure)
+        if (lane == 0)
             for (int r = 0; r < csplits; r++) mbar_arrive_cluster(mapa_rank(ready_bar, (uint32_t)r));
-        // every split's partial is in place: sum this CTA's rows in split order, store D
-        const bool ready = mbar_wait_cluster(ready_bar, 0u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_EPILOGUE);
-        if (ready) {
-            const int rows = 128 / csplits, n0 = sp * rows;
-            const uint32_t pbase = smem_u32(part);
+        if (mbar_wait_cluster(ready_bar, 0u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_EPILOGUE)) {
+            const float* recv = reinterpret_cast<const float*>(smem + (recv0 - base));
+            const int n0 = sp * rows;
             for (int i = t; i < rows * M; i += 128) {
-                const int m = i / rows, nn = n0 + i % rows;
-                const uint32_t off = pbase + (uint32_t)((m * 128 + nn) * 4);
+                const int m = i / rows, r0 = i - m * rows;
                 float acc = 0.0f;
-                for (int r = 0; r < csplits; r++) acc = __fadd_rn(acc, ld_cluster_f32(mapa_rank(off, (uint32_t)r)));
-                const int64_t o = (int64_t)m * N + (int64_t)nt * 128 + nn;
+                for (int s2 = 0; s2 < csplits; s2++) acc = __fadd_rn(acc, recv[(s2 * mp + m) * rows + r0]);
+                const int64_t o = (int64_t)m * N + (int64_t)nt * 128 + n0 + r0;
                 if (out_f32) reinterpret_cast<float*>(D)[o] = acc;
                 else reinterpret_cast<__nv_bfloat16*>(D)[o] = __float2bfloat16_rn(__fmul_rn(acc, alpha));
             }
         }
-        named_bar_sync(1, 128);
-        // this CTA has read every peer: tell them; then stay until every peer has read this one
-        if (t == 0)
-            for (int r = 0; r < csplits; r++) mbar_arrive_cluster(mapa_rank(read_bar, (uint32_t)r));
-        mbar_wait_cluster(read_bar, 0u, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_TEARDOWN);
     } else {
         // ------------------------------------------------ epilogue, workspace path ----
         const uint32_t q = (uint32_t)(warp & 3);
@@ -435,6 +435,8 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
     }
 
     __syncwarp();
+    // the threads that did not wait on the cluster barrier yet (all but the in-cluster epilogue)
+    if (csplits > 0 && !(warp >= 2 && warp < 6)) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -544,7 +546,8 @@ nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void*
         return st;
     if ((st = make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
-    const int smem = smem_bytes(mp);
+    const bool in_cluster = in_cluster_reduce(N, K);
+    const int smem = smem_bytes(mp, in_cluster);
     // the attribute is set once per device, to the largest footprint of any Mp
     static bool attr_set[64] = {};
     int dev = 0;
@@ -552,14 +555,14 @@ nvfp4_status_t launch(const void* A, const void* sfa, const void* B, const void*
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
         int most = 0;
         for (int m = 16; m <= 128; m += 16)
-            if (smem_bytes(m) > most) most = smem_bytes(m);
+            for (int cl = 0; cl < 2; cl++)
+                if (smem_bytes(m, cl) > most) most = smem_bytes(m, cl);
         cudaError_t e = cudaFuncSetAttribute(gemm_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
         if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "gemm (small M): smem attribute: %s", cudaGetErrorString(e));
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     const int units = (int)(N / 128) * splits;
     // in-cluster reduction: one CTA per unit, the S splits of an n-tile in one cluster
-    const bool in_cluster = in_cluster_reduce(N, K);
     const int grid = in_cluster ? units : persistent_grid(units, ctas_per_sm(mp) * sm_count());
     float* w = reinterpret_cast<float*>(ws);
     // Launched as a programmatic dependent of the previous work in the stream (and, in-cluster,

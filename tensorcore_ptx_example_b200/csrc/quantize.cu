@@ -39,13 +39,23 @@ __global__ void __launch_bounds__(QR_THREADS)
 quantize_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t cols, float gs_host,
                 const uint32_t* __restrict__ amax_word, float* __restrict__ gs_out, uint8_t* __restrict__ packed,
                 uint8_t* __restrict__ sf) {
-    float gs = gs_host, gs_inv;
-    if constexpr (kDevScale) {
-        global_scale_from_amax(__uint_as_float(*amax_word), gs, gs_inv);
-        if (blockIdx.x == 0 && threadIdx.x == 0 && gs_out) *gs_out = gs;
-    } else {
+    // Programmatic dependent launch.  Given scale: the input may come from the kernel before
+    // this one, so wait for it first.  Device scale: this kernel follows the amax kernel, whose
+    // input is the same x (complete before the amax kernel started); the first loads are issued
+    // before the wait and only the amax word is read after it.
+    float gs = gs_host, gs_inv = 0.0f;
+    bool have_scale = !kDevScale;
+    if constexpr (!kDevScale) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         gs_inv = __fdiv_rn(1.0f, gs);
     }
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    auto fetch_scale = [&]() {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        global_scale_from_amax(__uint_as_float(*reinterpret_cast<const volatile uint32_t*>(amax_word)), gs, gs_inv);
+        if (blockIdx.x == 0 && threadIdx.x == 0 && gs_out) *gs_out = gs;
+        have_scale = true;
+    };
     const int lane = threadIdx.x & 31;
     const int64_t katoms = cols / 64;
     const int64_t nblocks = rows * cols / 16;
@@ -75,6 +85,8 @@ quantize_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t cols,
                 for (int j = 0; j < 8; j++) raw[i][j] = 0u;
             }
         }
+        if constexpr (kDevScale)
+            if (!have_scale) fetch_scale();
 #pragma unroll
         for (int i = 0; i < QR_UNROLL; i++) {
             const int64_t b = b0 + i * step;
@@ -95,6 +107,8 @@ quantize_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t cols,
             if (col >= cols) { col -= cols; row++; }
         }
     }
+    if constexpr (kDevScale)
+        if (!have_scale) fetch_scale();
 }
 
 // Scale words of the padding rows of the last 128-row group (rows .. ceil(rows/128)*128 - 1):
@@ -179,6 +193,9 @@ __global__ void __launch_bounds__(AMAX_THREADS)
 amax_kernel(const uint8_t* __restrict__ x, int64_t numel, uint32_t* __restrict__ out) {
     constexpr int VB = kLoad32 ? 32 : 16;                  // bytes per load
     constexpr int VW = VB / 4;                             // words per load
+    // Launched as a programmatic dependent of amax_zero_kernel, which started only after all
+    // earlier work in the stream completed: x is ready; the zeroed output is waited for below.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int64_t nvec = numel * 2 / VB;
     const int64_t stride = (int64_t)gridDim.x * AMAX_THREADS;
     const int64_t first = (int64_t)blockIdx.x * AMAX_THREADS + threadIdx.x;
@@ -236,8 +253,33 @@ amax_kernel(const uint8_t* __restrict__ x, int64_t numel, uint32_t* __restrict__
     if (threadIdx.x < 32) {
         a = threadIdx.x < AMAX_THREADS / 32 ? warp_max[threadIdx.x] : 0u;
         a = __reduce_max_sync(0xFFFFFFFFu, a);
-        if (threadIdx.x == 0 && a != 0) atomicMax(out, a << 16);
+        if (threadIdx.x == 0) {
+            asm volatile("griddepcontrol.wait;" ::: "memory");      // the output word is zero
+            if (a != 0) atomicMax(out, a << 16);
+        }
     }
+}
+
+// Zeroes the amax word; the amax kernel is launched as its programmatic dependent, so its launch
+// and loads overlap this one-thread kernel instead of queueing behind a memset.
+__global__ void amax_zero_kernel(uint32_t* __restrict__ out) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (threadIdx.x == 0) *out = 0u;
+}
+
+// cudaLaunchKernelEx with programmatic stream serialization (no dynamic shared memory).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, cudaStream_t s, Args... args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(block, 1, 1);
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
 static int quant_grid(int64_t units) {
@@ -258,15 +300,15 @@ static nvfp4_status_t launch_quantize(const void* x, int64_t rows, int64_t cols,
     int64_t grid = (nblocks + per_cta - 1) / per_cta;
     if (grid > cap) grid = cap;
     if (grid < 1) grid = 1;
-    // 32-byte loads when the input allows them (16-byte alignment is the API's minimum)
-    if ((reinterpret_cast<uintptr_t>(x) & 31) == 0)
-        quantize_kernel<kDevScale, true><<<(unsigned)grid, QR_THREADS, 0, s>>>(
-            reinterpret_cast<const __nv_bfloat16*>(x), rows, cols, gs, amax_word, gs_out,
-            reinterpret_cast<uint8_t*>(packed), reinterpret_cast<uint8_t*>(sf));
-    else
-        quantize_kernel<kDevScale, false><<<(unsigned)grid, QR_THREADS, 0, s>>>(
-            reinterpret_cast<const __nv_bfloat16*>(x), rows, cols, gs, amax_word, gs_out,
-            reinterpret_cast<uint8_t*>(packed), reinterpret_cast<uint8_t*>(sf));
+    // 32-byte loads when the input allows them (16-byte alignment is the API's minimum); a
+    // programmatic dependent launch (the kernel waits before it reads what earlier work wrote)
+    const auto* xp = reinterpret_cast<const __nv_bfloat16*>(x);
+    auto* pp = reinterpret_cast<uint8_t*>(packed);
+    auto* sp = reinterpret_cast<uint8_t*>(sf);
+    const cudaError_t e = ((reinterpret_cast<uintptr_t>(x) & 31) == 0)
+        ? launch_pdl(quantize_kernel<kDevScale, true>, (unsigned)grid, QR_THREADS, s, xp, rows, cols, gs, amax_word, gs_out, pp, sp)
+        : launch_pdl(quantize_kernel<kDevScale, false>, (unsigned)grid, QR_THREADS, s, xp, rows, cols, gs, amax_word, gs_out, pp, sp);
+    if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "quantize_kernel: %s", cudaGetErrorString(e));
     nvfp4_status_t st = check_launch("quantize_kernel");
     if (st != NVFP4_OK || rows % 128 == 0) return st;
     sf_pad_kernel<<<64, 256, 0, s>>>(reinterpret_cast<uint8_t*>(sf), rows, cols);
@@ -274,19 +316,19 @@ static nvfp4_status_t launch_quantize(const void* x, int64_t rows, int64_t cols,
 }
 
 static nvfp4_status_t launch_amax(const void* x, int64_t numel, uint32_t* word, cudaStream_t s) {
-    cudaError_t e = cudaMemsetAsync(word, 0, sizeof(uint32_t), s);
-    if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "amax memset: %s", cudaGetErrorString(e));
-    if (numel == 0) return NVFP4_OK;
+    amax_zero_kernel<<<1, 32, 0, s>>>(word);
+    nvfp4_status_t st = check_launch("amax_zero_kernel");
+    if (st != NVFP4_OK || numel == 0) return st;
     const bool load32 = (reinterpret_cast<uintptr_t>(x) & 31) == 0;
     const int64_t per_cta = (int64_t)AMAX_THREADS * AMAX_UNROLL * (load32 ? 16 : 8);   // elements
     int64_t grid = (numel + per_cta - 1) / per_cta;
     const int64_t cap = (int64_t)sm_count() * 8;
     if (grid > cap) grid = cap;
     if (grid < 1) grid = 1;
-    if (load32)
-        amax_kernel<true><<<(unsigned)grid, AMAX_THREADS, 0, s>>>(reinterpret_cast<const uint8_t*>(x), numel, word);
-    else
-        amax_kernel<false><<<(unsigned)grid, AMAX_THREADS, 0, s>>>(reinterpret_cast<const uint8_t*>(x), numel, word);
+    const auto* xb = reinterpret_cast<const uint8_t*>(x);
+    const cudaError_t e = load32 ? launch_pdl(amax_kernel<true>, (unsigned)grid, AMAX_THREADS, s, xb, numel, word)
+                                 : launch_pdl(amax_kernel<false>, (unsigned)grid, AMAX_THREADS, s, xb, numel, word);
+    if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "amax_kernel: %s", cudaGetErrorString(e));
     return check_launch("amax_kernel");
 }
 

@@ -219,3 +219,75 @@ def test_multi_process_ipc_allreduce_bitexact(oracle):
         assert status == 0
         for algo in want:
             assert np.array_equal(outs[algo], want[algo]), (r, algo)
+
+
+def _nvls_worker(rank, world, port, numel, results):
+    """One rank of the in-switch (NVLS) bf16 all-reduce: torch symmetric memory binds every
+    rank's buffer to one NVLink multicast object; this library's kernel sums through it."""
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    ctx = None
+    try:
+        host = make_inputs(world, numel, seed0=31)
+        ctx = ar.AllReduce.from_process_group(numel)
+        if not ctx.enable_nvls():
+            results[rank] = ("no multicast", None, None, 0)
+            return
+        x = host[rank].cuda()
+        outs = []
+        for rep in range(3):                         # repeated calls: both halves of the buffer
+            o = ctx.bf16_allreduce(x, algo="nvls")
+            torch.cuda.synchronize()
+            outs.append(u16(o))
+        p2p = u16(ctx.bf16_allreduce(x, algo="twoshot"))
+        torch.cuda.synchronize()
+        import tensorcore_ptx_example_b200 as nv
+        results[rank] = ("ok", outs, p2p, nv.device_status())
+        dist.barrier()
+    finally:
+        if ctx is not None:
+            torch.cuda.synchronize()
+            ctx.close()
+        dist.destroy_process_group()
+
+
+@needs2
+def test_nvls_bf16_allreduce_within_tolerance(oracle):
+    """NVFP4_AR_NVLS on live ranks: every rank gets the same bf16 tensor, within 1 bf16 ulp of the
+    exact sum rounded once (the switch orders the fp32 additions), identical across repeated calls,
+    and equal to this library's fixed-order peer-to-peer sum except where the two fp32 orders
+    round to neighbouring bf16 values.  No rank leaves while its buffer is bound."""
+    import torch.multiprocessing as mp
+    world = min(ngpus(), 8)
+    numel = 8 * world * 4099
+    port = _free_port()
+    with mp.get_context("spawn").Manager() as m:
+        results = m.dict()
+        mp.spawn(_nvls_worker, args=(world, port, numel, results), nprocs=world, join=True)
+        res = dict(results)
+    if res[0][0] == "no multicast":
+        pytest.skip("this GPU / driver offers no NVLink multicast")
+    host = make_inputs(world, numel, seed0=31)
+    exact = oracle.sum_f64([u16(x) for x in host])
+    want_rn = oracle.f32_to_bf16(exact.astype(np.float32))      # exact sum rounded once (via fp32)
+    ref_p2p = oracle.ar_bf16([u16(x) for x in host])
+    b2f = oracle.bf16_to_f32
+    for r in range(world):
+        tag, outs, p2p, status = res[r]
+        assert tag == "ok" and status == 0
+        assert np.array_equal(p2p, ref_p2p)                      # the P2P path stays bit-exact
+        for o in outs:
+            assert np.array_equal(o, outs[0])                    # deterministic call to call
+            assert np.array_equal(o, res[0][1][0])               # same on every rank
+        got = b2f(outs[0]).astype(np.float64)
+        ulp = np.abs(b2f(want_rn).astype(np.float64)) * 2.0 ** -7
+        err = np.abs(got - exact)
+        assert np.all(err <= np.maximum(ulp, 2.0 ** -133)), float((err / np.maximum(ulp, 1e-30)).max())
+        assert np.mean(outs[0] != want_rn) < 0.01
