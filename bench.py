@@ -701,6 +701,7 @@ def _ar_time(fn, steps, warmup, flush, world):
         fn()
     torch.cuda.synchronize()
     barrier(world)
+    fn()                      # untimed: its own barrier lines up the GPUs' timelines
     ts = timed_steps(fn, steps, flush)
     barrier(world)
     return max_over_ranks(sum(ts) / len(ts), world)
@@ -1041,11 +1042,13 @@ def run_allreduce_line(args):
         fn = lambda: ctx.allreduce(x, out, global_scale=gs, algo="auto")  # noqa: E731
         for _ in range(args.warmup):
             fn()
-        torch.cuda.synchronize()
-        barrier(world)
-        torch.cuda.synchronize()
+        # the sampler starts first (its NVML set-up takes a varying while on each rank); the
+        # barrier right before the timed steps lines the ranks up
         sampler = ClockSampler(local)
         sampler.start()
+        torch.cuda.synchronize()
+        barrier(world)
+        fn()                  # untimed: its own barrier lines up the GPUs' timelines
         ts = timed_steps(fn, args.steps, flush)
         clocks = sampler.stop()
         barrier(world)
@@ -1297,13 +1300,28 @@ def run_only(args):
     flush = L2Flush()
     if args.only == "quantize":
         out = quantize_bench(nv, args.steps, args.warmup, flush)
+        # and the dequantizer over the same shape (cfg2 round trip)
+        from tensorcore_ptx_example_b200 import workloads
+        rows, cols = workloads.CFG2_SHAPE
+        x = workloads.activations(rows, cols, seed=2)
+        gs = float(nv.amax(x).item()) / 2688.0
+        packed, sf, _ = nv.quantize(x, gs)
+        y = torch.empty_like(x)
+        for _ in range(args.warmup):
+            nv.dequantize(packed, sf, rows, cols, gs, out=y)
+        ts = timed_steps(lambda: nv.dequantize(packed, sf, rows, cols, gs, out=y), args.steps, flush)
+        ms = sum(ts) / len(ts)
+        out["dequantize_us"] = round(ms * 1e3, 2)
+        out["dequantize_gbs"] = round(rows * cols * 2.5625 / (ms * 1e-3) / 1e9, 1)
     elif args.only == "gemm-decode":
         out = decode_bench(nv, args.steps, args.warmup, flush)
     elif args.only == "gemm-quantize":
         out = gemm_quantize_bench(nv, args.steps, flush)
     elif args.only == "ar-emulated":
         # the all-reduce data path of 8 ranks on this one GPU, phase by phase (no cross-GPU
-        # waits): for profiling the phase kernels' memory traffic on a single device
+        # waits): for profiling the phase kernels' memory traffic on a single device.  NVFP4
+        # two-shot and one-shot, the low-latency one-shot (on its 1 MB cap), bf16 two-shot and
+        # one-shot, in that order.
         from tensorcore_ptx_example_b200 import allreduce as ar
         from tensorcore_ptx_example_b200 import workloads
         world, numel = 8, args.numel
@@ -1311,14 +1329,40 @@ def run_only(args):
         gs = nv.global_scale_from_amax(max(float(nv.amax(x).item()) for x in ins))
         ctxs = [ar.AllReduce(world, r, numel) for r in range(world)]
         ar.join_in_process(ctxs)
-        for algo in ("twoshot", "oneshot"):
+        ll = min(numel, ar.LOWLAT_CAP_BYTES // 2)
+        for algo, bf16, n in (("twoshot", False, numel), ("oneshot", False, numel), ("lowlat", False, ll),
+                              ("twoshot", True, numel), ("oneshot", True, numel)):
             for _ in range(args.warmup + args.steps):
-                ar.emulated_allreduce(ins, gs, algo, contexts=ctxs)
+                ar.emulated_allreduce([x[:n] for x in ins], gs, algo, bf16=bf16, contexts=ctxs)
         torch.cuda.synchronize()
         for c in ctxs:
             c.close()
         out = {"workload": f"emulated 8-rank all-reduce, {numel} elements per rank", "launches_per_call":
-               "twoshot 3 phases x 8 ranks, oneshot 2 phases x 8 ranks"}
+               "nvfp4 twoshot 3 phases x 8 ranks, oneshot 2 x 8, lowlat 2 x 8, then bf16 twoshot / oneshot"}
+    elif args.only == "gemm-ar-emulated":
+        # the row-parallel GEMM + two-shot of 2 ranks on this one GPU (cfg4 output, K 4096 per
+        # rank): gemm2_kernel with the payload epilogue, then the all-reduce phases
+        from tensorcore_ptx_example_b200 import allreduce as ar
+        from tensorcore_ptx_example_b200 import workloads
+        world = 2
+        M, N = workloads.CFG4_SHAPE
+        K = 8192 // world
+        ops, alphas, ds = [], [], []
+        for r in range(world):
+            pa, sa, gsa = nv.quantize(workloads.activations(M, K, seed=11 + 2 * r), None)
+            pb, sb, gsb = nv.quantize(workloads.gaussian(N, K, seed=12 + 2 * r, std=0.02), None)
+            ops.append((pa, sa, pb, sb))
+            alphas.append(float(gsa.item()) * float(gsb.item()))
+            ds.append(nv.gemm(pa, sa, pb, sb, M, N, K, alpha=alphas[-1]))
+        gs = nv.global_scale_from_amax(max(float(d.float().abs().max()) for d in ds))
+        ctxs = [ar.AllReduce(world, r, M * N) for r in range(world)]
+        ar.join_in_process(ctxs)
+        for _ in range(args.warmup + args.steps):
+            ar.emulated_gemm_allreduce(ops, M, N, K, alphas, gs, ctxs)
+        torch.cuda.synchronize()
+        for c in ctxs:
+            c.close()
+        out = {"workload": f"emulated 2-rank row-parallel GEMM M{M} N{N} K{K} per rank + two-shot"}
     else:
         pa, sa, pb, sb, alpha, d = gemm_setup(nv, 0)
         fn = lambda: nv.gemm(pa, sa, pb, sb, M_, N_, K_, alpha=alpha, out=d)  # noqa: E731
@@ -1341,7 +1385,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--numel", type=int, default=4 << 20, help="elements per rank for --only ar-emulated")
-    ap.add_argument("--only", choices=["gemm", "gemm-decode", "gemm-quantize", "quantize", "ar-sweep", "ar-emulated"],
+    ap.add_argument("--only", choices=["gemm", "gemm-decode", "gemm-quantize", "quantize", "ar-sweep", "ar-emulated",
+                                       "gemm-ar-emulated"],
                     default=None,
                     help="profiling mode: run one workload (warmup + steps launches) and print its "
                          "timings; not the benchmark line")

@@ -98,7 +98,7 @@ class AllReduce:
         nbytes = 2 * ((self.max_numel * 2 + 15) // 16 * 16)
         buf = symm.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", self.device))
         hdl = symm.rendezvous(buf, group)
-        mc = int(hdl.multicast_ptr) if hdl.has_multicast_support() else 0
+        mc = int(hdl.multicast_ptr or 0)         # 0 when the device offers no NVLink multicast
         backend = dist.get_backend(group)
         dev = torch.device("cuda", self.device) if backend == "nccl" else torch.device("cpu")
         ok = torch.tensor([1 if mc else 0], dtype=torch.int32, device=dev)

@@ -518,7 +518,9 @@ __device__ __forceinline__ void multimem_st_bf16x8(uint8_t* mc, uint4 v) {
 // other: order the accesses across the two aliases.
 __device__ __forceinline__ void fence_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
 
-__global__ void __launch_bounds__(AR_THREADS) ar_bf16_nvls_kernel(const Params p) {
+constexpr int NVLS_UNROLL = 3;               // chunks in flight per thread in every phase (no spills at 2 blocks per SM)
+
+__global__ void __launch_bounds__(AR_THREADS, 2) ar_bf16_nvls_kernel(const Params p) {
     const int n = p.world, me = p.rank;
     const uint32_t v1 = p.epoch * 2u + 1u, v2 = p.epoch * 2u + 2u;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -527,30 +529,67 @@ __global__ void __launch_bounds__(AR_THREADS) ar_bf16_nvls_kernel(const Params p
     uint8_t* out = reinterpret_cast<uint8_t*>(p.out);
     const int64_t shard = p.numel / n;                 // elements
     const int64_t schunks = shard / 8;                 // 16-byte chunks of one shard
+    // Every phase walks this block's chunks of a shard (c = first, first + stride, ...) with
+    // NVLS_UNROLL of them loaded before any is stored: a load through the switch takes
+    // microseconds, and one at a time per thread would leave the links idle.
     // A: this rank's input into its buffer -- the chunks of every shard that block b of any rank
     // reduces in B, so that B only needs block b of every rank to have finished A
-    for (int64_t c = first; c < schunks; c += stride)
-        for (int q = 0; q < n; q++) {
-            const int64_t off = ((int64_t)q * shard) * 2 + c * 16;
-            st_v4(p.nvls_uc + off, ld_nc_v4(in + off));
+    for (int q = 0; q < n; q++) {
+        const int64_t base = ((int64_t)q * shard) * 2;
+        for (int64_t c0 = first; c0 < schunks; c0 += stride * NVLS_UNROLL) {
+            uint4 v[NVLS_UNROLL];
+#pragma unroll
+            for (int u = 0; u < NVLS_UNROLL; u++) {
+                const int64_t c = c0 + u * stride;
+                if (c < schunks) v[u] = ld_nc_v4(in + base + c * 16);
+            }
+#pragma unroll
+            for (int u = 0; u < NVLS_UNROLL; u++) {
+                const int64_t c = c0 + u * stride;
+                if (c < schunks) st_v4(p.nvls_uc + base + c * 16, v[u]);
+            }
         }
+    }
     fence_alias();
     if (!block_barrier(p, v1)) return;
     fence_alias();
     // B: the in-switch sum of this rank's shard, written back to every rank
-    for (int64_t c = first; c < schunks; c += stride) {
-        uint8_t* a = p.nvls_mc + ((int64_t)me * shard) * 2 + c * 16;
-        multimem_st_bf16x8(a, multimem_ld_reduce_bf16x8(a));
+    {
+        uint8_t* mine = p.nvls_mc + ((int64_t)me * shard) * 2;
+        for (int64_t c0 = first; c0 < schunks; c0 += stride * NVLS_UNROLL) {
+            uint4 v[NVLS_UNROLL];
+#pragma unroll
+            for (int u = 0; u < NVLS_UNROLL; u++) {
+                const int64_t c = c0 + u * stride;
+                if (c < schunks) v[u] = multimem_ld_reduce_bf16x8(mine + c * 16);
+            }
+#pragma unroll
+            for (int u = 0; u < NVLS_UNROLL; u++) {
+                const int64_t c = c0 + u * stride;
+                if (c < schunks) multimem_st_bf16x8(mine + c * 16, v[u]);
+            }
+        }
     }
     fence_alias();
     if (!block_barrier(p, v2)) return;
     fence_alias();
     // C: the reduced tensor out of this rank's buffer
-    for (int64_t c = first; c < schunks; c += stride)
-        for (int q = 0; q < n; q++) {
-            const int64_t off = ((int64_t)q * shard) * 2 + c * 16;
-            st_v4(out + off, ld_cg_v4(p.nvls_uc + off));
+    for (int q = 0; q < n; q++) {
+        const int64_t base = ((int64_t)q * shard) * 2;
+        for (int64_t c0 = first; c0 < schunks; c0 += stride * NVLS_UNROLL) {
+            uint4 v[NVLS_UNROLL];
+#pragma unroll
+            for (int u = 0; u < NVLS_UNROLL; u++) {
+                const int64_t c = c0 + u * stride;
+                if (c < schunks) v[u] = ld_cg_v4(p.nvls_uc + base + c * 16);
+            }
+#pragma unroll
+            for (int u = 0; u < NVLS_UNROLL; u++) {
+                const int64_t c = c0 + u * stride;
+                if (c < schunks) st_v4(out + base + c * 16, v[u]);
+            }
         }
+    }
 }
 
 }  // namespace ar
@@ -700,10 +739,12 @@ nvfp4_status_t nvfp4_ar_create(int world, int rank, int64_t max_numel, nvfp4_ar_
     }
     int g1 = resident_grid((const void*)ar_nvfp4_kernel<true>), g2 = resident_grid((const void*)ar_nvfp4_kernel<false>);
     int g3 = resident_grid((const void*)ar_bf16_kernel<true>), g4 = resident_grid((const void*)ar_bf16_kernel<false>);
+    const int g5 = resident_grid((const void*)ar_bf16_nvls_kernel);
     int g = g1;
     if (g2 < g) g = g2;
     if (g3 < g) g = g3;
     if (g4 < g) g = g4;
+    if (g5 < g) g = g5;   // every kernel that meets peers in block barriers keeps all its blocks resident
     h->max_grid = g;
     h->ll_max_grid = resident_grid((const void*)ar_nvfp4_ll_kernel, AR_LL_THREADS);
     h->peer[rank] = h->base;
@@ -901,7 +942,7 @@ static nvfp4_status_t launch_nvfp4(nvfp4_ar_t h, const Params& p, bool twoshot, 
 static nvfp4_status_t launch_bf16_nvls(nvfp4_ar_t h, Params p, cudaStream_t s) {
     p.nvls_mc = h->nvls_mc + (int64_t)(p.epoch & 1u) * h->nvls_half;
     p.nvls_uc = h->nvls_uc + (int64_t)(p.epoch & 1u) * h->nvls_half;
-    ar_bf16_nvls_kernel<<<grid_for(h, p.numel / p.world / 8), AR_THREADS, 0, s>>>(p);
+    ar_bf16_nvls_kernel<<<grid_for(h, (p.numel / p.world / 8 + NVLS_UNROLL - 1) / NVLS_UNROLL), AR_THREADS, 0, s>>>(p);
     return check_launch("ar_bf16_nvls_kernel");
 }
 static nvfp4_status_t launch_bf16(nvfp4_ar_t h, const Params& p, bool twoshot, cudaStream_t s) {
