@@ -1183,9 +1183,10 @@ def gemm_allreduce_bench(nv, world, rank, args, flush=None):
 
 
 def allreduce_sweep(args):
-    """cfg5: 16 KB .. 256 MB of bf16 per rank (doubling), NVFP4 low-latency one-shot (up to
-    1 MB) / one-shot / two-shot and bf16 one-shot / two-shot, max over ranks of the mean device
-    time per call over back-to-back calls."""
+    """cfg5: 16 KB .. 256 MB of bf16 per rank (doubling): NVFP4 low-latency one-shot (up to 1 MB),
+    one-shot and two-shot against the bf16 one-shot, two-shot and (where the GPUs offer NVLink
+    multicast) in-switch NVLS all-reduce; max over ranks of the mean device time per call over
+    back-to-back calls."""
     import torch
 
     import tensorcore_ptx_example_b200 as nv
@@ -1195,29 +1196,12 @@ def allreduce_sweep(args):
     sizes = [b for b in workloads.sweep_sizes_bytes() if (b // 2) % (32 * world) == 0]
     max_numel = max(sizes) // 2
     ctx = ar.AllReduce.from_process_group(max_numel)
-    xfull = workloads.gaussian(1, max_numel, seed=rank).view(-1)
-    gs = ar.agree_global_scale(float(nv.amax(xfull).item()))
-    ofull = torch.empty_like(xfull)
-    rows = []
     try:
-        for b in sizes:
-            n = b // 2
-            x, o = xfull[:n], ofull[:n]
-            calls = 50 if b <= (16 << 20) else 10
-            row = {"bytes": b, "numel": n}
-            algos = [
-                ("nvfp4_lowlat", lambda: ctx.allreduce(x, o, global_scale=gs, algo="lowlat"), 0.75),
-                ("nvfp4_oneshot", lambda: ctx.allreduce(x, o, global_scale=gs, algo="oneshot"), 0.5625),
-                ("nvfp4_twoshot", lambda: ctx.allreduce(x, o, global_scale=gs, algo="twoshot"), 0.5625),
-                ("bf16_oneshot", lambda: ctx.bf16_allreduce(x, o, algo="oneshot"), 2.0),
-                ("bf16_twoshot", lambda: ctx.bf16_allreduce(x, o, algo="twoshot"), 2.0)]
-            if b > ar.LOWLAT_CAP_BYTES:
-                algos = algos[1:]
-            for name, fn, bpe in algos:
-                ms = _ar_time_b2b(fn, calls, 3, world)
-                e = _ar_entry(name, n, world, ms, bpe)
-                row[name] = {"us": e["us"], "algbw_gbs": e["algbw_gbs"], "busbw_gbs": e["busbw_gbs"]}
-            rows.append(row)
+        nvls = ctx.enable_nvls()
+        xfull = workloads.gaussian(1, max_numel, seed=rank).view(-1)
+        gs = ar.agree_global_scale(float(nv.amax(xfull).item()))
+        ofull = torch.empty_like(xfull)
+        rows = ar_sweep_rows(ctx, xfull, ofull, gs, world, sizes=sizes, nvls=nvls)
         torch.cuda.synchronize()
         status = nv.device_status()
     finally:
@@ -1225,7 +1209,7 @@ def allreduce_sweep(args):
         ctx.close()
     if rank == 0:
         print(json.dumps({"sweep": "cfg5 all-reduce message sizes", "world": world, "device_status": status,
-                          "l2": "not flushed (back-to-back calls)", "rows": rows}), flush=True)
+                          "nvls": nvls, "l2": "not flushed (back-to-back calls)", "rows": rows}), flush=True)
     import torch.distributed as dist
     if world > 1:
         dist.destroy_process_group()
