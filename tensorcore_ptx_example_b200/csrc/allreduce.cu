@@ -354,31 +354,12 @@ __device__ __forceinline__ void ll_put(uint64_t* slot, int64_t chunks, int64_t c
 #pragma unroll
     for (int i = 0; i < AR_LL_WORDS; i++) st_relaxed_sys_u64(slot + i * chunks + c, w[i]);
 }
-// Waits (bounded) until every word of chunk c is tagged, then zeroes the words; false if the
-// wait ran out.
-__device__ __forceinline__ bool ll_get(uint64_t* slot, int64_t chunks, int64_t c, uint64_t timeout_ns, uint4& pk,
-                                       uint32_t& sc) {
-    uint64_t v[AR_LL_WORDS];
-    int spins = 0;
-    uint64_t t0 = 0;
-    for (;;) {
-        bool ready = true;
-#pragma unroll
-        for (int i = 0; i < AR_LL_WORDS; i++) {
-            v[i] = ld_relaxed_sys_u64(slot + i * chunks + c);
-            ready &= v[i] >= AR_LL_TAG;
-        }
-        if (ready) break;
-        if (++spins == 64) t0 = globaltimer_ns();
-        if (spins > 64 && (spins & 63) == 0 && globaltimer_ns() - t0 > timeout_ns) return false;
-    }
-#pragma unroll
-    for (int i = 0; i < AR_LL_WORDS; i++) slot[i * chunks + c] = 0;
-    const uint64_t lo = (v[0] & AR_LL_M56) | (v[1] << 56);
-    const uint64_t hi = ((v[1] & AR_LL_M56) >> 8) | (v[2] << 48);
+// The 144 payload bits of one chunk from its three tagged words (inverse of ll_put).
+__device__ __forceinline__ void ll_unpack(uint64_t w0, uint64_t w1, uint64_t w2, uint4& pk, uint32_t& sc) {
+    const uint64_t lo = (w0 & AR_LL_M56) | (w1 << 56);
+    const uint64_t hi = ((w1 & AR_LL_M56) >> 8) | (w2 << 48);
     pk = make_uint4((uint32_t)lo, (uint32_t)(lo >> 32), (uint32_t)hi, (uint32_t)(hi >> 32));
-    sc = (uint32_t)(v[2] >> 16) & 0xFFFFu;
-    return true;
+    sc = (uint32_t)(w2 >> 16) & 0xFFFFu;
 }
 
 // One-shot with the data-carried flags: A: quantize each chunk and push it to every peer;
@@ -404,18 +385,50 @@ __global__ void __launch_bounds__(AR_LL_THREADS) ar_nvfp4_ll_kernel(const Params
     }
     if (p.phase == -1 || p.phase == 1) {
         for (int64_t c = first; c < chunks; c += stride) {
-            float acc[32];
+            // every peer's three words of chunk c are loaded before any is checked (one round
+            // trip for all peers, not one per peer); only untagged words are loaded again
+            uint64_t w[AR_MAX_WORLD][AR_LL_WORDS];
 #pragma unroll
-            for (int i = 0; i < 32; i++) acc[i] = 0.0f;
-            for (int s = 0; s < n; s++) {                      // fixed sum order 0 .. n-1
-                uint4 pk;
-                uint32_t sc;
-                if (s == me) {
-                    quant32(p.in + c * 32, gs_inv, pk, sc);
-                } else if (!ll_get(ll_slot_of(p, me, s), chunks, c, p.timeout_ns, pk, sc)) {
+            for (int s = 0; s < AR_MAX_WORLD; s++)
+#pragma unroll
+                for (int i = 0; i < AR_LL_WORDS; i++)
+                    w[s][i] = (s < n && s != me) ? ld_relaxed_sys_u64(ll_slot_of(p, me, s) + i * chunks + c) : AR_LL_TAG;
+            int spins = 0;
+            uint64_t t0 = 0;
+            for (;;) {
+                bool ready = true;
+#pragma unroll
+                for (int s = 0; s < AR_MAX_WORLD; s++)
+#pragma unroll
+                    for (int i = 0; i < AR_LL_WORDS; i++) ready &= w[s][i] >= AR_LL_TAG;
+                if (ready) break;
+                if (++spins == 64) t0 = globaltimer_ns();
+                if (spins > 64 && (spins & 63) == 0 && globaltimer_ns() - t0 > p.timeout_ns) {
                     record_error(DEV_TIMEOUT_AR_BARRIER);
                     return;
                 }
+#pragma unroll
+                for (int s = 0; s < AR_MAX_WORLD; s++)
+#pragma unroll
+                    for (int i = 0; i < AR_LL_WORDS; i++)
+                        if (w[s][i] < AR_LL_TAG) w[s][i] = ld_relaxed_sys_u64(ll_slot_of(p, me, s) + i * chunks + c);
+            }
+            // consumed: zero the words, so the next call of this parity starts from an empty area
+#pragma unroll
+            for (int s = 0; s < AR_MAX_WORLD; s++)
+                if (s < n && s != me)
+#pragma unroll
+                    for (int i = 0; i < AR_LL_WORDS; i++) ll_slot_of(p, me, s)[i * chunks + c] = 0;
+            float acc[32];
+#pragma unroll
+            for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+#pragma unroll
+            for (int s = 0; s < AR_MAX_WORLD; s++) {              // fixed sum order 0 .. n-1
+                if (s >= n) break;
+                uint4 pk;
+                uint32_t sc;
+                if (s == me) quant32(p.in + c * 32, gs_inv, pk, sc);   // the same bits as the pushed chunk
+                else ll_unpack(w[s][0], w[s][1], w[s][2], pk, sc);
                 dq32_acc(pk, sc, p.gs, acc);
             }
             store_bf16x32(p.out + c * 32, acc);

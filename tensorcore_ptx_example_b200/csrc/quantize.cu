@@ -24,7 +24,6 @@
 
 namespace nvfp4 {
 
-constexpr int QTHREADS = 128;                 // dequantizer CTA
 constexpr int QR_THREADS = 256;               // quantizer CTA
 #ifndef QUANT_UNROLL
 #define QUANT_UNROLL 2
@@ -125,41 +124,67 @@ __global__ void sf_pad_kernel(uint8_t* __restrict__ sf, int64_t rows, int64_t co
     }
 }
 
-// Dequantize: same ownership as the quantizer; 32 packed bytes + one scale word in,
-// 64 bf16 out.  value = e2m1 * (e4m3(scale) * gs), one rounding for each product.
-__global__ void __launch_bounds__(QTHREADS)
-dequantize_kernel(const uint8_t* __restrict__ packed, const uint32_t* __restrict__ sf_words,
-                  int64_t rows, int64_t cols, float gs, __nv_bfloat16* __restrict__ out,
-                  int64_t units) {
+// Dequantize (the cfg2 round trip): the quantizer's flat sweep in reverse, one 16-element block
+// per thread and DQ_UNROLL blocks in flight: lane l of a warp reads bytes [8 l, 8 l + 8) of a
+// 256-byte stretch of codes and writes 32 contiguous bytes of bf16, so a warp reads and writes
+// contiguous memory; the four lanes of one row's 64-column group read the same scale word (one
+// transaction) and take their byte of it.  HBM-bound: 0.5625 B/elt read, 2 B/elt written.
+//   value = bf16(e2m1 * (e4m3(scale) * gs)), one rounding for each product.
+constexpr int DQ_THREADS = 256;
+constexpr int DQ_UNROLL = 4;
+
+__global__ void __launch_bounds__(DQ_THREADS)
+dequantize_kernel(const uint8_t* __restrict__ packed, const uint8_t* __restrict__ sf, int64_t rows, int64_t cols,
+                  float gs, __nv_bfloat16* __restrict__ out) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int64_t katoms = cols / 64;
-    const int t = threadIdx.x;
-    const int r_in_atom = (t & 3) * 32 + (t >> 2);
+    const int64_t nblocks = rows * cols / 16;
+    const int64_t step = (int64_t)gridDim.x * DQ_THREADS;
+    const int64_t e_step = step * 16;
+    const int64_t dr = e_step / cols, dc = e_step - dr * cols;
+    int64_t b0 = (int64_t)blockIdx.x * DQ_THREADS + threadIdx.x;
+    int64_t row = (b0 * 16) / cols, col = b0 * 16 - row * cols;
 #pragma unroll 1
-    for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
-        const int64_t rg = u / katoms, kg = u - rg * katoms;
-        const int64_t row = rg * 128 + r_in_atom;
-        if (row >= rows) continue;
-        const uint32_t word = sf_words[u * 128 + t];
-        const uint8_t* src = packed + row * (cols / 2) + kg * 32;
-        const uint4 p0 = ld_nc_v4(src), p1 = ld_nc_v4(src + 16);
-        const uint32_t nib[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-        uint8_t* dst = reinterpret_cast<uint8_t*>(out + row * cols + kg * 64);
+    for (; b0 < nblocks; b0 += step * DQ_UNROLL) {
+        uint2 code[DQ_UNROLL];
+        uint32_t word[DQ_UNROLL];
+        int64_t c[DQ_UNROLL];
 #pragma unroll
-        for (int b = 0; b < 4; b++) {
-            const float bs = __fmul_rn(e4m3_decode((word >> (8 * b)) & 0xFFu), gs);
+        for (int i = 0; i < DQ_UNROLL; i++) {
+            const int64_t b = b0 + i * step;
+            c[i] = col;
+            if (b < nblocks) {
+                asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
+                             : "=r"(code[i].x), "=r"(code[i].y)
+                             : "l"(packed + b * 8));
+                const int64_t off = ((row >> 7) * katoms + (col >> 6)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4;
+                word[i] = __ldg(reinterpret_cast<const uint32_t*>(sf + off));
+            }
+            row += dr;
+            col += dc;
+            if (col >= cols) { col -= cols; row++; }
+        }
+#pragma unroll
+        for (int i = 0; i < DQ_UNROLL; i++) {
+            const int64_t b = b0 + i * step;
+            if (b >= nblocks) break;
+            const uint32_t kb = (uint32_t)(c[i] >> 4) & 3u;
+            const float bs = __fmul_rn(e4m3_decode((word[i] >> (8 * kb)) & 0xFFu), gs);
+            uint32_t o[8];
 #pragma unroll
             for (int h = 0; h < 2; h++) {
                 float v[8];
-                e2m1x8_decode(nib[2 * b + h], v);
-                uint32_t o[4];
+                e2m1x8_decode(h ? code[i].y : code[i].x, v);
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
-                    const __nv_bfloat162 pr =
-                        __floats2bfloat162_rn(__fmul_rn(v[2 * j], bs), __fmul_rn(v[2 * j + 1], bs));
-                    o[j] = *reinterpret_cast<const uint32_t*>(&pr);
+                    const __nv_bfloat162 pr = __floats2bfloat162_rn(__fmul_rn(v[2 * j], bs), __fmul_rn(v[2 * j + 1], bs));
+                    o[4 * h + j] = *reinterpret_cast<const uint32_t*>(&pr);
                 }
-                st_v4(dst + (2 * b + h) * 16, make_uint4(o[0], o[1], o[2], o[3]));
             }
+            uint8_t* dst = reinterpret_cast<uint8_t*>(out) + b * 32;
+            st_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
+            st_v4(dst + 16, make_uint4(o[4], o[5], o[6], o[7]));
         }
     }
 }
@@ -282,11 +307,6 @@ static cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned 
     return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
-static int quant_grid(int64_t units) {
-    const int64_t cap = (int64_t)sm_count() * 16;
-    return (int)(units < cap ? units : cap);
-}
-
 // Launch the quantizer (kDevScale: the global scale comes from *amax_word).
 template <bool kDevScale>
 static nvfp4_status_t launch_quantize(const void* x, int64_t rows, int64_t cols, float gs, const uint32_t* amax_word,
@@ -389,11 +409,15 @@ nvfp4_status_t nvfp4_dequantize_bf16(const void* packed, const void* sf, int64_t
     clear_error();
     nvfp4_status_t st = check_quant_args("dequantize", out, rows, cols, packed, sf);
     if (st != NVFP4_OK) return st;
-    const int64_t units = ((rows + 127) / 128) * (cols / 64);
-    if (units == 0) return NVFP4_OK;
-    dequantize_kernel<<<quant_grid(units), QTHREADS, 0, (cudaStream_t)stream>>>(
-        reinterpret_cast<const uint8_t*>(packed), reinterpret_cast<const uint32_t*>(sf), rows, cols,
-        global_scale, reinterpret_cast<__nv_bfloat16*>(out), units);
+    const int64_t nblocks = rows * cols / 16;
+    if (nblocks == 0) return NVFP4_OK;
+    int64_t grid = (nblocks + (int64_t)DQ_THREADS * DQ_UNROLL - 1) / ((int64_t)DQ_THREADS * DQ_UNROLL);
+    const int64_t cap = (int64_t)sm_count() * 8;
+    if (grid > cap) grid = cap;
+    const cudaError_t e = launch_pdl(dequantize_kernel, (unsigned)grid, DQ_THREADS, (cudaStream_t)stream,
+                                     reinterpret_cast<const uint8_t*>(packed), reinterpret_cast<const uint8_t*>(sf),
+                                     rows, cols, global_scale, reinterpret_cast<__nv_bfloat16*>(out));
+    if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "dequantize_kernel: %s", cudaGetErrorString(e));
     return check_launch("dequantize_kernel");
 }
 
