@@ -172,11 +172,13 @@ __device__ bool block_barrier(const Params& p, uint32_t value) {
 }
 
 // ---------------------------------------------------------------- NVFP4 codec ----
-// 32 bf16 values at x (16-byte aligned) -> 16 packed bytes + 2 scale bytes (block 0 low byte).
-__device__ __forceinline__ void quant32(const __nv_bfloat16* x, float gs_inv, uint4& packed, uint32_t& scales) {
-    uint4 raw[4];
+// The 64 bytes of 32 bf16 values at x (16-byte aligned).
+__device__ __forceinline__ void load_raw32(const __nv_bfloat16* x, uint4* raw) {
 #pragma unroll
     for (int i = 0; i < 4; i++) raw[i] = ld_nc_v4(reinterpret_cast<const uint8_t*>(x) + 16 * i);
+}
+// 32 bf16 values (as loaded by load_raw32) -> 16 packed bytes + 2 scale bytes (block 0 low byte).
+__device__ __forceinline__ void quant_raw32(const uint4* raw, float gs_inv, uint4& packed, uint32_t& scales) {
     uint32_t w[4];
     scales = 0;
 #pragma unroll
@@ -186,6 +188,11 @@ __device__ __forceinline__ void quant32(const __nv_bfloat16* x, float gs_inv, ui
         scales |= q16_bf16(q, gs_inv, w[2 * b], w[2 * b + 1]) << (8 * b);
     }
     packed = make_uint4(w[0], w[1], w[2], w[3]);
+}
+__device__ __forceinline__ void quant32(const __nv_bfloat16* x, float gs_inv, uint4& packed, uint32_t& scales) {
+    uint4 raw[4];
+    load_raw32(x, raw);
+    quant_raw32(raw, gs_inv, packed, scales);
 }
 // Same from 32 fp32 values.
 __device__ __forceinline__ void quant32f(const float* v, float gs_inv, uint4& packed, uint32_t& scales) {
@@ -232,9 +239,34 @@ __device__ __forceinline__ void get_chunk(const uint8_t* src, int64_t n, int64_t
     scales = ld_cg_u16(src + align16(n / 2) + c * 2);
 }
 
+// acc = sum over s = 0..n-1 (in that order) of dequant(slot s, chunk c): the loads of two slots
+// are issued before either is accumulated (more would not fit the 64 registers that keep two
+// 512-thread blocks per SM), halving the memory round trips per chunk.
+template <typename SlotFn>
+__device__ __forceinline__ void sum_slots(SlotFn slot, int n, int64_t slot_elems, int64_t c, float gs, float* acc) {
+#pragma unroll
+    for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+#pragma unroll
+    for (int s0 = 0; s0 < AR_MAX_WORLD; s0 += 2) {
+        if (s0 >= n) break;
+        uint4 pk[2];
+        uint32_t sc[2];
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+            if (s0 + j < n) get_chunk(slot(s0 + j), slot_elems, c, pk[j], sc[j]);
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+            if (s0 + j < n) dq32_acc(pk[j], sc[j], gs, acc);
+    }
+}
+
 // ---------------------------------------------------------------- NVFP4 kernels ----
+// Every phase walks this block's chunks (c = first, first + stride, ...).  Loops over ranks or
+// shards prefetch: the next shard's input is loaded while the current one is quantized and pushed
+// (phase A), every slot of a chunk is loaded before the sum (phases B and the one-shot's second
+// phase), and the next owner's reduced chunk is loaded while the current one is written (phase C).
 template <bool kTwoShot>
-__global__ void __launch_bounds__(AR_THREADS) ar_nvfp4_kernel(const Params p) {
+__global__ void __launch_bounds__(AR_THREADS, 2) ar_nvfp4_kernel(const Params p) {
     const int n = p.world, me = p.rank;
     const float gs_inv = __fdiv_rn(1.0f, p.gs);
     const uint32_t v1 = p.epoch * 2u + 1u, v2 = p.epoch * 2u + 2u;
@@ -259,14 +291,7 @@ __global__ void __launch_bounds__(AR_THREADS) ar_nvfp4_kernel(const Params p) {
         if (fused || p.phase == 1) {
             for (int64_t c = first; c < chunks; c += stride) {
                 float acc[32];
-#pragma unroll
-                for (int i = 0; i < 32; i++) acc[i] = 0.0f;
-                for (int s = 0; s < n; s++) {                  // fixed sum order 0 .. n-1
-                    uint4 pk;
-                    uint32_t sc;
-                    get_chunk(in_slot(p, me, s), p.numel, c, pk, sc);
-                    dq32_acc(pk, sc, p.gs, acc);
-                }
+                sum_slots([&](int s) { return in_slot(p, me, s); }, n, p.numel, c, p.gs, acc);   // order 0 .. n-1
                 store_bf16x32(p.out + c * 32, acc);
             }
         }
@@ -289,12 +314,17 @@ __global__ void __launch_bounds__(AR_THREADS) ar_nvfp4_kernel(const Params p) {
     }
     if (p.phase == -1 || p.phase == 0) {
         for (int64_t c = first; c < schunks; c += stride) {
+            uint4 raw[4], nxt[4];
+            load_raw32(p.in + (int64_t)((me + 1) % n) * shard + c * 32, raw);
             for (int k = 1; k <= n; k++) {
                 const int o = (me + k) % n;
+                if (k < n) load_raw32(p.in + (int64_t)((me + k + 1) % n) * shard + c * 32, nxt);
                 uint4 pk;
                 uint32_t sc;
-                quant32(p.in + (int64_t)o * shard + c * 32, gs_inv, pk, sc);
+                quant_raw32(raw, gs_inv, pk, sc);
                 put_chunk(in_slot(p, o, me), shard, c, pk, sc);
+#pragma unroll
+                for (int i = 0; i < 4; i++) raw[i] = nxt[i];
             }
         }
     }
@@ -304,14 +334,7 @@ __global__ void __launch_bounds__(AR_THREADS) ar_nvfp4_kernel(const Params p) {
         const float gs_red_inv = __fdiv_rn(1.0f, gs_red);
         for (int64_t c = first; c < schunks; c += stride) {
             float acc[32];
-#pragma unroll
-            for (int i = 0; i < 32; i++) acc[i] = 0.0f;
-            for (int s = 0; s < n; s++) {
-                uint4 pk;
-                uint32_t sc;
-                get_chunk(in_slot(p, me, s), shard, c, pk, sc);
-                dq32_acc(pk, sc, p.gs, acc);
-            }
+            sum_slots([&](int s) { return in_slot(p, me, s); }, n, shard, c, p.gs, acc);       // order 0 .. n-1
             uint4 pk;
             uint32_t sc;
             quant32f(acc, gs_red_inv, pk, sc);
@@ -324,15 +347,18 @@ __global__ void __launch_bounds__(AR_THREADS) ar_nvfp4_kernel(const Params p) {
     if (fused && !block_barrier(p, v2)) return;
     if (fused || p.phase == 2) {
         for (int64_t c = first; c < schunks; c += stride) {
+            uint4 pk, npk;
+            uint32_t sc, nsc;
+            get_chunk(gather_slot(p, me, 0), shard, c, pk, sc);
             for (int o = 0; o < n; o++) {
-                uint4 pk;
-                uint32_t sc;
-                get_chunk(gather_slot(p, me, o), shard, c, pk, sc);
+                if (o + 1 < n) get_chunk(gather_slot(p, me, o + 1), shard, c, npk, nsc);
                 float acc[32];
 #pragma unroll
                 for (int i = 0; i < 32; i++) acc[i] = 0.0f;
                 dq32_acc(pk, sc, gs_red, acc);
                 store_bf16x32(p.out + (int64_t)o * shard + c * 32, acc);
+                pk = npk;
+                sc = nsc;
             }
         }
     }
@@ -456,8 +482,10 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float* acc) {
     return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// Loads of all ranks' chunks are issued before the first is used (the same prefetching as the NVFP4
+// kernels, so the baseline is not held back by one round trip per rank).
 template <bool kTwoShot>
-__global__ void __launch_bounds__(AR_THREADS) ar_bf16_kernel(const Params p) {
+__global__ void __launch_bounds__(AR_THREADS, 2) ar_bf16_kernel(const Params p) {
     const int n = p.world, me = p.rank;
     const uint32_t v1 = p.epoch * 2u + 1u, v2 = p.epoch * 2u + 2u;
     const bool fused = p.phase < 0;
@@ -465,6 +493,15 @@ __global__ void __launch_bounds__(AR_THREADS) ar_bf16_kernel(const Params p) {
     const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint8_t* in = reinterpret_cast<const uint8_t*>(p.in);
     uint8_t* out = reinterpret_cast<uint8_t*>(p.out);
+    auto sum_ranks = [&](auto src, int64_t c, float* acc) {      // fp32 sum in rank order 0 .. n-1
+        uint4 v[AR_MAX_WORLD];
+#pragma unroll
+        for (int s = 0; s < AR_MAX_WORLD; s++)
+            if (s < n) v[s] = ld_cg_v4(src(s) + c * 16);
+#pragma unroll
+        for (int s = 0; s < AR_MAX_WORLD; s++)
+            if (s < n) acc_bf16x8(v[s], acc);
+    };
 
     if (!kTwoShot) {
         const int64_t chunks = p.numel / 8;
@@ -478,7 +515,7 @@ __global__ void __launch_bounds__(AR_THREADS) ar_bf16_kernel(const Params p) {
         if (fused || p.phase == 1) {
             for (int64_t c = first; c < chunks; c += stride) {
                 float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                for (int s = 0; s < n; s++) acc_bf16x8(ld_cg_v4(in_slot(p, me, s) + c * 16), acc);
+                sum_ranks([&](int s) { return in_slot(p, me, s); }, c, acc);
                 st_v4(out + c * 16, pack_bf16x8(acc));
             }
         }
@@ -488,26 +525,35 @@ __global__ void __launch_bounds__(AR_THREADS) ar_bf16_kernel(const Params p) {
     const int64_t schunks = shard / 8;
     if (fused || p.phase == 0) {
         for (int64_t c = first; c < schunks; c += stride) {
-            for (int k = 1; k <= n; k++) {
-                const int o = (me + k) % n;
-                st_v4(in_slot(p, o, me) + c * 16, ld_nc_v4(in + ((int64_t)o * shard) * 2 + c * 16));
-            }
+            uint4 v[AR_MAX_WORLD];
+#pragma unroll
+            for (int k = 1; k <= AR_MAX_WORLD; k++)
+                if (k <= n) v[k - 1] = ld_nc_v4(in + ((int64_t)((me + k) % n) * shard) * 2 + c * 16);
+#pragma unroll
+            for (int k = 1; k <= AR_MAX_WORLD; k++)
+                if (k <= n) st_v4(in_slot(p, (me + k) % n, me) + c * 16, v[k - 1]);
         }
     }
     if (fused && !block_barrier(p, v1)) return;
     if (fused || p.phase == 1) {
         for (int64_t c = first; c < schunks; c += stride) {
             float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            for (int s = 0; s < n; s++) acc_bf16x8(ld_cg_v4(in_slot(p, me, s) + c * 16), acc);
+            sum_ranks([&](int s) { return in_slot(p, me, s); }, c, acc);
             const uint4 r = pack_bf16x8(acc);
             for (int k = 1; k <= n; k++) st_v4(gather_slot(p, (me + k) % n, me) + c * 16, r);
         }
     }
     if (fused && !block_barrier(p, v2)) return;
     if (fused || p.phase == 2) {
-        for (int64_t c = first; c < schunks; c += stride)
-            for (int o = 0; o < n; o++)
-                st_v4(out + ((int64_t)o * shard) * 2 + c * 16, ld_cg_v4(gather_slot(p, me, o) + c * 16));
+        for (int64_t c = first; c < schunks; c += stride) {
+            uint4 v[AR_MAX_WORLD];
+#pragma unroll
+            for (int o = 0; o < AR_MAX_WORLD; o++)
+                if (o < n) v[o] = ld_cg_v4(gather_slot(p, me, o) + c * 16);
+#pragma unroll
+            for (int o = 0; o < AR_MAX_WORLD; o++)
+                if (o < n) st_v4(out + ((int64_t)o * shard) * 2 + c * 16, v[o]);
+        }
     }
 }
 
@@ -669,9 +715,10 @@ int resident_grid(const void* fn, int threads = AR_THREADS) {
     return g < AR_MAX_BLOCKS ? g : AR_MAX_BLOCKS;
 }
 
-// Blocks for `work` thread-chunks: enough to cover the work once, at most what is resident.
+// Blocks for `work` chunks of a phase: a quarter of a chunk per thread or more blocks, at most what
+// is resident -- spreading the chunks over more SMs gives each SM fewer dependent round trips.
 int grid_for(nvfp4_ar_t h, int64_t work) {
-    int64_t g = (work + AR_THREADS - 1) / AR_THREADS;
+    int64_t g = (work + AR_THREADS / 4 - 1) / (AR_THREADS / 4);
     if (g < 1) g = 1;
     if (g > h->max_grid) g = h->max_grid;
     return (int)g;

@@ -63,8 +63,12 @@ constexpr int SF_STAGE = 2 * 4 * 512;                 // scale atoms of B and of
 #ifndef GSMALL_CTAS_PER_SM
 #define GSMALL_CTAS_PER_SM 2
 #endif
+#ifndef GSMALL_SMEM_BUDGET_M16_KB
+#define GSMALL_SMEM_BUDGET_M16_KB 100
+#endif
 constexpr int SMEM_BUDGET_1 = 200 * 1024;
 constexpr int SMEM_BUDGET_2 = 100 * 1024;
+constexpr int SMEM_BUDGET_M16 = GSMALL_SMEM_BUDGET_M16_KB * 1024;   // Mp = 16 (the decode shapes)
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 
 __host__ __device__ constexpr int stage_bytes(int mp) { return B_BOX + mp * 128 + SF_STAGE; }
@@ -73,7 +77,7 @@ __host__ __device__ constexpr int ctas_per_sm(int mp) { return (GSMALL_CTAS_PER_
 // fp32 (128 x mp floats in all), after the stage ring.
 __host__ __device__ constexpr int recv_bytes(int mp) { return 128 * mp * 4; }
 __host__ __device__ constexpr int stage_budget(int mp, bool cl) {
-    return (ctas_per_sm(mp) == 2 ? SMEM_BUDGET_2 : SMEM_BUDGET_1) - (cl ? recv_bytes(mp) : 0);
+    return (mp <= 16 ? SMEM_BUDGET_M16 : ctas_per_sm(mp) == 2 ? SMEM_BUDGET_2 : SMEM_BUDGET_1) - (cl ? recv_bytes(mp) : 0);
 }
 __host__ __device__ constexpr int num_stages(int mp, bool cl = false) {
     return stage_budget(mp, cl) / stage_bytes(mp) < MAX_STAGES ? stage_budget(mp, cl) / stage_bytes(mp) : MAX_STAGES;
@@ -97,7 +101,7 @@ constexpr int NUM_BARS = 3 * MAX_STAGES + 6;
 __host__ __device__ constexpr int smem_bytes(int mp, bool cl) {
     return 1024 + num_stages(mp, cl) * stage_bytes(mp) + (cl ? recv_bytes(mp) : 0) + NUM_BARS * 8 + 16;
 }
-static_assert(num_stages(16, true) == 4 && num_stages(64, true) >= 2 && num_stages(128, true) >= 2,
+static_assert(num_stages(16, true) >= 2 && num_stages(64, true) >= 2 && num_stages(128, true) >= 2,
               "stages left next to the receive buffer");
 constexpr int MAX_CLUSTER_SPLITS = 8;
 

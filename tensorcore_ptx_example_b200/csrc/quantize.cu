@@ -131,8 +131,9 @@ __global__ void sf_pad_kernel(uint8_t* __restrict__ sf, int64_t rows, int64_t co
 // transaction) and take their byte of it.  HBM-bound: 0.5625 B/elt read, 2 B/elt written.
 //   value = bf16(e2m1 * (e4m3(scale) * gs)), one rounding for each product.
 constexpr int DQ_THREADS = 256;
-constexpr int DQ_UNROLL = 4;
+constexpr int DQ_UNROLL = 8;
 
+template <bool kStore32>
 __global__ void __launch_bounds__(DQ_THREADS)
 dequantize_kernel(const uint8_t* __restrict__ packed, const uint8_t* __restrict__ sf, int64_t rows, int64_t cols,
                   float gs, __nv_bfloat16* __restrict__ out) {
@@ -183,8 +184,12 @@ dequantize_kernel(const uint8_t* __restrict__ packed, const uint8_t* __restrict_
                 }
             }
             uint8_t* dst = reinterpret_cast<uint8_t*>(out) + b * 32;
-            st_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
-            st_v4(dst + 16, make_uint4(o[4], o[5], o[6], o[7]));
+            if constexpr (kStore32) {
+                st_global_v8(dst, o);                       // one 32-byte store
+            } else {
+                st_v4(dst, make_uint4(o[0], o[1], o[2], o[3]));
+                st_v4(dst + 16, make_uint4(o[4], o[5], o[6], o[7]));
+            }
         }
     }
 }
@@ -414,9 +419,15 @@ nvfp4_status_t nvfp4_dequantize_bf16(const void* packed, const void* sf, int64_t
     int64_t grid = (nblocks + (int64_t)DQ_THREADS * DQ_UNROLL - 1) / ((int64_t)DQ_THREADS * DQ_UNROLL);
     const int64_t cap = (int64_t)sm_count() * 8;
     if (grid > cap) grid = cap;
-    const cudaError_t e = launch_pdl(dequantize_kernel, (unsigned)grid, DQ_THREADS, (cudaStream_t)stream,
-                                     reinterpret_cast<const uint8_t*>(packed), reinterpret_cast<const uint8_t*>(sf),
-                                     rows, cols, global_scale, reinterpret_cast<__nv_bfloat16*>(out));
+    const auto* pk = reinterpret_cast<const uint8_t*>(packed);
+    const auto* sp = reinterpret_cast<const uint8_t*>(sf);
+    auto* op = reinterpret_cast<__nv_bfloat16*>(out);
+    const cudaError_t e =
+        ((reinterpret_cast<uintptr_t>(out) & 31) == 0)
+            ? launch_pdl(dequantize_kernel<true>, (unsigned)grid, DQ_THREADS, (cudaStream_t)stream, pk, sp, rows, cols,
+                         global_scale, op)
+            : launch_pdl(dequantize_kernel<false>, (unsigned)grid, DQ_THREADS, (cudaStream_t)stream, pk, sp, rows, cols,
+                         global_scale, op);
     if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "dequantize_kernel: %s", cudaGetErrorString(e));
     return check_launch("dequantize_kernel");
 }
