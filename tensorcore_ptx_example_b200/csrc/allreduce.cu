@@ -1129,6 +1129,8 @@ nvfp4_status_t nvfp4_ar_allreduce_emulated(nvfp4_ar_t const* handles, int world,
     clear_error();
     if (!handles || !ins || !outs || world < 1 || world > AR_MAX_WORLD)
         return fail(NVFP4_ERR_INVALID_ARG, "ar_allreduce_emulated: bad arguments");
+    if (algo == NVFP4_AR_NVLS)
+        return fail(NVFP4_ERR_UNSUPPORTED, "ar_allreduce_emulated: NVFP4_AR_NVLS needs a multicast object across GPUs");
     for (int r = 0; r < world; r++) {
         nvfp4_status_t st = check_call(handles[r], "ar_allreduce_emulated", ins[r], outs[r], numel,
                                        algo == NVFP4_AR_AUTO ? NVFP4_AR_AUTO : algo, bf16_payload ? 8 : 32);
@@ -1136,8 +1138,6 @@ nvfp4_status_t nvfp4_ar_allreduce_emulated(nvfp4_ar_t const* handles, int world,
         if (handles[r]->world != world || handles[r]->rank != r || handles[r]->device != handles[0]->device)
             return fail(NVFP4_ERR_INVALID_ARG, "ar_allreduce_emulated: contexts must be ranks 0..%d of one device", world - 1);
     }
-    if (algo == NVFP4_AR_NVLS)
-        return fail(NVFP4_ERR_UNSUPPORTED, "ar_allreduce_emulated: NVFP4_AR_NVLS needs a multicast object across GPUs");
     if (numel == 0) return NVFP4_OK;
     if (!bf16_payload && (!(global_scale > 0.0f) || !isfinite(global_scale)))
         return fail(NVFP4_ERR_INVALID_ARG, "ar_allreduce_emulated: global_scale must be finite and > 0");

@@ -190,3 +190,33 @@ def test_cfg4_full_size_sampled(nv, oracle):
         rel = float(((outs[0].double() - exact).norm() / exact.norm()).item())
         assert rel < (0.12 if algo == "oneshot" else 0.16), (algo, rel)
         del outs
+
+
+def test_nvls_argument_checks(nv):
+    """NVFP4_AR_NVLS: bf16 only, only after a multicast buffer is registered, not emulated on one
+    GPU; the registration checks its addresses.  (The in-switch sum itself needs NVLink multicast
+    across GPUs: tests/test_allreduce_multigpu.py.)"""
+    import ctypes
+
+    from tensorcore_ptx_example_b200 import allreduce as ar
+    L = nv.lib()
+    numel = 1024
+    x = torch.zeros(numel, dtype=torch.bfloat16, device="cuda")
+    o = torch.empty_like(x)
+    ctx = ar.AllReduce(1, 0, numel)
+    try:
+        h = ctx.handle
+        p = ctypes.c_void_p
+        assert L.nvfp4_ar_bf16_allreduce(h, p(x.data_ptr()), p(o.data_ptr()), numel, ar.NVLS, None) == \
+            nv.NVFP4_ERR_NOT_READY
+        assert L.nvfp4_ar_allreduce(h, p(x.data_ptr()), p(o.data_ptr()), numel, ctypes.c_float(1.0), ar.NVLS,
+                                    None) == nv.NVFP4_ERR_UNSUPPORTED
+        assert L.nvfp4_ar_set_multicast(h, p(x.data_ptr() + 4), p(x.data_ptr()), 4096) == nv.NVFP4_ERR_INVALID_ARG
+        assert L.nvfp4_ar_set_multicast(h, None, p(x.data_ptr()), 4096) == nv.NVFP4_ERR_INVALID_ARG
+        hs = (ctypes.c_void_p * 1)(h)
+        ins = (ctypes.c_void_p * 1)(p(x.data_ptr()))
+        outs = (ctypes.c_void_p * 1)(p(o.data_ptr()))
+        assert L.nvfp4_ar_allreduce_emulated(hs, 1, ins, outs, numel, ctypes.c_float(1.0), ar.NVLS, 1, None) == \
+            nv.NVFP4_ERR_UNSUPPORTED
+    finally:
+        ctx.close()

@@ -98,6 +98,8 @@ def test_create_rejects_bad_arguments(nv):
                                   None) == nv.NVFP4_ERR_INVALID_ARG
     assert L.nvfp4_gemm_allreduce_emulated(None, 2, None, None, None, None, None, f1, None, 256, 256, 256,
                                            None) == nv.NVFP4_ERR_INVALID_ARG
+    assert L.nvfp4_ar_set_multicast(None, fake, fake, 1 << 20) == nv.NVFP4_ERR_INVALID_ARG
+    assert L.nvfp4_ar_bf16_allreduce(None, fake, fake, 64, 4, None) == nv.NVFP4_ERR_INVALID_ARG
 
 
 # ------------------------------------------------------------ gloo ranks ----
