@@ -298,33 +298,51 @@ __global__ void __launch_bounds__(AR_THREADS, 2) ar_nvfp4_kernel(const Params p)
         return;
     }
 
+    // Two-shot.  Block b owns the contiguous chunk range [c0, c1) of every shard, the same range
+    // on every rank, in every phase (so a phase needs block b of every rank, and no other block, to
+    // have finished the previous one).  Phases A and C work on (shard, chunk) pairs: the block's
+    // threads split the n x (c1 - c0) pairs, so every thread has independent work even when a
+    // block owns few chunks; each thread keeps the loads of two pairs in flight.  Pair order is
+    // shard-major with the shards rotated (rank me+1 first), so the ranks start on different
+    // peers.
     const int64_t shard = p.numel / n;
     const int64_t schunks = shard / 32;
+    const int64_t cpb = (schunks + gridDim.x - 1) / gridDim.x;
+    const int64_t c0 = (int64_t)blockIdx.x * cpb;
+    // per-block counts fit 32 bits (launch_nvfp4 checks n * cpb < 2^31): 32-bit division below
+    const uint32_t ncb = (uint32_t)(c0 < schunks ? (schunks - c0 < cpb ? schunks - c0 : cpb) : 0);
+    const uint32_t pairs = (uint32_t)n * ncb;
+    const uint32_t T = blockDim.x, t = threadIdx.x;
     if (p.phase == -3 || p.phase == 3) {
         // the shards were quantized by the producer of the data (a GEMM epilogue): push them
-        for (int64_t c = first; c < schunks; c += stride) {
-            for (int k = 1; k <= n; k++) {
-                const int o = (me + k) % n;
-                const int64_t e32 = (int64_t)o * schunks + c;     // chunk of 32 elements of the input
-                const uint4 pk = ld_nc_v4(p.q_codes + e32 * 16);
-                const uint32_t sc = *reinterpret_cast<const uint16_t*>(p.q_scales + e32 * 2);
-                put_chunk(in_slot(p, o, me), shard, c, pk, sc);
-            }
+        for (uint32_t i = t; i < pairs; i += T) {
+            const int o = (me + 1 + (int)(i / ncb)) % n;
+            const int64_t c = c0 + i % ncb;
+            const int64_t e32 = (int64_t)o * schunks + c;         // chunk of 32 elements of the input
+            const uint4 pk = ld_nc_v4(p.q_codes + e32 * 16);
+            const uint32_t sc = *reinterpret_cast<const uint16_t*>(p.q_scales + e32 * 2);
+            put_chunk(in_slot(p, o, me), shard, c, pk, sc);
         }
     }
     if (p.phase == -1 || p.phase == 0) {
-        for (int64_t c = first; c < schunks; c += stride) {
-            uint4 raw[4], nxt[4];
-            load_raw32(p.in + (int64_t)((me + 1) % n) * shard + c * 32, raw);
-            for (int k = 1; k <= n; k++) {
-                const int o = (me + k) % n;
-                if (k < n) load_raw32(p.in + (int64_t)((me + k + 1) % n) * shard + c * 32, nxt);
+        for (uint32_t i = t; i < pairs; i += 2 * T) {
+            uint4 raw[2][4];
+            int o[2];
+            int64_t c[2];
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const uint32_t j = i + u * T;
+                o[u] = (me + 1 + (int)(j / ncb)) % n;
+                c[u] = c0 + j % ncb;
+                if (j < pairs) load_raw32(p.in + (int64_t)o[u] * shard + c[u] * 32, raw[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                if (i + u * T >= pairs) break;
                 uint4 pk;
                 uint32_t sc;
-                quant_raw32(raw, gs_inv, pk, sc);
-                put_chunk(in_slot(p, o, me), shard, c, pk, sc);
-#pragma unroll
-                for (int i = 0; i < 4; i++) raw[i] = nxt[i];
+                quant_raw32(raw[u], gs_inv, pk, sc);
+                put_chunk(in_slot(p, o[u], me), shard, c[u], pk, sc);
             }
         }
     }
@@ -332,7 +350,8 @@ __global__ void __launch_bounds__(AR_THREADS, 2) ar_nvfp4_kernel(const Params p)
     const float gs_red = __fmul_rn(p.gs, (float)n);
     if (fused || p.phase == 1) {
         const float gs_red_inv = __fdiv_rn(1.0f, gs_red);
-        for (int64_t c = first; c < schunks; c += stride) {
+        for (uint32_t cl = t; cl < ncb; cl += T) {
+            const int64_t c = c0 + cl;
             float acc[32];
             sum_slots([&](int s) { return in_slot(p, me, s); }, n, shard, c, p.gs, acc);       // order 0 .. n-1
             uint4 pk;
@@ -346,19 +365,26 @@ __global__ void __launch_bounds__(AR_THREADS, 2) ar_nvfp4_kernel(const Params p)
     }
     if (fused && !block_barrier(p, v2)) return;
     if (fused || p.phase == 2) {
-        for (int64_t c = first; c < schunks; c += stride) {
-            uint4 pk, npk;
-            uint32_t sc, nsc;
-            get_chunk(gather_slot(p, me, 0), shard, c, pk, sc);
-            for (int o = 0; o < n; o++) {
-                if (o + 1 < n) get_chunk(gather_slot(p, me, o + 1), shard, c, npk, nsc);
+        for (uint32_t i = t; i < pairs; i += 2 * T) {
+            uint4 pk[2];
+            uint32_t sc[2];
+            int o[2];
+            int64_t c[2];
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const uint32_t j = i + u * T;
+                o[u] = (int)(j / ncb);
+                c[u] = c0 + j % ncb;
+                if (j < pairs) get_chunk(gather_slot(p, me, o[u]), shard, c[u], pk[u], sc[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                if (i + u * T >= pairs) break;
                 float acc[32];
 #pragma unroll
-                for (int i = 0; i < 32; i++) acc[i] = 0.0f;
-                dq32_acc(pk, sc, gs_red, acc);
-                store_bf16x32(p.out + (int64_t)o * shard + c * 32, acc);
-                pk = npk;
-                sc = nsc;
+                for (int k = 0; k < 32; k++) acc[k] = 0.0f;
+                dq32_acc(pk[u], sc[u], gs_red, acc);
+                store_bf16x32(p.out + (int64_t)o[u] * shard + c[u] * 32, acc);
             }
         }
     }
@@ -995,6 +1021,9 @@ static nvfp4_status_t launch_nvfp4_ll(nvfp4_ar_t h, const Params& p, cudaStream_
 static nvfp4_status_t launch_nvfp4(nvfp4_ar_t h, const Params& p, bool twoshot, cudaStream_t s) {
     const int64_t work = twoshot ? p.numel / p.world / 32 : p.numel / 32;
     const int grid = grid_for(h, work);
+    if (twoshot && (int64_t)p.world * ((work + grid - 1) / grid) >= (int64_t(1) << 31))
+        return fail(NVFP4_ERR_INVALID_ARG, "ar_allreduce: %lld elements per rank is too many for one call",
+                    (long long)p.numel);
     if (twoshot) ar_nvfp4_kernel<true><<<grid, AR_THREADS, 0, s>>>(p);
     else ar_nvfp4_kernel<false><<<grid, AR_THREADS, 0, s>>>(p);
     return check_launch("ar_nvfp4_kernel");

@@ -9,12 +9,12 @@
 // Split-K gives enough work units to stream B from every SM: unit (n-tile, s) covers K range
 // [s * Ks, (s + 1) * Ks).  The partial tiles are summed in split order 0..S-1 (fp32, round to
 // nearest) and alpha -> bf16 is applied, in one of two ways:
-//   in-cluster (one launch; when every unit gets its own CTA and S <= 8): the S CTAs of an n-tile
-//     form a thread-block cluster; each writes its partial tile into its own shared memory (the
-//     drained stage ring), and CTA s then sums rows [s * 128 / S, (s + 1) * 128 / S) of the tile
-//     from all S partials through distributed shared memory (ld.shared::cluster) and stores D.
-//     Two mbarriers per CTA, arrived on remotely by every CTA of the cluster, hand the partials
-//     over ("ready") and keep each CTA resident until every peer has read it ("read");
+//   in-cluster (one launch, no workspace; when S <= 8 divides 128): one CTA per unit, the S CTAs of
+//     an n-tile form a thread-block cluster.  CTA r owns rows [r * 128 / S, (r + 1) * 128 / S) of the
+//     tile: every CTA pushes its partial of those rows into CTA r's receive buffer (one-way
+//     st.shared::cluster stores) and arrives on CTA r's "ready" mbarrier; CTA r then sums the S
+//     partials in split order from its own shared memory and stores D.  (Reading the peers'
+//     partials with ld.shared::cluster instead was measured slower: one round trip per load.)
 //   workspace (otherwise): the partials go to a global workspace and a second kernel (four
 //     outputs per thread, all S partial loads in flight) sums them.  Both kernels are
 //     programmatic dependent launches.
@@ -63,12 +63,8 @@ constexpr int SF_STAGE = 2 * 4 * 512;                 // scale atoms of B and of
 #ifndef GSMALL_CTAS_PER_SM
 #define GSMALL_CTAS_PER_SM 2
 #endif
-#ifndef GSMALL_SMEM_BUDGET_M16_KB
-#define GSMALL_SMEM_BUDGET_M16_KB 100
-#endif
 constexpr int SMEM_BUDGET_1 = 200 * 1024;
 constexpr int SMEM_BUDGET_2 = 100 * 1024;
-constexpr int SMEM_BUDGET_M16 = GSMALL_SMEM_BUDGET_M16_KB * 1024;   // Mp = 16 (the decode shapes)
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 
 __host__ __device__ constexpr int stage_bytes(int mp) { return B_BOX + mp * 128 + SF_STAGE; }
@@ -77,7 +73,7 @@ __host__ __device__ constexpr int ctas_per_sm(int mp) { return (GSMALL_CTAS_PER_
 // fp32 (128 x mp floats in all), after the stage ring.
 __host__ __device__ constexpr int recv_bytes(int mp) { return 128 * mp * 4; }
 __host__ __device__ constexpr int stage_budget(int mp, bool cl) {
-    return (mp <= 16 ? SMEM_BUDGET_M16 : ctas_per_sm(mp) == 2 ? SMEM_BUDGET_2 : SMEM_BUDGET_1) - (cl ? recv_bytes(mp) : 0);
+    return (ctas_per_sm(mp) == 2 ? SMEM_BUDGET_2 : SMEM_BUDGET_1) - (cl ? recv_bytes(mp) : 0);
 }
 __host__ __device__ constexpr int num_stages(int mp, bool cl = false) {
     return stage_budget(mp, cl) / stage_bytes(mp) < MAX_STAGES ? stage_budget(mp, cl) / stage_bytes(mp) : MAX_STAGES;

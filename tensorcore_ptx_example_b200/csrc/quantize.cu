@@ -110,129 +110,6 @@ quantize_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t cols,
         if (!have_scale) fetch_scale();
 }
 
-// Staged variant (QUANT_RING builds): the input reaches shared memory through 1-D bulk copies
-// (cp.async.bulk) of RING_CHUNK contiguous bytes into a ring of RING_STAGES slots per CTA, issued by
-// one producer thread, so each SM has up to 2 x RING_STAGES x RING_CHUNK bytes of loads in flight
-// without spending registers on them; eight consumer warps quantize a landed chunk (one 16-element
-// block per thread per pass, the same q16_bf16 and scale-word layout as quantize_kernel) and free
-// the slot.  Every wait is bounded.
-constexpr int RING_CHUNK = 24576;                      // 768 blocks of 16 bf16
-constexpr int RING_BLOCKS = RING_CHUNK / 32;
-constexpr int RING_STAGES = 4;
-constexpr int RING_CONSUMERS = 256;
-constexpr int RING_THREADS = 32 + RING_CONSUMERS;
-constexpr int RING_SMEM = 1024 + RING_STAGES * RING_CHUNK + 2 * RING_STAGES * 8;
-constexpr uint64_t RING_WAIT_NS = 2000000000ull;
-
-template <bool kDevScale>
-__global__ void __launch_bounds__(RING_THREADS)
-quantize_ring_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t cols, float gs_host,
-                     const uint32_t* __restrict__ amax_word, float* __restrict__ gs_out, uint8_t* __restrict__ packed,
-                     uint8_t* __restrict__ sf) {
-    extern __shared__ uint8_t ring_raw[];
-    const uint32_t raw_addr = smem_u32(ring_raw);
-    const uint32_t base = (raw_addr + 1023u) & ~1023u;
-    uint8_t* ring = ring_raw + (base - raw_addr);
-    const uint32_t bar0 = base + RING_STAGES * RING_CHUNK;
-    auto full_bar = [&](int st) { return bar0 + 8u * st; };
-    auto empty_bar = [&](int st) { return bar0 + 8u * (RING_STAGES + st); };
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t nblocks = rows * cols / 16;
-    const int64_t chunks = (nblocks + RING_BLOCKS - 1) / RING_BLOCKS;
-    if (threadIdx.x == 0) {
-        for (int st = 0; st < RING_STAGES; st++) {
-            mbar_init(full_bar(st), 1);
-            mbar_init(empty_bar(st), RING_CONSUMERS / 32);
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
-    // x may come from the previous kernel (given scale) -- and with a device scale this kernel
-    // follows the amax kernel, whose input is the same x -- so loads start after the wait in the
-    // first case only
-    if constexpr (!kDevScale) asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    if (warp == 0) {
-        // ------------------------------------------------------------ producer ----
-        if (lane == 0) {
-            int st = 0;
-            uint32_t ph = 0;
-            for (int64_t ch = blockIdx.x, j = 0; ch < chunks; ch += gridDim.x, j++) {
-                if (j >= RING_STAGES && !mbar_wait(empty_bar(st), ph ^ 1u, RING_WAIT_NS, DEV_TIMEOUT_QUANT)) break;
-                const int64_t nb = (nblocks - ch * RING_BLOCKS) < RING_BLOCKS ? (nblocks - ch * RING_BLOCKS) : RING_BLOCKS;
-                mbar_arrive_expect_tx(full_bar(st), (uint32_t)(nb * 32));
-                bulk_load(base + st * RING_CHUNK, reinterpret_cast<const uint8_t*>(x) + ch * RING_CHUNK, (uint32_t)(nb * 32),
-                          full_bar(st));
-                if (++st == RING_STAGES) { st = 0; ph ^= 1u; }
-            }
-        }
-        return;
-    }
-    // -------------------------------------------------------------- consumers ----
-    float gs = gs_host, gs_inv;
-    if constexpr (kDevScale) {
-        asm volatile("griddepcontrol.wait;" ::: "memory");
-        global_scale_from_amax(__uint_as_float(*reinterpret_cast<const volatile uint32_t*>(amax_word)), gs, gs_inv);
-        if (blockIdx.x == 0 && threadIdx.x == 32 && gs_out) *gs_out = gs;
-    } else {
-        gs_inv = __fdiv_rn(1.0f, gs);
-    }
-    const int t = threadIdx.x - 32;
-    const int64_t katoms = cols / 64;
-    // (row, col) of this thread's first block in its CTA's first chunk, then advanced without
-    // division: +RING_CONSUMERS blocks inside a chunk, and to the next chunk of this CTA
-    int64_t e = ((int64_t)blockIdx.x * RING_BLOCKS + t) * 16;
-    int64_t row = e / cols, col = e - row * cols;
-    const int64_t ein = (int64_t)RING_CONSUMERS * 16;
-    const int64_t dri = ein / cols, dci = ein - dri * cols;
-    const int64_t passes = RING_BLOCKS / RING_CONSUMERS;                       // 3
-    const int64_t enext = ((int64_t)gridDim.x * RING_BLOCKS - passes * RING_CONSUMERS) * 16;
-    const int64_t drn = enext / cols, dcn = enext - drn * cols;
-    int st = 0;
-    uint32_t ph = 0;
-    for (int64_t ch = blockIdx.x; ch < chunks; ch += gridDim.x) {
-        const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(full_bar(st), ph, RING_WAIT_NS, DEV_TIMEOUT_QUANT));
-        if (!ok) break;
-        const int64_t nb = (nblocks - ch * RING_BLOCKS) < RING_BLOCKS ? (nblocks - ch * RING_BLOCKS) : RING_BLOCKS;
-        const uint8_t* src = ring + st * RING_CHUNK;
-#pragma unroll
-        for (int i = 0; i < RING_BLOCKS / RING_CONSUMERS; i++) {
-            const int blk = t + i * RING_CONSUMERS;
-            uint32_t w[8];
-            if (blk < nb) {
-                const uint4 lo = *reinterpret_cast<const uint4*>(src + blk * 32);
-                const uint4 hi = *reinterpret_cast<const uint4*>(src + blk * 32 + 16);
-                w[0] = lo.x; w[1] = lo.y; w[2] = lo.z; w[3] = lo.w; w[4] = hi.x; w[5] = hi.y; w[6] = hi.z; w[7] = hi.w;
-            } else {
-#pragma unroll
-                for (int j = 0; j < 8; j++) w[j] = 0u;
-            }
-            uint32_t n0, n1;
-            const uint32_t code = q16_bf16(w, gs_inv, n0, n1);
-            const uint32_t c1 = __shfl_down_sync(0xFFFFFFFFu, code, 1);
-            const uint32_t c2 = __shfl_down_sync(0xFFFFFFFFu, code, 2);
-            const uint32_t c3 = __shfl_down_sync(0xFFFFFFFFu, code, 3);
-            if (blk < nb) {
-                const int64_t b = ch * RING_BLOCKS + blk;
-                *reinterpret_cast<uint2*>(packed + b * 8) = make_uint2(n0, n1);
-                if ((lane & 3) == 0) {
-                    const int64_t off = ((row >> 7) * katoms + (col >> 6)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4;
-                    *reinterpret_cast<uint32_t*>(sf + off) = code | (c1 << 8) | (c2 << 16) | (c3 << 24);
-                }
-            }
-            row += dri;
-            col += dci;
-            if (col >= cols) { col -= cols; row++; }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty_bar(st));
-        if (++st == RING_STAGES) { st = 0; ph ^= 1u; }
-        row += drn;
-        col += dcn;
-        while (col >= cols) { col -= cols; row++; }
-    }
-}
-
 // Scale words of the padding rows of the last 128-row group (rows .. ceil(rows/128)*128 - 1):
 // zero, as the layout requires for rows that do not exist.
 __global__ void sf_pad_kernel(uint8_t* __restrict__ sf, int64_t rows, int64_t cols) {
@@ -453,34 +330,9 @@ static nvfp4_status_t launch_quantize(const void* x, int64_t rows, int64_t cols,
     const auto* xp = reinterpret_cast<const __nv_bfloat16*>(x);
     auto* pp = reinterpret_cast<uint8_t*>(packed);
     auto* sp = reinterpret_cast<uint8_t*>(sf);
-#ifdef QUANT_RING
-    static bool ring_attr[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !ring_attr[dev]) {
-        cudaFuncSetAttribute(quantize_ring_kernel<kDevScale>, cudaFuncAttributeMaxDynamicSharedMemorySize, RING_SMEM);
-        ring_attr[dev] = true;
-    }
-    const int64_t rchunks = (nblocks + RING_BLOCKS - 1) / RING_BLOCKS;
-    const int64_t rgrid = rchunks < 2 * (int64_t)sm_count() ? rchunks : 2 * (int64_t)sm_count();
-    cudaLaunchAttribute rattr[1];
-    rattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    rattr[0].val.programmaticStreamSerializationAllowed = 1;
-    cudaLaunchConfig_t rcfg = {};
-    rcfg.gridDim = dim3((unsigned)rgrid, 1, 1);
-    rcfg.blockDim = dim3(RING_THREADS, 1, 1);
-    rcfg.dynamicSmemBytes = RING_SMEM;
-    rcfg.stream = s;
-    rcfg.attrs = rattr;
-    rcfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&rcfg, quantize_ring_kernel<kDevScale>, xp, rows, cols, gs, amax_word, gs_out,
-                                             pp, sp);
-    (void)grid;
-#else
     const cudaError_t e = ((reinterpret_cast<uintptr_t>(x) & 31) == 0)
         ? launch_pdl(quantize_kernel<kDevScale, true>, (unsigned)grid, QR_THREADS, s, xp, rows, cols, gs, amax_word, gs_out, pp, sp)
         : launch_pdl(quantize_kernel<kDevScale, false>, (unsigned)grid, QR_THREADS, s, xp, rows, cols, gs, amax_word, gs_out, pp, sp);
-#endif
     if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "quantize_kernel: %s", cudaGetErrorString(e));
     nvfp4_status_t st = check_launch("quantize_kernel");
     if (st != NVFP4_OK || rows % 128 == 0) return st;
