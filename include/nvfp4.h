@@ -239,7 +239,8 @@ NVFP4_API nvfp4_status_t nvfp4_ar_set_timeout(nvfp4_ar_t h, uint64_t timeout_ns)
  * restarts its epoch count.  Synchronises the device.  Every rank must call it, with no all-reduce of any rank in
  * flight (synchronise all ranks first, e.g. with a host barrier), before the next call. */
 NVFP4_API nvfp4_status_t nvfp4_ar_reset(nvfp4_ar_t h);
-/* The algorithm NVFP4_AR_AUTO resolves to. */
+/* The algorithm NVFP4_AR_AUTO resolves to: LOWLAT up to NVFP4_AR_LOWLAT_MAX_BYTES of bf16, then
+ * ONESHOT (always with two ranks, up to NVFP4_AR_ONESHOT_MAX_BYTES with more), then TWOSHOT. */
 NVFP4_API int nvfp4_ar_choose_algo(int world, int64_t numel);
 /* NVFP4 all-reduce: numel % (32 * world) == 0, 16-byte aligned bf16 buffers on this rank's GPU;
  * in and out may not alias. */

@@ -978,6 +978,10 @@ int nvfp4_ar_choose_algo(int world, int64_t numel) {
     // needs one barrier: better than two-shot while the call is latency-bound (measured
     // crossover on 8 x B200 between 4 and 8 MB of bf16)
     if (numel * 2 <= NVFP4_AR_LOWLAT_MAX_BYTES) return NVFP4_AR_LOWLAT;
+    // with two ranks the two-shot sends as many bytes as the one-shot (half the payload, twice)
+    // and adds a barrier and a pass over HBM: one-shot at every size (measured on 2 x B200 from
+    // 4 MB to 256 MB of bf16: 17.5 vs 26.1 us ... 221 vs 254 us)
+    if (world == 2) return NVFP4_AR_ONESHOT;
     return numel * 2 <= NVFP4_AR_ONESHOT_MAX_BYTES ? NVFP4_AR_ONESHOT : NVFP4_AR_TWOSHOT;
 }
 

@@ -78,6 +78,8 @@ def test_buffer_bytes_and_algo_choice(nv):
     assert L.nvfp4_ar_choose_algo(8, (1 << 20) // 2 + 256) == 1
     assert L.nvfp4_ar_choose_algo(8, (4 << 20) // 2) == 1          # 4 MB of bf16: one-shot
     assert L.nvfp4_ar_choose_algo(8, (4 << 20) // 2 + 256) == 2    # above: two-shot
+    assert L.nvfp4_ar_choose_algo(2, 1024) == 3
+    assert L.nvfp4_ar_choose_algo(2, 1 << 30) == 1                  # two ranks: one-shot at any size
 
 
 def test_create_rejects_bad_arguments(nv):
