@@ -347,7 +347,8 @@ def decode_bench(nv, steps, warmup, flush):
                        "timing": "back-to-back calls over 8 different B (264 MB > L2), one event pair",
                        "us_per_call_weights_const": round(ms_stream_wc * 1e3, 2),
                        "frac_weights_const": round(byts / (ms_stream_wc * 1e-3) / 1e9 / hbm, 4)},
-            "launches_per_call": 2}
+            # the in-cluster split-K reduction needs no workspace and no second kernel
+            "launches_per_call": 1 if int(nv.lib().nvfp4_gemm_workspace_bytes(M, N, K)) == 0 else 2}
 
 
 def gemm_quantize_bench(nv, steps, flush):

@@ -14,15 +14,17 @@
 //   g % 2 == k), warp 14 scale TMA producer.  The scale warps move the scale atoms shared memory ->
 //   registers -> TMEM with tcgen05.st into a ring of TMEM slots and then arrive (in both CTAs)
 //   on the leader's "full" barrier of the stage, which therefore completes when A/B have landed
-//   AND the scales are in TMEM: the MMA thread makes one wait per stage.  It issues four
+//   AND the scales are in TMEM.  It issues four
 //   tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X (M256 N256 K64) per stage
 //   and releases the stage (shared memory and scale slot) in both CTAs with one tcgen05.commit
 //   carrying a CTA mask.
 //   Measured on B200 (probes of the MMA-issuing thread, M256 N256 K64 MMAs): an mbarrier wait in
 //   that thread costs tensor-pipe time even when the phase completed long ago -- with 4 MMAs per
 //   wait, try_wait runs the pipe at ~5.7 PFLOP/s and test_wait at ~6.8, against 8.1 without
-//   waits; with 8 MMAs per wait the loss is gone.  Hence one wait per stage, polled with
-//   test_wait.  The commit itself costs nothing.
+//   waits; with 8 MMAs per wait the loss is gone.  Hence the MMA thread waits once per PAIR of
+//   stages, polled with test_wait: one leader scale warp arrives on the second stage's "full"
+//   barrier only after the first stage's has completed, so the second barrier stands for both.
+//   The commit itself costs nothing.
 //   Scales do not go through tcgen05.cp: tcgen05 operations execute in issue order in the
 //   tensor pipe, so a copy issued by the MMA thread waits for every MMA queued before it and
 //   drains the pipe, and copies from another thread still occupy the pipe (measured on B200:
@@ -330,25 +332,32 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                 }
                 tc_fence_after();
                 const uint32_t dcol = (iter & 1) ? ACC1_COL : 0;
-                for (int kb = 0; kb < nkb; kb++) {
-                    // A/B of the stage have landed and its scales are in TMEM.  One wait per
-                    // stage: each wait in this thread costs tensor-pipe time.
-                    if (!mbar_wait_spin(full_bar(stage), phase, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA)) {
+                for (int kb = 0; kb < nkb; kb += 2) {
+                    // Stages go in pairs (kb, kb + 1): the scale warps complete the second
+                    // stage's "full" barrier only after the first one's, so one wait here covers
+                    // both (A/B landed, scales in TMEM) and the thread waits once per 8 MMAs --
+                    // each wait in this thread costs tensor-pipe time.
+                    const int nst = kb + 1 < nkb ? 2 : 1;
+                    const int s2 = (nst == 2 && stage + 1 == STAGES) ? 0 : stage + nst - 1;
+                    const uint32_t ph2 = (nst == 2 && stage + 1 == STAGES) ? (phase ^ 1u) : phase;
+                    if (!mbar_wait_spin(full_bar(s2), ph2, WAIT_LIMIT_NS, DEV_TIMEOUT_GEMM_MMA)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = base + OFF_A + stage * A_BYTES;
-                    const uint32_t b0 = base + OFF_B + stage * B_BYTES;
-                    const uint32_t scol = tmem + SF_RING_COL + SF_SLOT_COLS * sf_slot;
+                    for (int h = 0; h < nst; h++) {
+                        const uint32_t a0 = base + OFF_A + stage * A_BYTES;
+                        const uint32_t b0 = base + OFF_B + stage * B_BYTES;
+                        const uint32_t scol = tmem + SF_RING_COL + SF_SLOT_COLS * sf_slot;
 #pragma unroll
-                    for (int j = 0; j < 4; j++)
-                        tc_mma2(tmem + dcol, desc_sw128(a0 + 32 * j), desc_sw128(b0 + 32 * j), scol + 12 * j,
-                                scol + 12 * j + 4, (kb | j) != 0);
-                    // releases the stage's shared memory (producer) and its scale slot (scale warps)
-                    tc_commit2_pair(empty_bar(stage));
-                    if (++sf_slot == SF_SLOTS) sf_slot = 0;
-                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                        for (int j = 0; j < 4; j++)
+                            tc_mma2(tmem + dcol, desc_sw128(a0 + 32 * j), desc_sw128(b0 + 32 * j), scol + 12 * j,
+                                    scol + 12 * j + 4, ((kb + h) | j) != 0);
+                        // releases the stage's shared memory (producer) and its scale slot (scale warps)
+                        tc_commit2_pair(empty_bar(stage));
+                        if (++sf_slot == SF_SLOTS) sf_slot = 0;
+                        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                    }
                 }
                 if (!ok) break;
                 tc_commit2_pair(tmem_full);
@@ -452,8 +461,21 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
                 // before this arrival, so a relaxed arrival hands the slot over.  A release at
                 // cluster scope costs ~1300 cycles per arrival here (measured), more than a stage.
                 if (lane == 0) {
-                    if (leader) mbar_arrive_relaxed(full_bar(stage));
-                    else mbar_arrive_remote_relaxed(mapa(full_bar(stage), 0));
+                    if (leader && q == 0 && (kb & 1)) {
+                        // second stage of an MMA pair (kb - 1, kb): arrive only once the first
+                        // stage's "full" phase has completed, with release semantics, so that
+                        // this barrier's completion implies the other's (the MMA thread waits on
+                        // this one alone).  A timed-out wait is recorded; the MMA thread's own
+                        // bounded wait then ends the kernel.
+                        const long p = g - 1;
+                        if (mbar_wait(full_bar((int)(p % STAGES)), (uint32_t)((p / STAGES) & 1), WAIT_LIMIT_NS,
+                                      DEV_TIMEOUT_GEMM_SF))
+                            mbar_arrive(full_bar(stage));
+                    } else if (leader) {
+                        mbar_arrive_relaxed(full_bar(stage));
+                    } else {
+                        mbar_arrive_remote_relaxed(mapa(full_bar(stage), 0));
+                    }
                     mbar_arrive(sf_free(sm));                  // the atoms are in TMEM: refill the slot
                 }
                 if (++sf_slot == SF_SLOTS) sf_slot = 0;
