@@ -545,11 +545,14 @@ def fp4_peak_measure(local):
     from tensorcore_ptx_example_b200 import diag
     sampler = ClockSampler(local)
     sampler.start()
+    diag.mma_peak_clock()                                    # reset the in-kernel clock counters
     tf = diag.mma_peak(cta_group=2, iters=32768, repeats=5, random_operands=True)
+    mhz = diag.mma_peak_clock()
     clocks = sampler.stop()
     assert diag.device_status() == 0
-    return {"tflops": round(tf, 1), "clocks": clocks,
-            "probe": "nvfp4_diag_mma_peak cta_group 2, 32768 MMAs per SM pair, random operands, best of 5"}
+    return {"tflops": round(tf, 1), "clocks": clocks, "sm_mhz_in_kernel": round(mhz, 1),
+            "probe": "nvfp4_diag_mma_peak cta_group 2, 32768 MMAs per SM pair, random operands, best of 5; "
+                     "sm_mhz_in_kernel = SM cycles / elapsed ns inside the probe's CTAs (clock64, globaltimer)"}
 
 
 def run_gemm_line(args):
@@ -762,6 +765,48 @@ def _ar_time_b2b(fn, calls, warmup, world):
     return max_over_ranks(e0.elapsed_time(e1) / calls, world)
 
 
+ROT_BYTES = 192 << 20     # inputs rotated through by back-to-back timed calls: more than the 126 MB L2
+
+
+def rotating_inputs(x, min_bytes=ROT_BYTES):
+    """Copies of x at distinct places of one buffer of at least min_bytes (more than L2): calls
+    that take them in turn read their input from HBM, as after an L2 flush, with neither a flush
+    nor a host gap between calls.  Every copy holds x, so every call computes the same result."""
+    n = x.numel()
+    sets = max(2, -(-min_bytes // (x.element_size() * n)))
+    buf = x.reshape(1, -1).expand(sets, -1).contiguous()
+    return [buf[i] for i in range(sets)]
+
+
+def _ar_time_rot(fn, xs, steps, warmup, world, sampler=None):
+    """Per-call device time (ms) of `steps` back-to-back calls fn(xs[i % len(xs)]) between one
+    pair of events, max over ranks: the reference harness's method (bench_ar.cu:965-972) with
+    the input rotating through more than L2.  Barrier and synchronize on both sides; the GPU
+    spins while the host queues the calls, and one untimed call lines the ranks up (every call
+    meets its peers, whose clocks and queues differ), so the region holds device time only.
+    With a sampler, it runs from before the first barrier to after the region."""
+    import torch
+    for i in range(warmup):
+        fn(xs[i % len(xs)])
+    if sampler is not None:
+        sampler.start()
+    torch.cuda.synchronize()
+    barrier(world)
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(HIDE_HOST_CYCLES * max(1, steps // 4))
+    fn(xs[-1])
+    e0.record(s)
+    for i in range(steps):
+        fn(xs[i % len(xs)])
+    e1.record(s)
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler is not None else None
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    return (ms, clocks) if sampler is not None else ms
+
+
 def _wire_bytes(name, numel, world, payload_bytes_per_elt):
     """Bytes one rank sends over NVLink per call: two-shot 2 (n-1)/n of the payload, one-shot
     (n-1) times the payload."""
@@ -850,21 +895,22 @@ def ar_parity(ctx, x, out, gs, world, rank, windows=12, win=8192, nvls=False):
     return res
 
 
-def allreduce_algos(ctx, x, out, gs, world, steps, flush, nvls=False):
-    """cfg4, every algorithm: device time per call (max over ranks, L2 flushed between calls),
-    and the NVFP4 error against the exact fp32 sum."""
+def allreduce_algos(ctx, xs, out, gs, world, steps, nvls=False):
+    """cfg4, every algorithm: device time per call of back-to-back calls over rotating inputs (max
+    over ranks), and the NVFP4 error against the exact fp32 sum."""
     import torch
     import torch.distributed as dist
+    x = xs[0]
     numel = x.numel()
     res = {}
-    runs = [("nvfp4_twoshot", lambda: ctx.allreduce(x, out, global_scale=gs, algo="twoshot"), 0.5625),
-            ("nvfp4_oneshot", lambda: ctx.allreduce(x, out, global_scale=gs, algo="oneshot"), 0.5625),
-            ("bf16_twoshot", lambda: ctx.bf16_allreduce(x, out, algo="twoshot"), 2.0),
-            ("bf16_oneshot", lambda: ctx.bf16_allreduce(x, out, algo="oneshot"), 2.0)]
+    runs = [("nvfp4_twoshot", lambda xi: ctx.allreduce(xi, out, global_scale=gs, algo="twoshot"), 0.5625),
+            ("nvfp4_oneshot", lambda xi: ctx.allreduce(xi, out, global_scale=gs, algo="oneshot"), 0.5625),
+            ("bf16_twoshot", lambda xi: ctx.bf16_allreduce(xi, out, algo="twoshot"), 2.0),
+            ("bf16_oneshot", lambda xi: ctx.bf16_allreduce(xi, out, algo="oneshot"), 2.0)]
     if nvls:
-        runs.append(("bf16_nvls", lambda: ctx.bf16_allreduce(x, out, algo="nvls"), 2.0))
+        runs.append(("bf16_nvls", lambda xi: ctx.bf16_allreduce(xi, out, algo="nvls"), 2.0))
     for name, fn, bpe in runs:
-        res[name] = _ar_entry(name, numel, world, _ar_time(fn, steps, 3, flush, world), bpe)
+        res[name] = _ar_entry(name, numel, world, _ar_time_rot(fn, xs, steps, 3, world), bpe)
     exact = x.float().clone()
     dist.all_reduce(exact)
     for algo in ("twoshot", "oneshot"):
@@ -912,14 +958,15 @@ def ar_sweep_rows(ctx, xfull, ofull, gs, world, sizes=SWEEP_ROWS_BYTES, nvls=Fal
     return rows
 
 
-def reference_ar_kernels(world, rank, x, gs, steps, flush, exact):
+def reference_ar_kernels(world, rank, xs, gs, steps, exact):
     """Same-box baseline: the reference's own fused two-shot and one-shot kernels
     (launch_fused_rank / launch_oneshot_fused_rank, nvfp4_allreduce.cuh:650-682), compiled from
     the reference header into oracle/_ref/libref_ar.so, on the same GPUs and inputs (SFScaleVal =
     1 / gs), their buffers shared through CUDA IPC: device time per call (max over ranks) and
     error against the exact fp32 sum.  Each grid is the launcher's NVLink default capped at the
     blocks that are resident at once (the fused kernels' block barriers wait for the same block
-    index on every rank).  Every rank takes the same steps; the kernels launch only after every
+    index on every rank).  Timed like this repository's kernels: back-to-back calls over the same
+    rotating inputs.  Every rank takes the same steps; the kernels launch only after every
     rank has confirmed its buffers and peer mappings."""
     import ctypes
 
@@ -942,6 +989,7 @@ def reference_ar_kernels(world, rank, x, gs, steps, flush, exact):
     if not all_ok(py_oracle.ref_ar_available() and world in (2, 4, 8)):
         return {"unavailable": "oracle/_ref/libref_ar.so not built, or world not in {2, 4, 8}"}
     L = py_oracle.ref_ar_lib()
+    x = xs[0]
     numel = x.numel()
     shard = numel // world
     sizes = {"comm2": L.ref_fused_comm_bytes(shard, world), "bin": 4 * L.ref_fused_barrier_words(world),
@@ -988,27 +1036,27 @@ def reference_ar_kernels(world, rank, x, gs, steps, flush, exact):
         out = torch.empty_like(x)
         sf_val = float(np.float32(1.0) / np.float32(gs))
         st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-        xp, op = ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(out.data_ptr())
+        op = ctypes.c_void_p(out.data_ptr())
         flags = {"two": 0, "one": 0}
 
-        def twoshot():
+        def twoshot(xi):
             flags["two"] += 1
-            rc = L.ref_launch_twoshot(world, xp, op, arrays["comm2"], arrays["bin"], arrays["bout"], rank, numel,
+            rc = L.ref_launch_twoshot(world, ctypes.c_void_p(xi.data_ptr()), op, arrays["comm2"], arrays["bin"], arrays["bout"], rank, numel,
                                       sf_val, flags["two"], st, grid2)
             if rc:
                 raise RuntimeError(f"ref_launch_twoshot: cuda error {rc}")
 
-        def oneshot():
+        def oneshot(xi):
             flags["one"] += 1
-            rc = L.ref_launch_oneshot(world, xp, op, arrays["comm1"], arrays["bar1"], rank, numel, sf_val,
+            rc = L.ref_launch_oneshot(world, ctypes.c_void_p(xi.data_ptr()), op, arrays["comm1"], arrays["bar1"], rank, numel, sf_val,
                                       flags["one"], st, grid1)
             if rc:
                 raise RuntimeError(f"ref_launch_oneshot: cuda error {rc}")
 
         for name, fn in (("reference_twoshot", twoshot), ("reference_oneshot", oneshot)):
-            ms = _ar_time(fn, steps, 3, flush, world)
+            ms = _ar_time_rot(fn, xs, steps, 3, world)
             e = _ar_entry(name, numel, world, ms, 0.5625)
-            fn()
+            fn(x)
             o = out.float()
             e["rel_rmse_vs_fp32_sum"] = round(float((o - exact).norm() / exact.norm()), 5)
             e["grid"] = grid2 if "two" in name else grid1
@@ -1070,28 +1118,21 @@ def run_allreduce_line(args):
     algo = {ar.ONESHOT: "oneshot", ar.TWOSHOT: "twoshot", ar.LOWLAT: "lowlat"}[ar.choose_algo(world, numel)]
     extra = {}
     try:
-        fn = lambda: ctx.allreduce(x, out, global_scale=gs, algo="auto")  # noqa: E731
-        for _ in range(args.warmup):
-            fn()
-        # the sampler starts first (its NVML set-up takes a varying while on each rank); the
-        # barrier right before the timed steps lines the ranks up
-        sampler = ClockSampler(local)
-        sampler.start()
-        torch.cuda.synchronize()
-        barrier(world)
-        fn()                  # untimed: its own barrier lines up the GPUs' timelines
-        ts = timed_steps(fn, args.steps, flush)
-        clocks = sampler.stop()
-        barrier(world)
-        total_ms = max_over_ranks(sum(ts), world)
-        mean_ms = max_over_ranks(sum(ts) / len(ts), world)
+        # K back-to-back steps over copies of the input that together exceed L2 (each step
+        # reads its input from HBM); the sampler starts before the barrier (its NVML set-up takes
+        # a varying while on each rank)
+        xs = rotating_inputs(x)
+        nsets = len(xs)
+        fn = lambda xi: ctx.allreduce(xi, out, global_scale=gs, algo="auto")  # noqa: E731
+        mean_ms, clocks = _ar_time_rot(fn, xs, args.steps, args.warmup, world, sampler=ClockSampler(local))
+        total_ms = mean_ms * args.steps
         status = nv.device_status()
         value = 2.0 * numel * args.steps / (total_ms * 1e-3) / 1e9
         wire = _wire_bytes(algo, numel, world, 0.5625)
         achieved = wire / (mean_ms * 1e-3) / 1e9
 
         parity = ar_parity(ctx, x, out, gs, world, rank, nvls=nvls)
-        algos, exact = allreduce_algos(ctx, x, out, gs, world, max(5, min(args.steps, 20)), flush, nvls=nvls)
+        algos, exact = allreduce_algos(ctx, xs, out, gs, world, max(5, min(args.steps, 20)), nvls=nvls)
 
         # end to end through the public API with host buffers: the input copied from pinned
         # host memory and the result copied back every step (pipelined like the GEMM's)
@@ -1119,7 +1160,8 @@ def run_allreduce_line(args):
         extra[key] = fn_()
     # the reference's kernels last: they wait without a time limit, so they run only after every
     # measurement of ours is in
-    extra["reference_kernels"] = reference_ar_kernels(world, rank, x, gs, max(5, min(args.steps, 20)), flush, exact)
+    extra["reference_kernels"] = reference_ar_kernels(world, rank, xs, gs, max(5, min(args.steps, 20)), exact)
+    del xs
 
     line = {
         "metric": METRIC,
@@ -1137,7 +1179,8 @@ def run_allreduce_line(args):
         "config": {"workload": f"cfg4 NVFP4 all-reduce, {rows}x{cols} bf16 per rank", "numel_per_rank": numel,
                    "algorithm": f"NVFP4_AR_AUTO -> {algo}", "parallelism": f"all-reduce over {world} GPUs (NVLink P2P)",
                    "value_convention": "bf16-equivalent algbw = 2 * numel_per_rank / t (nccl-tests)",
-                   "l2": "flushed between timed steps (256 MB write, then 256 MB read); input 58.7 MB per rank"},
+                   "l2": f"inputs larger than L2: back-to-back steps rotate through {nsets} copies of the "
+                         f"58.7 MB input ({nsets * numel * 2 / 1e6:.0f} MB per rank), one event pair around K steps"},
         "busbw_gbs": round(value * 2.0 * (world - 1) / world, 1),
         "roofline": {"bound": "nvlink", "achieved": round(achieved, 1), "peak": NVLINK_PEER_GBS, "unit": "GB/s",
                      "frac": round(achieved / NVLINK_PEER_GBS, 4),

@@ -62,6 +62,9 @@ NVFP4_DIAG_API nvfp4_status_t nvfp4_diag_mma_tile(const void* A, const void* sfa
  * FLOPs = 2 * 128 * 256 * 64 * iters * (number of SMs); time it with events around the call.
  * The measured rate is the roofline denominator of nvfp4_gemm_bf16. */
 NVFP4_DIAG_API nvfp4_status_t nvfp4_diag_mma_peak(int cta_group, int iters, int random_operands, void* stream);
+/* Effective SM clock (MHz: SM cycles / elapsed ns, summed over CTAs) of the nvfp4_diag_mma_peak
+ * launches since the previous call (synchronises the device; resets the counters). */
+NVFP4_DIAG_API nvfp4_status_t nvfp4_diag_mma_peak_clock(double* mhz);
 
 #ifdef __cplusplus
 }

@@ -15,6 +15,12 @@ namespace diag {
 
 constexpr int MMA_GROUP = 32;
 
+// Effective SM clock of the launches since the last read: per CTA, thread 0 adds the SM cycles
+// (clock64) and nanoseconds (globaltimer) between its start and its end.  Under a power limit the
+// SM clock drops below the reported application clock while the tensor pipe is busy, so the
+// rate is quoted together with the clock it ran at.
+__device__ unsigned long long peak_clock[3];          // cycles, ns, CTAs
+
 // Shared memory: A 16 KB (128 rows x 128 B) | B 32 KB (256 rows; a pair CTA reads 128) | one
 // scale atom 512 B.  Every operand the MMAs read lies inside this buffer.
 constexpr int PEAK_A = 16384, PEAK_B = 32768, PEAK_SF = 512;
@@ -27,6 +33,7 @@ static_assert(PEAK_SMEM >= PEAK_SMEM_USED, "peak kernel buffer");
 template <int kCtaGroup>
 __global__ void __launch_bounds__(128, 1) mma_peak_kernel(int iters, int random_operands) {
     extern __shared__ uint8_t peak_raw[];
+    const unsigned long long c_start = clock64(), t_start = globaltimer_ns();
     __shared__ __align__(8) uint64_t bars[2];
     __shared__ uint32_t tmem_slot;
     const uint32_t raw_addr = smem_u32(peak_raw);
@@ -121,6 +128,11 @@ __global__ void __launch_bounds__(128, 1) mma_peak_kernel(int iters, int random_
     __syncthreads();
     if constexpr (kCtaGroup == 2) asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
     tc_fence_after();
+    if (threadIdx.x == 0) {
+        atomicAdd(&peak_clock[0], clock64() - c_start);
+        atomicAdd(&peak_clock[1], globaltimer_ns() - t_start);
+        atomicAdd(&peak_clock[2], 1ull);
+    }
     if (warp == 0) {
         if constexpr (kCtaGroup == 2) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(tmem));
         else asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
@@ -161,6 +173,18 @@ nvfp4_status_t nvfp4_diag_mma_peak(int cta_group, int iters, int random_operands
         if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "diag_mma_peak: %s", cudaGetErrorString(e));
     }
     return check_launch("mma_peak_kernel");
+}
+
+nvfp4_status_t nvfp4_diag_mma_peak_clock(double* mhz) {
+    clear_error();
+    if (!mhz) return fail(NVFP4_ERR_INVALID_ARG, "diag_mma_peak_clock: null output");
+    unsigned long long v[3] = {0, 0, 0};
+    cudaError_t e = cudaMemcpyFromSymbol(v, diag::peak_clock, sizeof(v));
+    const unsigned long long z[3] = {0, 0, 0};
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(diag::peak_clock, z, sizeof(z));
+    if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "diag_mma_peak_clock: %s", cudaGetErrorString(e));
+    *mhz = v[1] ? (double)v[0] / (double)v[1] * 1e3 : 0.0;
+    return NVFP4_OK;
 }
 
 }  // extern "C"

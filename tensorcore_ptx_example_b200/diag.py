@@ -22,6 +22,7 @@ SIGNATURES = {
     "nvfp4_diag_rcp_approx": (_I, [_P, _P, _I64, _P]),
     "nvfp4_diag_mma_tile": (_I, [_P, _P, _P, _P, _P, _P]),
     "nvfp4_diag_mma_peak": (_I, [_I, _I, _I, _P]),
+    "nvfp4_diag_mma_peak_clock": (_I, [ctypes.POINTER(ctypes.c_double)]),
 }
 
 _lib = None
@@ -103,3 +104,10 @@ def mma_peak(cta_group: int = 2, iters: int = 4096, repeats: int = 3, random_ope
         b.synchronize()
         best = max(best, flops / (a.elapsed_time(b) * 1e-3) / 1e12)
     return best
+
+
+def mma_peak_clock() -> float:
+    """Effective SM clock (MHz) inside the mma_peak launches since the previous call."""
+    v = ctypes.c_double()
+    check(lib().nvfp4_diag_mma_peak_clock(ctypes.byref(v)))
+    return float(v.value)
