@@ -1373,6 +1373,13 @@ def run_only(args):
         out["dequantize_gbs"] = round(rows * cols * 2.5625 / (ms * 1e-3) / 1e9, 1)
     elif args.only == "gemm-decode":
         out = decode_bench(nv, args.steps, args.warmup, flush)
+    elif args.only == "mma-peak":
+        # the FP4 MMA issue-rate probe alone (the GEMM's roofline), with its in-kernel SM clock
+        from tensorcore_ptx_example_b200 import diag
+        diag.mma_peak_clock()
+        tf = diag.mma_peak(cta_group=2, iters=32768, repeats=max(1, args.steps), random_operands=True)
+        out = {"workload": "FP4 MMA issue-rate probe (nvfp4_diag_mma_peak, cta_group 2, 32768 MMAs per pair)",
+               "tflops": round(tf, 1), "sm_mhz_in_kernel": round(diag.mma_peak_clock(), 1)}
     elif args.only == "gemm-quantize":
         out = gemm_quantize_bench(nv, args.steps, flush)
     elif args.only == "ar-emulated":
@@ -1444,7 +1451,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--numel", type=int, default=4 << 20, help="elements per rank for --only ar-emulated")
     ap.add_argument("--only", choices=["gemm", "gemm-decode", "gemm-quantize", "quantize", "ar-sweep", "ar-emulated",
-                                       "gemm-ar-emulated"],
+                                       "gemm-ar-emulated", "mma-peak"],
                     default=None,
                     help="profiling mode: run one workload (warmup + steps launches) and print its "
                          "timings; not the benchmark line")

@@ -172,13 +172,12 @@ __device__ bool block_barrier(const Params& p, uint32_t value) {
 }
 
 // ---------------------------------------------------------------- NVFP4 codec ----
-// The 64 bytes of 32 bf16 values at x (16-byte aligned).
-__device__ __forceinline__ void load_raw32(const __nv_bfloat16* x, uint4* raw) {
+// 32 bf16 values at x (16-byte aligned) -> 16 packed bytes + 2 scale bytes (block 0 low byte); the
+// four 16-byte loads are issued before any arithmetic.
+__device__ __forceinline__ void quant32(const __nv_bfloat16* x, float gs_inv, uint4& packed, uint32_t& scales) {
+    uint4 raw[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) raw[i] = ld_nc_v4(reinterpret_cast<const uint8_t*>(x) + 16 * i);
-}
-// 32 bf16 values (as loaded by load_raw32) -> 16 packed bytes + 2 scale bytes (block 0 low byte).
-__device__ __forceinline__ void quant_raw32(const uint4* raw, float gs_inv, uint4& packed, uint32_t& scales) {
     uint32_t w[4];
     scales = 0;
 #pragma unroll
@@ -188,11 +187,6 @@ __device__ __forceinline__ void quant_raw32(const uint4* raw, float gs_inv, uint
         scales |= q16_bf16(q, gs_inv, w[2 * b], w[2 * b + 1]) << (8 * b);
     }
     packed = make_uint4(w[0], w[1], w[2], w[3]);
-}
-__device__ __forceinline__ void quant32(const __nv_bfloat16* x, float gs_inv, uint4& packed, uint32_t& scales) {
-    uint4 raw[4];
-    load_raw32(x, raw);
-    quant_raw32(raw, gs_inv, packed, scales);
 }
 // Same from 32 fp32 values.
 __device__ __forceinline__ void quant32f(const float* v, float gs_inv, uint4& packed, uint32_t& scales) {
@@ -239,34 +233,16 @@ __device__ __forceinline__ void get_chunk(const uint8_t* src, int64_t n, int64_t
     scales = ld_cg_u16(src + align16(n / 2) + c * 2);
 }
 
-// acc = sum over s = 0..n-1 (in that order) of dequant(slot s, chunk c): the loads of two slots
-// are issued before either is accumulated (more would not fit the 64 registers that keep two
-// 512-thread blocks per SM), halving the memory round trips per chunk.
-template <typename SlotFn>
-__device__ __forceinline__ void sum_slots(SlotFn slot, int n, int64_t slot_elems, int64_t c, float gs, float* acc) {
-#pragma unroll
-    for (int i = 0; i < 32; i++) acc[i] = 0.0f;
-#pragma unroll
-    for (int s0 = 0; s0 < AR_MAX_WORLD; s0 += 2) {
-        if (s0 >= n) break;
-        uint4 pk[2];
-        uint32_t sc[2];
-#pragma unroll
-        for (int j = 0; j < 2; j++)
-            if (s0 + j < n) get_chunk(slot(s0 + j), slot_elems, c, pk[j], sc[j]);
-#pragma unroll
-        for (int j = 0; j < 2; j++)
-            if (s0 + j < n) dq32_acc(pk[j], sc[j], gs, acc);
-    }
-}
-
 // ---------------------------------------------------------------- NVFP4 kernels ----
-// Every phase walks this block's chunks (c = first, first + stride, ...).  Loops over ranks or
-// shards prefetch: the next shard's input is loaded while the current one is quantized and pushed
-// (phase A), every slot of a chunk is loaded before the sum (phases B and the one-shot's second
-// phase), and the next owner's reduced chunk is loaded while the current one is written (phase C).
+// Every phase is a grid-stride loop over chunks of 32 elements (one chunk per thread per pass); a
+// thread handles a chunk's every rank or shard in turn.  Measured on 2 x B200 against variants
+// that prefetched the next rank's or shard's data, split (shard, chunk) pairs over a block's
+// threads, or ran two 512-thread blocks per SM (cfg4, back-to-back calls): two-shot 58.9-59.5 us
+// here against 61.0 and 66.2 us, and 22 against 27-28 us at 4 MB of bf16 (one-shot 15 vs 18 us);
+// the prefetching one-shot was 2 % faster at cfg4 only.  (Emulated on one GPU, where every
+// "remote" access is local, the other variants were faster: the NVLink round trips decide.)
 template <bool kTwoShot>
-__global__ void __launch_bounds__(AR_THREADS, 2) ar_nvfp4_kernel(const Params p) {
+__global__ void __launch_bounds__(AR_THREADS) ar_nvfp4_kernel(const Params p) {
     const int n = p.world, me = p.rank;
     const float gs_inv = __fdiv_rn(1.0f, p.gs);
     const uint32_t v1 = p.epoch * 2u + 1u, v2 = p.epoch * 2u + 2u;
@@ -291,58 +267,42 @@ __global__ void __launch_bounds__(AR_THREADS, 2) ar_nvfp4_kernel(const Params p)
         if (fused || p.phase == 1) {
             for (int64_t c = first; c < chunks; c += stride) {
                 float acc[32];
-                sum_slots([&](int s) { return in_slot(p, me, s); }, n, p.numel, c, p.gs, acc);   // order 0 .. n-1
+#pragma unroll
+                for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+                for (int s = 0; s < n; s++) {                  // fixed sum order 0 .. n-1
+                    uint4 pk;
+                    uint32_t sc;
+                    get_chunk(in_slot(p, me, s), p.numel, c, pk, sc);
+                    dq32_acc(pk, sc, p.gs, acc);
+                }
                 store_bf16x32(p.out + c * 32, acc);
             }
         }
         return;
     }
 
-    // Two-shot.  Block b owns the contiguous chunk range [c0, c1) of every shard, the same range
-    // on every rank, in every phase (so a phase needs block b of every rank, and no other block, to
-    // have finished the previous one).  Phases A and C work on (shard, chunk) pairs: the block's
-    // threads split the n x (c1 - c0) pairs, so every thread has independent work even when a
-    // block owns few chunks; each thread keeps the loads of two pairs in flight.  Pair order is
-    // shard-major with the shards rotated (rank me+1 first), so the ranks start on different
-    // peers.
     const int64_t shard = p.numel / n;
     const int64_t schunks = shard / 32;
-    const int64_t cpb = (schunks + gridDim.x - 1) / gridDim.x;
-    const int64_t c0 = (int64_t)blockIdx.x * cpb;
-    // per-block counts fit 32 bits (launch_nvfp4 checks n * cpb < 2^31): 32-bit division below
-    const uint32_t ncb = (uint32_t)(c0 < schunks ? (schunks - c0 < cpb ? schunks - c0 : cpb) : 0);
-    const uint32_t pairs = (uint32_t)n * ncb;
-    const uint32_t T = blockDim.x, t = threadIdx.x;
     if (p.phase == -3 || p.phase == 3) {
         // the shards were quantized by the producer of the data (a GEMM epilogue): push them
-        for (uint32_t i = t; i < pairs; i += T) {
-            const int o = (me + 1 + (int)(i / ncb)) % n;
-            const int64_t c = c0 + i % ncb;
-            const int64_t e32 = (int64_t)o * schunks + c;         // chunk of 32 elements of the input
-            const uint4 pk = ld_nc_v4(p.q_codes + e32 * 16);
-            const uint32_t sc = *reinterpret_cast<const uint16_t*>(p.q_scales + e32 * 2);
-            put_chunk(in_slot(p, o, me), shard, c, pk, sc);
+        for (int64_t c = first; c < schunks; c += stride) {
+            for (int k = 1; k <= n; k++) {
+                const int o = (me + k) % n;
+                const int64_t e32 = (int64_t)o * schunks + c;     // chunk of 32 elements of the input
+                const uint4 pk = ld_nc_v4(p.q_codes + e32 * 16);
+                const uint32_t sc = *reinterpret_cast<const uint16_t*>(p.q_scales + e32 * 2);
+                put_chunk(in_slot(p, o, me), shard, c, pk, sc);
+            }
         }
     }
     if (p.phase == -1 || p.phase == 0) {
-        for (uint32_t i = t; i < pairs; i += 2 * T) {
-            uint4 raw[2][4];
-            int o[2];
-            int64_t c[2];
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                const uint32_t j = i + u * T;
-                o[u] = (me + 1 + (int)(j / ncb)) % n;
-                c[u] = c0 + j % ncb;
-                if (j < pairs) load_raw32(p.in + (int64_t)o[u] * shard + c[u] * 32, raw[u]);
-            }
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                if (i + u * T >= pairs) break;
+        for (int64_t c = first; c < schunks; c += stride) {
+            for (int k = 1; k <= n; k++) {                     // owner me+1 first, own shard last
+                const int o = (me + k) % n;
                 uint4 pk;
                 uint32_t sc;
-                quant_raw32(raw[u], gs_inv, pk, sc);
-                put_chunk(in_slot(p, o[u], me), shard, c[u], pk, sc);
+                quant32(p.in + (int64_t)o * shard + c * 32, gs_inv, pk, sc);
+                put_chunk(in_slot(p, o, me), shard, c, pk, sc);
             }
         }
     }
@@ -350,10 +310,16 @@ __global__ void __launch_bounds__(AR_THREADS, 2) ar_nvfp4_kernel(const Params p)
     const float gs_red = __fmul_rn(p.gs, (float)n);
     if (fused || p.phase == 1) {
         const float gs_red_inv = __fdiv_rn(1.0f, gs_red);
-        for (uint32_t cl = t; cl < ncb; cl += T) {
-            const int64_t c = c0 + cl;
+        for (int64_t c = first; c < schunks; c += stride) {
             float acc[32];
-            sum_slots([&](int s) { return in_slot(p, me, s); }, n, shard, c, p.gs, acc);       // order 0 .. n-1
+#pragma unroll
+            for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+            for (int s = 0; s < n; s++) {                      // fixed sum order 0 .. n-1
+                uint4 pk;
+                uint32_t sc;
+                get_chunk(in_slot(p, me, s), shard, c, pk, sc);
+                dq32_acc(pk, sc, p.gs, acc);
+            }
             uint4 pk;
             uint32_t sc;
             quant32f(acc, gs_red_inv, pk, sc);
@@ -365,26 +331,16 @@ __global__ void __launch_bounds__(AR_THREADS, 2) ar_nvfp4_kernel(const Params p)
     }
     if (fused && !block_barrier(p, v2)) return;
     if (fused || p.phase == 2) {
-        for (uint32_t i = t; i < pairs; i += 2 * T) {
-            uint4 pk[2];
-            uint32_t sc[2];
-            int o[2];
-            int64_t c[2];
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                const uint32_t j = i + u * T;
-                o[u] = (int)(j / ncb);
-                c[u] = c0 + j % ncb;
-                if (j < pairs) get_chunk(gather_slot(p, me, o[u]), shard, c[u], pk[u], sc[u]);
-            }
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                if (i + u * T >= pairs) break;
+        for (int64_t c = first; c < schunks; c += stride) {
+            for (int o = 0; o < n; o++) {
+                uint4 pk;
+                uint32_t sc;
+                get_chunk(gather_slot(p, me, o), shard, c, pk, sc);
                 float acc[32];
 #pragma unroll
-                for (int k = 0; k < 32; k++) acc[k] = 0.0f;
-                dq32_acc(pk[u], sc[u], gs_red, acc);
-                store_bf16x32(p.out + (int64_t)o[u] * shard + c[u] * 32, acc);
+                for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+                dq32_acc(pk, sc, gs_red, acc);
+                store_bf16x32(p.out + (int64_t)o * shard + c * 32, acc);
             }
         }
     }
@@ -508,8 +464,8 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float* acc) {
     return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// Loads of all ranks' chunks are issued before the first is used (the same prefetching as the NVFP4
-// kernels, so the baseline is not held back by one round trip per rank).
+// Loads of all ranks' chunks are issued before the first is used, so the baseline is not held back
+// by one round trip per rank.
 template <bool kTwoShot>
 __global__ void __launch_bounds__(AR_THREADS, 2) ar_bf16_kernel(const Params p) {
     const int n = p.world, me = p.rank;
@@ -696,7 +652,8 @@ struct nvfp4_ar {
     bool ready = false;
     uint32_t epoch = 0;
     uint64_t timeout_ns = AR_DEFAULT_TIMEOUT_NS;
-    int max_grid = 0, ll_max_grid = 0;
+    int max_grid = 0, ll_max_grid = 0;   // resident grids: bf16 / NVLS kernels, low-latency kernel
+    int nvfp4_max_grid = 0;              // resident grid of the NVFP4 one- and two-shot kernels
     uint8_t* nvls_mc = nullptr;      // NVLS buffer (nvfp4_ar_set_multicast): multicast address,
     uint8_t* nvls_uc = nullptr;      // this rank's unicast address,
     int64_t nvls_half = 0;           // bytes of one parity half
@@ -823,14 +780,15 @@ nvfp4_status_t nvfp4_ar_create(int world, int rank, int64_t max_numel, nvfp4_ar_
         cudaGetLastError();
         return fail(NVFP4_ERR_CUDA, "ar_create: %s", cudaGetErrorString(e));
     }
-    int g1 = resident_grid((const void*)ar_nvfp4_kernel<true>), g2 = resident_grid((const void*)ar_nvfp4_kernel<false>);
+    // every kernel that meets peers in block barriers keeps all its blocks resident: each family's
+    // grid is capped at the smallest resident grid of its kernels
+    const int g1 = resident_grid((const void*)ar_nvfp4_kernel<true>), g2 = resident_grid((const void*)ar_nvfp4_kernel<false>);
+    h->nvfp4_max_grid = g1 < g2 ? g1 : g2;
     int g3 = resident_grid((const void*)ar_bf16_kernel<true>), g4 = resident_grid((const void*)ar_bf16_kernel<false>);
     const int g5 = resident_grid((const void*)ar_bf16_nvls_kernel);
-    int g = g1;
-    if (g2 < g) g = g2;
-    if (g3 < g) g = g3;
+    int g = g3;
     if (g4 < g) g = g4;
-    if (g5 < g) g = g5;   // every kernel that meets peers in block barriers keeps all its blocks resident
+    if (g5 < g) g = g5;
     h->max_grid = g;
     h->ll_max_grid = resident_grid((const void*)ar_nvfp4_ll_kernel, AR_LL_THREADS);
     h->peer[rank] = h->base;
@@ -1023,11 +981,11 @@ static nvfp4_status_t launch_nvfp4_ll(nvfp4_ar_t h, const Params& p, cudaStream_
     return check_launch("ar_nvfp4_ll_kernel");
 }
 static nvfp4_status_t launch_nvfp4(nvfp4_ar_t h, const Params& p, bool twoshot, cudaStream_t s) {
+    // one chunk per thread and pass, at most the resident blocks
     const int64_t work = twoshot ? p.numel / p.world / 32 : p.numel / 32;
-    const int grid = grid_for(h, work);
-    if (twoshot && (int64_t)p.world * ((work + grid - 1) / grid) >= (int64_t(1) << 31))
-        return fail(NVFP4_ERR_INVALID_ARG, "ar_allreduce: %lld elements per rank is too many for one call",
-                    (long long)p.numel);
+    int64_t g = (work + AR_THREADS - 1) / AR_THREADS;
+    if (g > h->nvfp4_max_grid) g = h->nvfp4_max_grid;
+    const int grid = g < 1 ? 1 : (int)g;
     if (twoshot) ar_nvfp4_kernel<true><<<grid, AR_THREADS, 0, s>>>(p);
     else ar_nvfp4_kernel<false><<<grid, AR_THREADS, 0, s>>>(p);
     return check_launch("ar_nvfp4_kernel");
