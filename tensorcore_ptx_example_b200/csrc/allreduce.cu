@@ -266,14 +266,18 @@ __global__ void __launch_bounds__(AR_THREADS) ar_nvfp4_kernel(const Params p) {
         if (fused && !block_barrier(p, v1)) return;
         if (fused || p.phase == 1) {
             for (int64_t c = first; c < chunks; c += stride) {
+                // fixed sum order 0 .. n-1, the loads of two slots in flight (measured on 2 x B200:
+                // 2-5 % faster below cfg4, equal at cfg4; the same in the two-shot's sum was not faster)
                 float acc[32];
 #pragma unroll
                 for (int i = 0; i < 32; i++) acc[i] = 0.0f;
-                for (int s = 0; s < n; s++) {                  // fixed sum order 0 .. n-1
-                    uint4 pk;
-                    uint32_t sc;
-                    get_chunk(in_slot(p, me, s), p.numel, c, pk, sc);
-                    dq32_acc(pk, sc, p.gs, acc);
+                for (int s = 0; s < n; s += 2) {
+                    uint4 pk0, pk1;
+                    uint32_t sc0, sc1 = 0;
+                    get_chunk(in_slot(p, me, s), p.numel, c, pk0, sc0);
+                    if (s + 1 < n) get_chunk(in_slot(p, me, s + 1), p.numel, c, pk1, sc1);
+                    dq32_acc(pk0, sc0, p.gs, acc);
+                    if (s + 1 < n) dq32_acc(pk1, sc1, p.gs, acc);
                 }
                 store_bf16x32(p.out + c * 32, acc);
             }
