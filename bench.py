@@ -279,11 +279,11 @@ def quantize_bench(nv, steps, warmup, flush):
     }
 
 
-def decode_bench(nv, steps, warmup, flush):
-    """cfg3 decode shape M16 N7168 K8192 (HBM-bound: the kernel streams B once)."""
+def decode_bench(nv, steps, warmup, flush, shape=None):
+    """cfg3 decode shape M16 N7168 K8192 (HBM-bound: the kernel streams B once), or `shape`."""
     import torch
     from tensorcore_ptx_example_b200 import workloads
-    M, N, K = workloads.CFG3_DECODE_SHAPE
+    M, N, K = shape or workloads.CFG3_DECODE_SHAPE
     a = workloads.activations(M, K, seed=5)
     b = workloads.gaussian(N, K, seed=6, std=0.02)
     pa, sa, gsa = nv.quantize(a, None)
@@ -335,7 +335,7 @@ def decode_bench(nv, steps, warmup, flush):
     hbm = float(peaks.get("hbm_gbs", HBM_FALLBACK_GBS))
     gbs = byts / (ms * 1e-3) / 1e9
     gbs_stream = byts / (ms_stream * 1e-3) / 1e9
-    return {"workload": "cfg3 decode GEMM M16 N7168 K8192 (split-K over 128-row tiles of B)",
+    return {"workload": f"{'cfg3 ' if shape is None else ''}decode GEMM M{M} N{N} K{K} (split-K over 128-row tiles of B)",
             "us": round(ms * 1e3, 2), "tflops": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1),
             "bytes_per_call": int(byts),
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
@@ -1372,7 +1372,8 @@ def run_only(args):
         out["dequantize_us"] = round(ms * 1e3, 2)
         out["dequantize_gbs"] = round(rows * cols * 2.5625 / (ms * 1e-3) / 1e9, 1)
     elif args.only == "gemm-decode":
-        out = decode_bench(nv, args.steps, args.warmup, flush)
+        shape = tuple(int(v) for v in args.shape.split("x")) if args.shape else None
+        out = decode_bench(nv, args.steps, args.warmup, flush, shape=shape)
     elif args.only == "mma-peak":
         # the FP4 MMA issue-rate probe alone (the GEMM's roofline), with its in-kernel SM clock
         from tensorcore_ptx_example_b200 import diag
@@ -1455,6 +1456,9 @@ def main():
                     default=None,
                     help="profiling mode: run one workload (warmup + steps launches) and print its "
                          "timings; not the benchmark line")
+    ap.add_argument("--shape", default=None,
+                    help="with --only gemm-decode: MxNxK instead of cfg3's decode shape (e.g. 16x1024x16384, "
+                         "which takes the workspace split-K path)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
