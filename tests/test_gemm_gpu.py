@@ -306,3 +306,16 @@ def test_gemm_decode_cfg3_full_size(nv, oracle):
     got = D.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
     assert np.count_nonzero(got != want) == 0
     assert torch.equal(D, D2)
+
+
+def test_mma_peak_probe_reports_rate_and_clock(nv):
+    """The FP4 issue-rate probe (the GEMM roofline's denominator in bench.py) runs without a device
+    error and reports a plausible rate and in-kernel SM clock (SM cycles / globaltimer ns)."""
+    from tensorcore_ptx_example_b200 import diag
+    diag.mma_peak_clock()                                   # reset the counters
+    tf = diag.mma_peak(cta_group=2, iters=1024, repeats=1)
+    mhz = diag.mma_peak_clock()
+    assert diag.device_status() == 0
+    assert 1000.0 < tf < 20000.0, tf
+    assert 500.0 < mhz < 2500.0, mhz
+    assert diag.mma_peak_clock() == 0.0                     # read-and-reset
