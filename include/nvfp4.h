@@ -208,7 +208,7 @@ typedef struct nvfp4_ar* nvfp4_ar_t;
 /* NVFP4_AR_AUTO picks the low-latency one-shot up to NVFP4_AR_LOWLAT_MAX_BYTES of bf16,
  * one-shot up to NVFP4_AR_ONESHOT_MAX_BYTES, two-shot above. */
 #define NVFP4_AR_LOWLAT_MAX_BYTES (1 << 20)
-#define NVFP4_AR_ONESHOT_MAX_BYTES (4 << 20)
+#define NVFP4_AR_ONESHOT_MAX_BYTES (2 << 20)
 
 /* Device bytes a context allocates (flags + two parities of comm buffers + two parities of the
  * low-latency area). */

@@ -350,6 +350,69 @@ __global__ void __launch_bounds__(AR_THREADS) ar_nvfp4_kernel(const Params p) {
     }
 }
 
+// Two-shot for small shards (at most one group of chunks per resident block): the grid-stride
+// kernel above gives a thread all n shards of its chunk in phases A and C, n dependent round
+// trips per thread, and at 4 MB of bf16 on 8 ranks it ran 16 blocks (41.5 us).  Here block b owns
+// the chunk group [b * per, (b + 1) * per) of every shard (per = AR_THREADS / n) and its threads
+// split the group's (shard, chunk) pairs: thread o_idx * per + j takes shard o_idx's chunk j in
+// phases A and C; in phase B threads j < per sum chunk j of this rank's shard.  The same chunks
+// go to block b on every rank in every phase, so the per-block barrier suffices.  Arithmetic and
+// order as in ar_nvfp4_kernel<true>: the same bits.
+__global__ void __launch_bounds__(AR_THREADS, 2) ar_nvfp4_twoshot_split_kernel(const Params p) {
+    const int n = p.world, me = p.rank;
+    const int per = AR_THREADS / n;
+    const int t = threadIdx.x, o_idx = t / per, j = t % per;
+    const int64_t shard = p.numel / n;
+    const int64_t schunks = shard / 32;
+    const int64_t c = (int64_t)blockIdx.x * per + j;
+    const bool pair_ok = o_idx < n && c < schunks;
+    const uint32_t v1 = p.epoch * 2u + 1u, v2 = p.epoch * 2u + 2u;
+    const bool fused = p.phase < 0;
+    if ((p.phase == -3 || p.phase == 3) && pair_ok) {
+        // the shards were quantized by the producer of the data (a GEMM epilogue): push them
+        const int o = (me + 1 + o_idx) % n;
+        const int64_t e32 = (int64_t)o * schunks + c;
+        const uint4 pk = ld_nc_v4(p.q_codes + e32 * 16);
+        const uint32_t sc = *reinterpret_cast<const uint16_t*>(p.q_scales + e32 * 2);
+        put_chunk(in_slot(p, o, me), shard, c, pk, sc);
+    }
+    if ((p.phase == -1 || p.phase == 0) && pair_ok) {
+        const int o = (me + 1 + o_idx) % n;                  // owner me+1 first, own shard last
+        uint4 pk;
+        uint32_t sc;
+        quant32(p.in + (int64_t)o * shard + c * 32, __fdiv_rn(1.0f, p.gs), pk, sc);
+        put_chunk(in_slot(p, o, me), shard, c, pk, sc);
+    }
+    if (fused && !block_barrier(p, v1)) return;
+    const float gs_red = __fmul_rn(p.gs, (float)n);
+    if ((fused || p.phase == 1) && t < per && c < schunks) {
+        float acc[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+        for (int s = 0; s < n; s++) {                          // fixed sum order 0 .. n-1
+            uint4 pk;
+            uint32_t sc;
+            get_chunk(in_slot(p, me, s), shard, c, pk, sc);
+            dq32_acc(pk, sc, p.gs, acc);
+        }
+        uint4 pk;
+        uint32_t sc;
+        quant32f(acc, __fdiv_rn(1.0f, gs_red), pk, sc);
+        for (int k = 1; k <= n; k++) put_chunk(gather_slot(p, (me + k) % n, me), shard, c, pk, sc);
+    }
+    if (fused && !block_barrier(p, v2)) return;
+    if ((fused || p.phase == 2) && pair_ok) {
+        uint4 pk;
+        uint32_t sc;
+        get_chunk(gather_slot(p, me, o_idx), shard, c, pk, sc);
+        float acc[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+        dq32_acc(pk, sc, gs_red, acc);
+        store_bf16x32(p.out + (int64_t)o_idx * shard + c * 32, acc);
+    }
+}
+
 // ---------------------------------------------------------------- low-latency one-shot ----
 constexpr int AR_LL_THREADS = 128;
 constexpr int AR_LL_WORDS = 3;                 // u64 words per 32-element chunk
@@ -658,6 +721,7 @@ struct nvfp4_ar {
     uint64_t timeout_ns = AR_DEFAULT_TIMEOUT_NS;
     int max_grid = 0, ll_max_grid = 0;   // resident grids: bf16 / NVLS kernels, low-latency kernel
     int nvfp4_max_grid = 0;              // resident grid of the NVFP4 one- and two-shot kernels
+    int split_max_grid = 0;              // resident grid of the small-shard two-shot kernel
     uint8_t* nvls_mc = nullptr;      // NVLS buffer (nvfp4_ar_set_multicast): multicast address,
     uint8_t* nvls_uc = nullptr;      // this rank's unicast address,
     int64_t nvls_half = 0;           // bytes of one parity half
@@ -788,6 +852,7 @@ nvfp4_status_t nvfp4_ar_create(int world, int rank, int64_t max_numel, nvfp4_ar_
     // grid is capped at the smallest resident grid of its kernels
     const int g1 = resident_grid((const void*)ar_nvfp4_kernel<true>), g2 = resident_grid((const void*)ar_nvfp4_kernel<false>);
     h->nvfp4_max_grid = g1 < g2 ? g1 : g2;
+    h->split_max_grid = resident_grid((const void*)ar_nvfp4_twoshot_split_kernel);
     int g3 = resident_grid((const void*)ar_bf16_kernel<true>), g4 = resident_grid((const void*)ar_bf16_kernel<false>);
     const int g5 = resident_grid((const void*)ar_bf16_nvls_kernel);
     int g = g3;
@@ -937,8 +1002,8 @@ int nvfp4_ar_choose_algo(int world, int64_t numel) {
     if (world <= 1) return NVFP4_AR_ONESHOT;
     // the low-latency one-shot needs no barrier but sends 1.33x the payload (faster than one-shot
     // up to its 1 MB cap on 2 and 8 x B200); one-shot pushes the whole payload to every peer but
-    // needs one barrier: better than two-shot while the call is latency-bound (measured
-    // crossover on 8 x B200 between 4 and 8 MB of bf16)
+    // needs one barrier: better than two-shot while the call is latency-bound (on 8 x B200 the
+    // small-shard two-shot is ahead from 4 MB of bf16: 25.8 vs 30.0 us)
     if (numel * 2 <= NVFP4_AR_LOWLAT_MAX_BYTES) return NVFP4_AR_LOWLAT;
     // with two ranks the two-shot sends as many bytes as the one-shot (half the payload, twice)
     // and adds a barrier and a pass over HBM: one-shot at every size (measured on 2 x B200 from
@@ -985,6 +1050,15 @@ static nvfp4_status_t launch_nvfp4_ll(nvfp4_ar_t h, const Params& p, cudaStream_
     return check_launch("ar_nvfp4_ll_kernel");
 }
 static nvfp4_status_t launch_nvfp4(nvfp4_ar_t h, const Params& p, bool twoshot, cudaStream_t s) {
+    if (twoshot) {
+        // small shards: one chunk group per block, the threads splitting (shard, chunk) pairs
+        const int per = AR_THREADS / p.world;
+        const int64_t groups = (p.numel / p.world / 32 + per - 1) / per;
+        if (groups <= h->split_max_grid) {
+            ar_nvfp4_twoshot_split_kernel<<<(int)(groups < 1 ? 1 : groups), AR_THREADS, 0, s>>>(p);
+            return check_launch("ar_nvfp4_twoshot_split_kernel");
+        }
+    }
     // one chunk per thread and pass, at most the resident blocks
     const int64_t work = twoshot ? p.numel / p.world / 32 : p.numel / 32;
     int64_t g = (work + AR_THREADS - 1) / AR_THREADS;

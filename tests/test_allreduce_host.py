@@ -76,8 +76,9 @@ def test_buffer_bytes_and_algo_choice(nv):
     assert L.nvfp4_ar_choose_algo(8, 1024) == 3                      # small: low-latency one-shot
     assert L.nvfp4_ar_choose_algo(8, (1 << 20) // 2) == 3
     assert L.nvfp4_ar_choose_algo(8, (1 << 20) // 2 + 256) == 1
-    assert L.nvfp4_ar_choose_algo(8, (4 << 20) // 2) == 1          # 4 MB of bf16: one-shot
-    assert L.nvfp4_ar_choose_algo(8, (4 << 20) // 2 + 256) == 2    # above: two-shot
+    assert L.nvfp4_ar_choose_algo(8, (2 << 20) // 2) == 1          # 2 MB of bf16: one-shot
+    assert L.nvfp4_ar_choose_algo(8, (2 << 20) // 2 + 256) == 2    # above: two-shot
+    assert L.nvfp4_ar_choose_algo(8, (4 << 20) // 2) == 2
     assert L.nvfp4_ar_choose_algo(2, 1024) == 3
     assert L.nvfp4_ar_choose_algo(2, 1 << 30) == 1                  # two ranks: one-shot at any size
 
