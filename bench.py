@@ -14,8 +14,9 @@ epilogue, the CPU baselines, an end-to-end number through the C ABI with host bu
 clocks sampled during the timed region.
 
 N > 1 (one process per GPU under torchrun): the cfg4 NVFP4 all-reduce (4096 x 7168 bf16 per
-rank, N(0,1), seed = rank; algorithm NVFP4_AR_AUTO).  One step = one all-reduce call; L2 flushed
-between steps; the time is the max over ranks.  `value` is the bf16-equivalent algorithm
+rank, N(0,1), seed = rank; algorithm NVFP4_AR_AUTO).  One step = one all-reduce call; the K steps
+run back to back between one pair of events, each reading the next of several copies of the input
+that together exceed L2; the time is the max over ranks.  `value` is the bf16-equivalent algorithm
 bandwidth 2 * numel / t (nccl-tests convention; busbw = algbw * 2 (n-1) / n).  The line also
 carries bit-exact parity against the CPU oracle on sampled windows of every algorithm's output,
 each algorithm's time and wire rate, compact cfg5 rows (best NVFP4 against best bf16), the
