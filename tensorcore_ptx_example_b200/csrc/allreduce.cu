@@ -23,6 +23,9 @@
 //             B: owner sums IN[0..n-1] of its shard in rank order, requantizes with gs * n and
 //             pushes the result into GATHER[me] of every rank; barrier;
 //             C: out = bf16(dequant(GATHER[o])) for every owner o.
+//             Two kernels run it: a grid-stride one (a thread takes one chunk and all n shards of
+//             it) and, for small shards, one whose threads split the (shard, chunk) pairs of their
+//             block's chunk group; both give the same bits.
 //   Sums are fp32 fma(code, scale * gs, acc) in rank order 0..n-1 (the reference sums in a
 //   rank-rotated order, :515-518); only the order of the pushes is rotated (rank me+1 first) so
 //   that the ranks do not all target the same peer at once.
